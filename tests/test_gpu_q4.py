@@ -1,0 +1,207 @@
+"""Parity of the CUDA path with the oracle, through the C ABI.
+
+Repacks are bit-exact (matrixRow read back from the device equals the
+oracle's matrixRow of the reference's QuantMatrix). Matmul outputs must be
+within the north star's rel 1e-3 of BOTH oracle modes (fp64 exact, and the
+reference shader's fp16-partial emulation), measured as
+||y - ref||_2 / ||ref||_2 and max|y - ref| / max|ref|.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+import webgllm_b200 as wg  # noqa: E402
+
+TOL = O.TOL
+
+
+def make(N, K, seed):
+    blocks = O.config_q4_0_blocks(N, K, seed)
+    m = wg.newQuantMatrix(N, K)
+    wg.packQ4_0(m, 0, blocks, N)
+    host = O.HostQuantMatrix(N, K)
+    O.c_pack_q4_0(host, 0, blocks, N)
+    return blocks, m, host
+
+
+def check_close(y, ref, what):
+    l2, mx = O.rel_errors(y, ref)
+    assert l2 <= TOL and mx <= TOL, f"{what}: l2 {l2:.3e} max {mx:.3e}"
+    return l2, mx
+
+
+def run(m, x_np, x_dtype=torch.float16, y_dtype=torch.float32):
+    x = torch.from_numpy(x_np).to("cuda", dtype=x_dtype)
+    y = wg.matmul(x, m, out_dtype=y_dtype)
+    torch.cuda.synchronize()
+    return y.float().cpu().numpy(), x.float().cpu().numpy()
+
+
+# ---------------------------------------------------------------- repack
+
+
+@pytest.mark.parametrize("N,K", [(4, 32), (12, 96), (16, 64), (64, 256), (260, 160), (2048, 2048)])
+def test_pack_q4_0_round_trip_is_bit_exact(N, K):
+    _, m, host = make(N, K, N * 7 + K)
+    for n in sorted({0, 1, N // 2, N - 1, min(N - 1, 17)}):
+        assert np.array_equal(wg.matrixRow(m, n), O.c_matrix_row(host, n)), n
+
+
+def test_pack_in_parts_with_permutation_matches_one_pack():
+    # Parts of 4 and 20 rows: the boundary falls inside a 16-row tile.
+    N, K = 24, 128
+    blocks = O.config_q4_0_blocks(N, K, 5)
+    perm = np.array([3, 0, 2, 1], dtype=np.int32)
+    m = wg.newQuantMatrix(N, K)
+    wg.packQ4_0(m, 4, blocks[: 4 * (K // 32) * 18], 4, perm)
+    wg.packQ4_0(m, 8, blocks[8 * (K // 32) * 18:], N - 8)
+    host = O.HostQuantMatrix(N, K)
+    O.c_pack_q4_0(host, 4, blocks[: 4 * (K // 32) * 18], 4, perm)
+    O.c_pack_q4_0(host, 8, blocks[8 * (K // 32) * 18:], N - 8)
+    for n in range(N):
+        assert np.array_equal(wg.matrixRow(m, n), O.c_matrix_row(host, n)), n
+    # rows 0..3 were never written: weight 0
+    assert not wg.matrixRow(m, 2).any()
+
+
+def test_pack_errors_follow_the_reference():
+    m = wg.newQuantMatrix(8, 64)
+    with pytest.raises(wg.RangeError):
+        wg.packQ4_0(m, 6, np.zeros(4 * 2 * 18, np.uint8), 4)
+    with pytest.raises(wg.ShapeError, match="too short"):
+        wg.packQ4_0(m, 0, np.zeros(4 * 2 * 18 - 1, np.uint8), 4)
+
+
+def _nbits(N, K, seed):
+    rng = np.random.default_rng(seed)
+    blocks = K // 32
+    quant = rng.integers(0, 256, N * blocks * 16, dtype=np.uint8)
+    scales = (np.abs(rng.standard_normal(N * blocks)) * 0.02 / 8).astype(np.float16).view(np.uint8)
+    zp = rng.integers(0, 256, N * ((blocks + 1) // 2), dtype=np.uint8)
+    return quant, scales, zp
+
+
+@pytest.mark.parametrize("N,K", [(8, 64), (20, 96), (64, 2048)])
+def test_pack_matmulnbits_with_zero_points_round_trip(N, K):
+    quant, scales, zp = _nbits(N, K, N + K)
+    m = wg.newQuantMatrix(N, K, withZeros=True)
+    wg.packMatMulNBits(m, 0, quant, scales, zp, N)
+    host = O.HostQuantMatrix(N, K, with_zeros=True)
+    O.c_pack_matmulnbits(host, 0, quant, scales, zp, N)
+    for n in range(0, N, max(1, N // 9)):
+        assert np.array_equal(wg.matrixRow(m, n), O.c_matrix_row(host, n)), n
+
+
+def test_write_quantmatrix_round_trip():
+    N, K = 36, 192
+    quant, scales, zp = _nbits(N, K, 9)
+    host = O.HostQuantMatrix(N, K, with_zeros=True)
+    O.c_pack_matmulnbits(host, 0, quant, scales, zp, N)
+    m = wg.newQuantMatrix(N, K, withZeros=True)
+    wg.writeMatrix(m, host.quants, host.scales, host.zeros)
+    for n in range(N):
+        assert np.array_equal(wg.matrixRow(m, n), O.c_matrix_row(host, n)), n
+
+
+# ---------------------------------------------------------------- decode GEMV
+
+
+def test_config0_gemv_fp32():
+    # x fp32 [1 x 2048] ~ N(0,1), W 2048 x 2048 Q4_0, seed 0.
+    N = K = 2048
+    blocks, m, host = make(N, K, 0)
+    x = O.config_activations(1, K, 0)
+    y, _ = run(m, x, torch.float32, torch.float32)
+    check_close(y, O.c_ref_f64(blocks, x, N, K), "vs fp64")
+    check_close(y, O.c_split_emulate(host, x), "vs shader emulation")
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 7, 8, 9, 12, 16, 17, 24, 31, 32])
+def test_gemv_rows(M):
+    N, K = 512, 1024
+    blocks, m, host = make(N, K, M)
+    y, x16 = run(m, O.config_activations(M, K, M))
+    check_close(y, O.c_ref_f64(blocks, x16, N, K), f"M={M} vs fp64")
+    check_close(y, O.c_split_emulate(host, x16), f"M={M} vs emulation")
+
+
+@pytest.mark.parametrize("N,K", [(4, 32), (12, 96), (20, 160), (36, 64), (100, 4096),
+                                 (2560, 2048), (2048, 5632), (256, 14336), (4, 32768),
+                                 # K split over clusters whose last CTA has a shorter range
+                                 (1024, 2048), (512, 1600), (64, 3520), (1536, 4608)])
+def test_gemv_shapes(N, K):
+    blocks, m, host = make(N, K, N + K)
+    for M in (1, 5):
+        y, x16 = run(m, O.config_activations(M, K, 3))
+        check_close(y, O.c_ref_f64(blocks, x16, N, K), f"{N}x{K} M={M}")
+
+
+@pytest.mark.parametrize("xd", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("yd", ["float32", "float16", "bfloat16"])
+def test_gemv_dtypes(xd, yd):
+    N, K = 256, 512
+    blocks, m, host = make(N, K, 11)
+    xt, yt = getattr(torch, xd), getattr(torch, yd)
+    y, xq = run(m, O.config_activations(3, K, 11), xt, yt)
+    ref = O.c_ref_f64(blocks, xq, N, K)
+    if yd == "bfloat16":  # bf16 storage itself rounds at 2^-9
+        l2, mx = O.rel_errors(y, ref)
+        assert l2 <= 4e-3 and mx <= 4e-3
+    else:
+        check_close(y, ref, f"{xd}->{yd}")
+
+
+def test_gemv_zero_points():
+    N, K = 1024, 2048
+    quant, scales, zp = _nbits(N, K, 4)
+    m = wg.newQuantMatrix(N, K, withZeros=True)
+    wg.packMatMulNBits(m, 0, quant, scales, zp, N)
+    host = O.HostQuantMatrix(N, K, with_zeros=True)
+    O.c_pack_matmulnbits(host, 0, quant, scales, zp, N)
+    W = np.stack([O.c_matrix_row(host, n) for n in range(N)]).astype(np.float64)
+    for M in (1, 6, 20):
+        y, x16 = run(m, O.config_activations(M, K, M))
+        check_close(y, x16.astype(np.float64) @ W.T, f"zeros M={M} vs fp64")
+        check_close(y, O.c_split_emulate(host, x16), f"zeros M={M} vs emulation")
+
+
+def test_fp16_output_saturates_like_packh2():
+    # Scales of 64 and codes 15: |y| far above 65504 -> +-65504 (kernels.ts:32-36).
+    N, K = 16, 256
+    blk = np.zeros((N * K // 32, 18), np.uint8)
+    blk[:, 0:2] = np.array([64.0], np.float16).view(np.uint8)
+    blk[:, 2:] = 0xFF
+    m = wg.newQuantMatrix(N, K)
+    wg.packQ4_0(m, 0, blk.reshape(-1), N)
+    x = np.full((1, K), 100.0, np.float32)
+    y, _ = run(m, x, torch.float32, torch.float16)
+    assert np.all(np.abs(y) == 65504.0)
+
+
+def test_empty_batch_is_a_no_op():
+    _, m, _ = make(16, 64, 1)
+    x = torch.zeros((0, 64), device="cuda", dtype=torch.float16)
+    y = wg.matmul(x, m)
+    assert y.shape == (0, 16)
+
+
+# ---------------------------------------------------------------- config 1 sweep
+
+
+@pytest.mark.parametrize("s,M", list(enumerate([1, 4, 16, 64, 256, 1024])))
+def test_config1_sweep(s, M):
+    # K = N = 4096, x fp16 ~ N(0,1), seed s for shape s.
+    N = K = 4096
+    blocks, m, host = make(N, K, s)
+    y, x16 = run(m, O.config_activations(M, K, s))
+    ref = O.c_ref_f64(blocks, x16, N, K)
+    check_close(y, ref, f"config 1 M={M} vs fp64")
+    emul = O.c_split_emulate(host, x16) if M <= 8 else O.c_prefill_emulate(host, x16)
+    check_close(y, emul, f"config 1 M={M} vs emulation")

@@ -1,0 +1,531 @@
+// The C ABI of include/webgllm_q4.h.
+//
+// Host-side plumbing only: contexts, memory, transfers, argument checks (with
+// the reference's error rules), and the dispatch of the Q4 matmul by row
+// count, as Engine.project does (src/engine.ts:4677-4688: rows <= 8 take the
+// split GEMV, more rows the prompt matmul).
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "q4_kernels.cuh"
+#include "q4_layout.cuh"
+
+struct wg_ctx {
+  int device = 0;
+  int num_sms = wg::kB200Sms;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  unsigned *d_flags = nullptr;  // device error flags (kFlag*)
+  uint8_t *staging = nullptr;   // device copy of a repack's source bytes
+  size_t staging_bytes = 0;
+  bool pdl = true;              // programmatic dependent launch for the GEMV
+  int trigger_at = 1;           // GemvArgs::trigger_at (WG_GEMV_TRIGGER overrides)
+  unsigned long long *trace = nullptr;       // wg_trace buffer (device) or null
+  unsigned long long trace_cap = 0;          // records that fit
+  unsigned long long *d_trace_next = nullptr;  // device record counter
+  unsigned launch_index = 0;
+  std::string last_error;
+};
+
+struct wg_q4mat {
+  wg::Q4Dims d;
+  int device;
+  uint8_t *base;  // one allocation: nib | scl | zro
+  uint32_t *nib;
+  uint16_t *scl;
+  uint8_t *zro;
+  size_t bytes;
+};
+
+namespace {
+
+int fail(wg_ctx *ctx, int status, const char *fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->last_error = buf;
+  }
+  return status;
+}
+
+int cuda_fail(wg_ctx *ctx, cudaError_t e, const char *what) {
+  return fail(ctx, wg::status_of(e), "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define WG_CUDA(ctx, call)                                 \
+  do {                                                     \
+    cudaError_t e_ = (call);                               \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+  } while (0)
+
+int use_device(wg_ctx *ctx) {
+  WG_CUDA(ctx, cudaSetDevice(ctx->device));
+  return WG_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Grows the context's device staging buffer to `bytes` (stream-ordered: the
+// old buffer is released only after the stream has drained).
+int ensure_staging(wg_ctx *ctx, size_t bytes) {
+  if (bytes <= ctx->staging_bytes) return WG_OK;
+  WG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if (ctx->staging) WG_CUDA(ctx, cudaFree(ctx->staging));
+  ctx->staging = nullptr;
+  ctx->staging_bytes = 0;
+  size_t want = align_up(bytes, 1 << 20);
+  WG_CUDA(ctx, cudaMalloc(&ctx->staging, want));
+  ctx->staging_bytes = want;
+  return WG_OK;
+}
+
+bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+int check_shape(wg_ctx *ctx, int N, int K) {
+  if (N <= 0 || K <= 0)
+    return fail(ctx, WG_INVALID_SHAPE, "matrix shape %d x %d must be positive", N, K);
+  // src/repack.ts:21-24
+  if (N % 4 != 0) return fail(ctx, WG_INVALID_SHAPE, "matrix rows (%d) must be a multiple of 4", N);
+  if (K % 32 != 0)
+    return fail(ctx, WG_INVALID_SHAPE, "matrix columns (%d) must be a multiple of 32", K);
+  return WG_OK;
+}
+
+int check_rows(wg_ctx *ctx, const wg_q4mat *m, int row0, int rows) {
+  // src/repack.ts:52-53
+  if (row0 < 0 || rows < 0 || row0 + rows > m->d.N)
+    return fail(ctx, WG_OUT_OF_RANGE, "rows %d..%d are outside the matrix", row0, row0 + rows);
+  return WG_OK;
+}
+
+// Copies `parts` host buffers into the staging buffer (each 256-byte
+// aligned) and returns their device addresses.
+struct Part {
+  const void *host;
+  size_t bytes;
+  const uint8_t *dev;
+};
+
+int stage(wg_ctx *ctx, std::vector<Part> &parts) {
+  size_t total = 0;
+  for (auto &p : parts) total += align_up(p.bytes, 256);
+  int st = ensure_staging(ctx, total);
+  if (st) return st;
+  size_t off = 0;
+  for (auto &p : parts) {
+    p.dev = nullptr;
+    if (p.host && p.bytes) {
+      WG_CUDA(ctx, cudaMemcpyAsync(ctx->staging + off, p.host, p.bytes, cudaMemcpyHostToDevice,
+                                   ctx->stream));
+      p.dev = ctx->staging + off;
+    }
+    off += align_up(p.bytes, 256);
+  }
+  return WG_OK;
+}
+
+int run_repack(wg_ctx *ctx, wg_q4mat *m, int kind, int row0, int rows, const uint8_t *src,
+               size_t src_bytes, const uint8_t *scale_src, size_t scale_bytes,
+               const uint8_t *zero_src, size_t zero_bytes, const int32_t *src_rows) {
+  std::vector<Part> parts = {{src, src_bytes, nullptr},
+                             {scale_src, scale_bytes, nullptr},
+                             {zero_src, zero_bytes, nullptr},
+                             {src_rows, src_rows ? (size_t)rows * 4 : 0, nullptr}};
+  int st = stage(ctx, parts);
+  if (st) return st;
+  wg::RepackArgs a{};
+  a.d = m->d;
+  a.nib = m->nib;
+  a.scl = m->scl;
+  a.zro = m->zro;
+  a.src = parts[0].dev;
+  a.scale_src = parts[1].dev;
+  a.zero_src = parts[2].dev;
+  a.src_rows = reinterpret_cast<const int32_t *>(parts[3].dev);
+  a.row0 = row0;
+  a.rows = rows;
+  a.kind = kind;
+  WG_CUDA(ctx, wg::launch_repack(a, ctx->stream));
+  return WG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wg_init(int device, wg_ctx **out) {
+  if (!out) return WG_INVALID_ARGUMENT;
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) return WG_NO_DEVICE;
+  if (device < 0 || device >= count) return WG_NO_DEVICE;
+  wg_ctx *ctx = new (std::nothrow) wg_ctx;
+  if (!ctx) return WG_OUT_OF_MEMORY;
+  ctx->device = device;
+  int st = WG_OK;
+  if ((e = cudaSetDevice(device)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device)) !=
+          cudaSuccess ||
+      (e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking)) != cudaSuccess ||
+      (e = cudaMalloc(&ctx->d_flags, sizeof(unsigned))) != cudaSuccess ||
+      (e = cudaMemset(ctx->d_flags, 0, sizeof(unsigned))) != cudaSuccess) {
+    st = wg::status_of(e);
+    if (ctx->d_flags) cudaFree(ctx->d_flags);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return st;
+  }
+  ctx->stream = ctx->own_stream;
+  const char *pdl = getenv("WG_PDL");
+  if (pdl && pdl[0] == '0') ctx->pdl = false;
+  const char *trig = getenv("WG_GEMV_TRIGGER");
+  if (trig && trig[0] >= '0' && trig[0] <= '2') ctx->trigger_at = trig[0] - '0';
+  *out = ctx;
+  return WG_OK;
+}
+
+int wg_destroy(wg_ctx *ctx) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->staging) cudaFree(ctx->staging);
+  if (ctx->d_flags) cudaFree(ctx->d_flags);
+  if (ctx->d_trace_next) cudaFree(ctx->d_trace_next);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+  return WG_OK;
+}
+
+int wg_set_stream(wg_ctx *ctx, void *stream) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  ctx->stream = stream ? reinterpret_cast<cudaStream_t>(stream) : ctx->own_stream;
+  return WG_OK;
+}
+
+int wg_alloc(wg_ctx *ctx, size_t bytes, void **dptr) {
+  if (!ctx || !dptr) return fail(ctx, WG_INVALID_ARGUMENT, "wg_alloc: null argument");
+  *dptr = nullptr;
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaMalloc(dptr, bytes ? bytes : 1));
+  return WG_OK;
+}
+
+int wg_free(wg_ctx *ctx, void *dptr) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  if (!dptr) return WG_OK;
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  WG_CUDA(ctx, cudaFree(dptr));
+  return WG_OK;
+}
+
+int wg_host_alloc(wg_ctx *ctx, size_t bytes, void **hptr) {
+  if (!ctx || !hptr) return fail(ctx, WG_INVALID_ARGUMENT, "wg_host_alloc: null argument");
+  *hptr = nullptr;
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaMallocHost(hptr, bytes ? bytes : 1));
+  return WG_OK;
+}
+
+int wg_host_free(wg_ctx *ctx, void *hptr) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  if (!hptr) return WG_OK;
+  WG_CUDA(ctx, cudaFreeHost(hptr));
+  return WG_OK;
+}
+
+int wg_upload(wg_ctx *ctx, void *dst, const void *src, size_t bytes) {
+  if (!ctx || (!dst && bytes) || (!src && bytes))
+    return fail(ctx, WG_INVALID_ARGUMENT, "wg_upload: null argument");
+  if (!bytes) return WG_OK;
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  return WG_OK;
+}
+
+int wg_read(wg_ctx *ctx, void *host, const void *src, size_t bytes) {
+  if (!ctx || (!host && bytes) || (!src && bytes))
+    return fail(ctx, WG_INVALID_ARGUMENT, "wg_read: null argument");
+  int st = use_device(ctx);
+  if (st) return st;
+  if (bytes) WG_CUDA(ctx, cudaMemcpyAsync(host, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  return wg_sync(ctx);
+}
+
+int wg_sync(wg_ctx *ctx) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  unsigned flags = 0;
+  WG_CUDA(ctx, cudaMemcpy(&flags, ctx->d_flags, sizeof flags, cudaMemcpyDeviceToHost));
+  if (flags) {
+    WG_CUDA(ctx, cudaMemset(ctx->d_flags, 0, sizeof(unsigned)));
+    if (flags & wg::kFlagTimeout)
+      return fail(ctx, WG_TIMEOUT, "a device-side wait ran out (flags 0x%x)", flags);
+    return fail(ctx, WG_INVALID_ARGUMENT, "a kernel rejected its arguments (flags 0x%x)", flags);
+  }
+  return WG_OK;
+}
+
+int wg_q4_new(wg_ctx *ctx, int N, int K, int with_zeros, wg_q4mat **out) {
+  if (!ctx || !out) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_new: null argument");
+  *out = nullptr;
+  int st = check_shape(ctx, N, K);
+  if (st) return st;
+  st = use_device(ctx);
+  if (st) return st;
+  wg_q4mat *m = new (std::nothrow) wg_q4mat{};
+  if (!m) return fail(ctx, WG_OUT_OF_MEMORY, "host allocation failed");
+  m->d = wg::q4_dims(N, K);
+  m->device = ctx->device;
+  const size_t tiles = (size_t)m->d.NT * m->d.KT;
+  const size_t nib = align_up(tiles * wg::kTileNibBytes, 256);
+  const size_t scl = align_up(tiles * wg::kTileSclBytes, 256);
+  const size_t zro = with_zeros ? align_up(tiles * wg::kTileZroBytes, 256) : 0;
+  m->bytes = nib + scl + zro;
+  cudaError_t e = cudaMalloc(&m->base, m->bytes);
+  if (e != cudaSuccess) {
+    delete m;
+    return cuda_fail(ctx, e, "wg_q4_new: cudaMalloc");
+  }
+  m->nib = reinterpret_cast<uint32_t *>(m->base);
+  m->scl = reinterpret_cast<uint16_t *>(m->base + nib);
+  m->zro = with_zeros ? m->base + nib + scl : nullptr;
+  // Every weight 0: code 8 (0x88 bytes), scale 0, zero point 8.
+  if ((e = cudaMemsetAsync(m->nib, 0x88, nib, ctx->stream)) != cudaSuccess ||
+      (e = cudaMemsetAsync(m->scl, 0, scl, ctx->stream)) != cudaSuccess ||
+      (with_zeros && (e = cudaMemsetAsync(m->zro, 8, zro, ctx->stream)) != cudaSuccess)) {
+    cudaFree(m->base);
+    delete m;
+    return cuda_fail(ctx, e, "wg_q4_new: memset");
+  }
+  *out = m;
+  return WG_OK;
+}
+
+int wg_q4_free(wg_ctx *ctx, wg_q4mat *m) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  if (!m) return WG_OK;
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  WG_CUDA(ctx, cudaFree(m->base));
+  delete m;
+  return WG_OK;
+}
+
+int wg_q4_info(const wg_q4mat *m, int *N, int *K, size_t *device_bytes) {
+  if (!m) return WG_INVALID_ARGUMENT;
+  if (N) *N = m->d.N;
+  if (K) *K = m->d.K;
+  if (device_bytes) *device_bytes = m->bytes;
+  return WG_OK;
+}
+
+int wg_q4_pack_q4_0(wg_ctx *ctx, wg_q4mat *m, int row0, const uint8_t *src, size_t src_len,
+                    int rows, const int32_t *src_rows) {
+  if (!ctx || !m) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_pack_q4_0: null argument");
+  int st = check_rows(ctx, m, row0, rows);
+  if (st) return st;
+  const size_t need = (size_t)rows * (m->d.K / 32) * 18;
+  // src/repack.ts:69
+  if (src_len < need || (!src && need)) return fail(ctx, WG_DATA_TOO_SHORT, "Q4_0 data is too short");
+  if (src_rows)
+    for (int i = 0; i < rows; i++)
+      if (src_rows[i] < 0 || (size_t)(src_rows[i] + 1) * (m->d.K / 32) * 18 > src_len)
+        return fail(ctx, WG_DATA_TOO_SHORT, "Q4_0 data is too short for source row %d", src_rows[i]);
+  if (!rows) return WG_OK;
+  st = use_device(ctx);
+  if (st) return st;
+  size_t src_bytes = need;
+  if (src_rows) {
+    int hi = 0;
+    for (int i = 0; i < rows; i++) hi = src_rows[i] > hi ? src_rows[i] : hi;
+    src_bytes = (size_t)(hi + 1) * (m->d.K / 32) * 18;
+  }
+  return run_repack(ctx, m, wg::kSrcGguf, row0, rows, src, src_bytes, nullptr, 0, nullptr, 0,
+                    src_rows);
+}
+
+int wg_q4_pack_nbits(wg_ctx *ctx, wg_q4mat *m, int row0, const uint8_t *quant, size_t quant_len,
+                     const uint8_t *scale_bytes, size_t scale_len, const uint8_t *zp, size_t zp_len,
+                     int rows, const int32_t *src_rows) {
+  if (!ctx || !m) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_pack_nbits: null argument");
+  int st = check_rows(ctx, m, row0, rows);
+  if (st) return st;
+  const size_t blocks = m->d.K / 32, zstride = (blocks + 1) / 2;
+  size_t src_n = rows;
+  if (src_rows) {
+    int hi = -1;
+    for (int i = 0; i < rows; i++) {
+      if (src_rows[i] < 0) return fail(ctx, WG_INVALID_ARGUMENT, "negative source row");
+      hi = src_rows[i] > hi ? src_rows[i] : hi;
+    }
+    src_n = (size_t)(hi + 1);
+  }
+  // src/repack.ts:353-363
+  if (quant_len < src_n * blocks * 16 || scale_len < src_n * blocks * 2 ||
+      (!quant && rows) || (!scale_bytes && rows))
+    return fail(ctx, WG_DATA_TOO_SHORT, "MatMulNBits data is too short");
+  if (zp && !m->zro)
+    return fail(ctx, WG_INVALID_ARGUMENT, "zero points given for a matrix without them");
+  if (zp && zp_len < src_n * zstride)
+    return fail(ctx, WG_DATA_TOO_SHORT, "MatMulNBits zero points are too short");
+  if (!rows) return WG_OK;
+  st = use_device(ctx);
+  if (st) return st;
+  return run_repack(ctx, m, wg::kSrcNbits, row0, rows, quant, src_n * blocks * 16, scale_bytes,
+                    src_n * blocks * 2, zp, zp ? src_n * zstride : 0, src_rows);
+}
+
+int wg_q4_write_quantmatrix(wg_ctx *ctx, wg_q4mat *m, const uint32_t *quants,
+                            const uint16_t *scales, const uint8_t *zeros) {
+  if (!ctx || !m || !quants || !scales)
+    return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_write_quantmatrix: null argument");
+  if (zeros && !m->zro)
+    return fail(ctx, WG_INVALID_ARGUMENT, "zero points given for a matrix without them");
+  int st = use_device(ctx);
+  if (st) return st;
+  const size_t blocks = (size_t)m->d.N * (m->d.K / 32);
+  return run_repack(ctx, m, wg::kSrcQmat, 0, m->d.N, reinterpret_cast<const uint8_t *>(quants),
+                    blocks * 16, reinterpret_cast<const uint8_t *>(scales), blocks * 2, zeros,
+                    zeros ? blocks : 0, nullptr);
+}
+
+int wg_q4_matrix_row(wg_ctx *ctx, const wg_q4mat *m, int n, float *out) {
+  if (!ctx || !m || !out) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matrix_row: null argument");
+  if (n < 0 || n >= m->d.N) return fail(ctx, WG_OUT_OF_RANGE, "row %d is outside the matrix", n);
+  int st = use_device(ctx);
+  if (st) return st;
+  const int nt = n / wg::kTileRows, KT = m->d.KT;
+  std::vector<uint8_t> nib((size_t)KT * wg::kTileNibBytes);
+  std::vector<uint16_t> scl((size_t)KT * 32);
+  std::vector<uint8_t> zro(m->zro ? (size_t)KT * 32 : 0);
+  const size_t t0 = (size_t)nt * KT;
+  WG_CUDA(ctx, cudaMemcpyAsync(nib.data(), reinterpret_cast<uint8_t *>(m->nib) + t0 * wg::kTileNibBytes,
+                               nib.size(), cudaMemcpyDeviceToHost, ctx->stream));
+  WG_CUDA(ctx, cudaMemcpyAsync(scl.data(), m->scl + t0 * 32, scl.size() * 2, cudaMemcpyDeviceToHost,
+                               ctx->stream));
+  if (m->zro)
+    WG_CUDA(ctx, cudaMemcpyAsync(zro.data(), m->zro + t0 * 32, zro.size(), cudaMemcpyDeviceToHost,
+                                 ctx->stream));
+  st = wg_sync(ctx);
+  if (st) return st;
+  for (int k = 0; k < m->d.K; k++) {
+    wg::Q4Place pl = wg::q4_place(m->d, n, k);
+    const size_t nb = pl.nib_byte - t0 * wg::kTileNibBytes;
+    const size_t si = pl.sz_index - t0 * 32;
+    const int code = pl.nib_high ? (nib[nb] >> 4) : (nib[nb] & 15);
+    const float d = __half2float(*reinterpret_cast<const __half *>(&scl[si]));
+    const float z = m->zro ? (float)zro[si] : 8.0f;
+    out[k] = d * ((float)code - z);
+  }
+  return WG_OK;
+}
+
+int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y,
+                 int y_dtype) {
+  if (!ctx || !m) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul: null argument");
+  if (M < 0) return fail(ctx, WG_INVALID_ARGUMENT, "negative row count %d", M);
+  if (M == 0) return WG_OK;
+  if (!x || !y) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul: null x or y");
+  if (x_dtype < WG_F32 || x_dtype > WG_BF16 || y_dtype < WG_F32 || y_dtype > WG_BF16)
+    return fail(ctx, WG_INVALID_ARGUMENT, "unknown dtype (x %d, y %d)", x_dtype, y_dtype);
+  if (!aligned16(x) || !aligned16(y))
+    return fail(ctx, WG_INVALID_ARGUMENT, "x and y must be 16-byte aligned");
+  if (m->device != ctx->device)
+    return fail(ctx, WG_INVALID_ARGUMENT, "matrix lives on device %d, context on %d", m->device,
+                ctx->device);
+  int st = use_device(ctx);
+  if (st) return st;
+  const size_t xsz = x_dtype == WG_F32 ? 4 : 2, ysz = y_dtype == WG_F32 ? 4 : 2;
+  // Rows beyond what one GEMV launch holds go in chunks (until the
+  // tensor-core GEMM takes them).
+  for (int m0 = 0; m0 < M; m0 += wg::kGemvMaxTokens) {
+    const int mc = M - m0 < wg::kGemvMaxTokens ? M - m0 : wg::kGemvMaxTokens;
+    wg::GemvArgs a{};
+    a.nib = m->nib;
+    a.scl = m->scl;
+    a.zro = m->zro;
+    a.x = reinterpret_cast<const uint8_t *>(x) + (size_t)m0 * m->d.K * xsz;
+    a.y = reinterpret_cast<uint8_t *>(y) + (size_t)m0 * m->d.N * ysz;
+    a.M = mc;
+    a.N = m->d.N;
+    a.K = m->d.K;
+    a.NT = m->d.NT;
+    a.KT = m->d.KT;
+    a.x_dtype = x_dtype;
+    a.y_dtype = y_dtype;
+    a.flags = ctx->d_flags;
+    a.trace = ctx->trace;
+    a.trace_next = ctx->d_trace_next;
+    a.trace_cap = ctx->trace_cap;
+    a.launch_index = ctx->launch_index++;
+    a.trigger_at = ctx->trigger_at;
+    if (!wg::plan_gemv(a, ctx->num_sms))
+      return fail(ctx, WG_UNSUPPORTED, "K = %d is beyond the GEMV's largest cluster split", m->d.K);
+    WG_CUDA(ctx, wg::launch_gemv(a, ctx->stream, ctx->pdl));
+  }
+  return WG_OK;
+}
+
+int wg_trace(wg_ctx *ctx, void *buf, size_t bytes) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  int st = use_device(ctx);
+  if (st) return st;
+  if (!ctx->d_trace_next) WG_CUDA(ctx, cudaMalloc(&ctx->d_trace_next, sizeof(unsigned long long)));
+  WG_CUDA(ctx, cudaMemsetAsync(ctx->d_trace_next, 0, sizeof(unsigned long long), ctx->stream));
+  ctx->trace = reinterpret_cast<unsigned long long *>(buf);
+  ctx->trace_cap = buf ? bytes / (WG_TRACE_WORDS * sizeof(unsigned long long)) : 0;
+  ctx->launch_index = 0;
+  return WG_OK;
+}
+
+int wg_trace_count(wg_ctx *ctx, size_t *records) {
+  if (!ctx || !records) return fail(ctx, WG_INVALID_ARGUMENT, "wg_trace_count: null argument");
+  *records = 0;
+  if (!ctx->d_trace_next) return WG_OK;
+  int st = wg_sync(ctx);
+  if (st) return st;
+  unsigned long long n = 0;
+  WG_CUDA(ctx, cudaMemcpy(&n, ctx->d_trace_next, sizeof n, cudaMemcpyDeviceToHost));
+  *records = (size_t)(n < ctx->trace_cap ? n : ctx->trace_cap);
+  return WG_OK;
+}
+
+const char *wg_error_string(int status) {
+  switch (status) {
+    case WG_OK: return "ok";
+    case WG_INVALID_ARGUMENT: return "invalid argument";
+    case WG_INVALID_SHAPE: return "invalid shape";
+    case WG_OUT_OF_RANGE: return "out of range";
+    case WG_DATA_TOO_SHORT: return "data too short";
+    case WG_OUT_OF_MEMORY: return "out of memory";
+    case WG_CUDA_ERROR: return "CUDA error";
+    case WG_TIMEOUT: return "device wait timed out";
+    case WG_DEVICE_LOST: return "the GPU context was lost";
+    case WG_UNSUPPORTED: return "unsupported";
+    case WG_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+const char *wg_last_error(const wg_ctx *ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+}  // extern "C"

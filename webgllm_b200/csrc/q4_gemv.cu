@@ -1,0 +1,374 @@
+// The Q4 decode GEMV (M <= 32 rows of activations): y = x . W^T.
+//
+// Replaces the reference's split matmul (src/engine.ts:5241-5391 dispatching
+// matmulSplitRgba4, src/gpu/kernels.ts:744-895, or matmul({split: true}),
+// kernels.ts:163-296) and its consumers' slice reduction (pf,
+// kernels.ts:69-79): the K-slices are summed on chip, not written as fp16
+// partials.
+//
+// Design (HBM-bound: 0.5625 bytes of weights per multiply-add at M = 1):
+// - A CTA of 8 warps owns one 16-row tile column (16 outputs) and a range of
+//   K tiles (all of K unless K is large, then a thread-block cluster splits
+//   it). Its first thread starts bulk asynchronous copies (the TMA engine) of
+//   the whole range's codes and scales into shared memory, in chunks of 8
+//   tiles with one mbarrier each, before anything waits: weight streaming
+//   needs no registers and does not depend on the kernel that produced x.
+// - The CTA then triggers its dependents (programmatic dependent launch) and
+//   only afterwards waits for x's producer, so in a chain of matmuls the next
+//   one's weight copies are in flight while this one finishes. The kernel
+//   keeps to a fraction of an SM (<= 64 registers a thread, modest shared
+//   memory) so that the next kernel's CTAs can be resident at the same time.
+// - Codes become exact fp16 (q - z) in registers (q4_layout.cuh), x is staged
+//   once as fp16 in shared memory, and mma.m16n8k16 (fp32 accumulate)
+//   multiplies each 32-weight block into a fresh accumulator that is scaled
+//   by the block's scale in fp32: the reference's per-block arithmetic
+//   d * (sum q*a - z * sum a) (kernels.ts:182-217) without its fp16
+//   partials.
+// - The 8 warps' partial tiles are summed in shared memory; across a cluster
+//   through distributed shared memory (no atomics, no global scratch).
+#include <cooperative_groups.h>
+
+#include <cstdlib>
+
+#include "common.cuh"
+#include "device_utils.cuh"
+#include "q4_kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace wg {
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxTilesPerWarp = 8;
+constexpr int kMaxTilesPerCta = kWarps * kMaxTilesPerWarp;
+constexpr int kSmemBudget = 100 * 1024;  // per CTA, so that two kernels' CTAs fit an SM
+constexpr int kMaxSmem = 200 * 1024;
+
+struct GemvSmem {
+  int nib, scl, zro, x, red, bar, total;
+  int tpw;       // tiles per warp
+  int x_stride;  // halves per staged token row (per warp)
+  int x_warp;    // halves per warp's x slice
+};
+
+__host__ __device__ inline int align_to(int v, int a) { return (v + a - 1) / a * a; }
+
+// Shared memory of one CTA with a K range of `ktc` tiles (the planned range:
+// every CTA of a grid uses the same layout, so that the cluster reduction
+// can address a peer's `part` at its own offset).
+__host__ __device__ inline GemvSmem gemv_smem(int M, int ktc, int NG, bool zeros) {
+  GemvSmem s;
+  s.tpw = (ktc + kWarps - 1) / kWarps;
+  s.nib = 0;
+  s.scl = s.nib + ktc * kTileNibBytes;
+  s.zro = s.scl + ktc * kTileSclBytes;
+  s.x = align_to(s.zro + (zeros ? ktc * kTileZroBytes : 0), 128);
+  // +16 halves (32 bytes) per row: the 8-byte fragment loads of 8 rows by 4
+  // threads hit 32 distinct banks.
+  s.x_stride = s.tpw * kTileK + 16;
+  s.x_warp = M * s.x_stride;
+  s.red = align_to(s.x + kWarps * s.x_warp * 2, 128);
+  s.bar = align_to(s.red + (kWarps * NG * 128 + 128 * NG) * 4, 8);
+  s.total = s.bar + kWarps * 8;
+  return s;
+}
+
+__device__ __forceinline__ void mma_16816(float d[4], const uint32_t a0, const uint32_t a1,
+                                          const uint32_t a2, const uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 16 x 64 tile: four K steps of mma.m16n8k16 per token group, two
+// 32-weight blocks each scaled in fp32 into acc.
+template <int NG, bool ZEROS>
+__device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_scl, const uint8_t *s_zro,
+                                         const __half *xt, int stride, int M, int lane, float acc[NG][4]) {
+  const int g = lane >> 2;
+  const uint4 wv = *reinterpret_cast<const uint4 *>(s_nib + lane * 16);
+  const uint2 sv = *reinterpret_cast<const uint2 *>(s_scl + g * 8);
+  uint32_t zv = 0;
+  if (ZEROS) zv = *reinterpret_cast<const uint32_t *>(s_zro + g * 4);
+  const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int bsel = 0; bsel < 2; bsel++) {
+    uint32_t lo_g = kZpLo8, hi_g = kZpHi8, lo_g8 = kZpLo8, hi_g8 = kZpHi8;
+    if (ZEROS) {
+      const uint32_t zz = zv >> (16 * bsel);
+      lo_g = zp_lo(zz & 15u);
+      hi_g = zp_hi(zz & 15u);
+      lo_g8 = zp_lo((zz >> 8) & 15u);
+      hi_g8 = zp_hi((zz >> 8) & 15u);
+    }
+    float blk[NG][4];
+#pragma unroll
+    for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) blk[ng][e] = 0.0f;
+#pragma unroll
+    for (int js = 0; js < 2; js++) {
+      const int j = 2 * bsel + js;
+      uint32_t P[4];
+      unpack_codes(w[j], lo_g, hi_g, lo_g8, hi_g8, P);
+#pragma unroll
+      for (int ng = 0; ng < NG; ng++) {
+        const int tok = ng * 8 + g;
+        uint2 b = make_uint2(0, 0);
+        if (tok < M) b = *reinterpret_cast<const uint2 *>(xt + (size_t)tok * stride + 16 * j);
+        // fragment k {2t,2t+1 | 2t+8,2t+9} <-> K offset {4t,4t+1 | 4t+2,4t+3}
+        mma_16816(blk[ng], P[0], P[2], P[1], P[3], b.x, b.y);
+      }
+    }
+    const uint32_t sp = bsel ? sv.y : sv.x;
+    const float2 sc = __half22float2(*reinterpret_cast<const __half2 *>(&sp));
+#pragma unroll
+    for (int ng = 0; ng < NG; ng++) {
+      acc[ng][0] = fmaf(sc.x, blk[ng][0], acc[ng][0]);
+      acc[ng][1] = fmaf(sc.x, blk[ng][1], acc[ng][1]);
+      acc[ng][2] = fmaf(sc.y, blk[ng][2], acc[ng][2]);
+      acc[ng][3] = fmaf(sc.y, blk[ng][3], acc[ng][3]);
+    }
+  }
+}
+
+template <int NG, bool ZEROS>
+__global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = lane & 3;
+  const int nt = blockIdx.y;
+  const int crank = blockIdx.x;
+  const int kt0 = crank * a.kt_per_cta;
+  const int kt1 = min(a.KT, kt0 + a.kt_per_cta);
+  const int ktc = kt1 - kt0;  // >= 1 (plan_gemv)
+  const GemvSmem L = gemv_smem(a.M, a.kt_per_cta, NG, ZEROS);
+  // This warp's tiles: [wt0, wt1) of the CTA's range, contiguous in memory.
+  const int wt0 = min(ktc, warp * L.tpw);
+  const int wt1 = min(ktc, wt0 + L.tpw);
+  const int nw = wt1 - wt0;
+  uint8_t *s_nib = smem + L.nib;
+  uint8_t *s_scl = smem + L.scl;
+  uint8_t *s_zro = smem + L.zro;
+  __half *xw = reinterpret_cast<__half *>(smem + L.x) + warp * L.x_warp;
+  float *red = reinterpret_cast<float *>(smem + L.red);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L.bar) + warp;
+  __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
+  if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
+
+  // 1. Each warp starts the copies of its own tiles (the TMA engine, one
+  //    mbarrier a warp): weights depend on nothing the previous kernel
+  //    writes, so this happens before any wait.
+  if (lane == 0 && nw > 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    const size_t tile = (size_t)nt * a.KT + kt0 + wt0;
+    mbar_expect_tx(bar, nw * (kTileNibBytes + kTileSclBytes + (ZEROS ? kTileZroBytes : 0)));
+    bulk_g2s(s_nib + wt0 * kTileNibBytes, reinterpret_cast<const uint8_t *>(a.nib) + tile * kTileNibBytes,
+             nw * kTileNibBytes, bar);
+    bulk_g2s(s_scl + wt0 * kTileSclBytes, reinterpret_cast<const uint8_t *>(a.scl) + tile * kTileSclBytes,
+             nw * kTileSclBytes, bar);
+    if (ZEROS)
+      bulk_g2s(s_zro + wt0 * kTileZroBytes, a.zro + tile * kTileZroBytes, nw * kTileZroBytes, bar);
+  }
+  __syncwarp();
+  if (a.trace && threadIdx.x == 0) ts[1] = globaltimer();
+
+  // 2. Wait for the kernel that wrote x. The next kernel in the stream is
+  //    let in (programmatic dependent launch) at a.trigger_at: 0 here, 1 once
+  //    x is staged, 2 after the multiplies. Later is better when its weight
+  //    copies would otherwise queue ahead of this kernel's x loads at the
+  //    SMs.
+  if (a.trigger_at == 0) pdl_trigger();
+  pdl_wait();
+  if (a.trace && threadIdx.x == 0) ts[2] = globaltimer();
+
+  // 3. Each warp stages its own K slice of x[0..M) as fp16 (no CTA barrier).
+  const int M = a.M;
+  const int stride = L.x_stride;
+  {
+    // Up to 4 loads in flight per lane before any store (one L2 round trip
+    // for the usual M * 8 tiles <= 128 chunks).
+    const int chunks = nw * (kTileK / 8);
+    const int kbase = (kt0 + wt0) * kTileK;
+    for (int base = 0; base < M * chunks; base += 4 * 32) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int idx = base + u * 32 + lane;
+        v[u] = make_uint4(0, 0, 0, 0);
+        if (idx < M * chunks) {
+          const int m = idx / chunks, c = idx - m * chunks;
+          const int k = kbase + c * 8;
+          if (k < a.K) v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int idx = base + u * 32 + lane;
+        if (idx < M * chunks) {
+          const int m = idx / chunks, c = idx - m * chunks;
+          *reinterpret_cast<uint4 *>(xw + (size_t)m * stride + c * 8) = v[u];
+        }
+      }
+    }
+  }
+  __syncwarp();
+  if (a.trigger_at == 1) pdl_trigger();
+  if (a.trace && threadIdx.x == 0) ts[3] = globaltimer();
+
+  // 4. Tensor-core steps over this warp's tiles.
+  float acc[NG][4];
+#pragma unroll
+  for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[ng][e] = 0.0f;
+  if (nw > 0) {
+    mbar_wait_bounded(bar, 0, a.flags);
+#pragma unroll 2
+    for (int i = 0; i < nw; i++) {
+      const int ti = wt0 + i;
+      tile_mma<NG, ZEROS>(s_nib + ti * kTileNibBytes, s_scl + ti * kTileSclBytes, s_zro + ti * kTileZroBytes,
+                          xw + i * kTileK + 4 * t, stride, M, lane, acc);
+    }
+  }
+
+  if (a.trigger_at == 2) pdl_trigger();
+
+  // 5. Sum the warps' fragments: red[warp][ng][e][lane], then one output
+  //    (row r, token) per thread.
+  float *part = red + kWarps * NG * 128;
+#pragma unroll
+  for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) red[((warp * NG + ng) * 4 + e) * 32 + lane] = acc[ng][e];
+  __syncthreads();
+  if (a.trace && threadIdx.x == 0) ts[4] = globaltimer();
+  constexpr int kOut = 16 * 8 * NG;
+  const int C = a.cluster;
+  for (int o = threadIdx.x; o < kOut; o += kThreads) {
+    const int r = o / (8 * NG), tok = o - r * (8 * NG);
+    const int ng = tok >> 3, tk = tok & 7;
+    const int ln = 4 * (r & 7) + (tk >> 1);
+    const int e = ((r >> 3) << 1) | (tk & 1);
+    float s = 0.0f;
+#pragma unroll
+    for (int w2 = 0; w2 < kWarps; w2++) s += red[((w2 * NG + ng) * 4 + e) * 32 + ln];
+    if (C > 1) {
+      part[o] = s;
+    } else {
+      const int n = nt * kTileRows + r;
+      if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
+    }
+  }
+
+  // 6. With a K split, rank c sums outputs o = c (mod C) over the cluster's
+  //    CTAs through distributed shared memory and writes them.
+  if (C > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    for (int o = crank + C * (int)threadIdx.x; o < kOut; o += C * kThreads) {
+      float s = 0.0f;
+      for (int c = 0; c < C; c++) s += cluster.map_shared_rank(part, c)[o];
+      const int r = o / (8 * NG), tok = o - r * (8 * NG);
+      const int n = nt * kTileRows + r;
+      if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
+    }
+    cluster.sync();
+  }
+
+  // 7. No copy may still be writing this CTA's shared memory when it exits
+  //    (only possible after a timed-out wait).
+  if (lane == 0 && nw > 0) mbar_wait_bounded(bar, 0, a.flags);
+  if (a.trace && threadIdx.x == 0) {
+    ts[5] = globaltimer();
+    trace_record(a.trace, a.trace_next, a.trace_cap, ts, a.launch_index, blockIdx.y * gridDim.x + blockIdx.x);
+  }
+}
+
+template <int NG, bool ZEROS>
+cudaError_t launch_t(const GemvArgs &a, cudaStream_t stream, bool pdl) {
+  const GemvSmem L = gemv_smem(a.M, a.kt_per_cta, NG, ZEROS);
+  auto kern = gemv_kernel<NG, ZEROS>;
+  // Function attributes once per instantiation (not per launch: launches may
+  // be captured into a CUDA graph).
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  if (L.total > kMaxSmem) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.cluster, (unsigned)a.NT, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)L.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  if (a.cluster > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = (unsigned)a.cluster;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
+    n++;
+  }
+  if (pdl) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+}  // namespace
+
+bool plan_gemv(GemvArgs &a, int num_sms) {
+  if (a.M < 1 || a.M > kGemvMaxTokens) return false;
+  const int NG = (a.M + 7) / 8;
+  const bool zeros = a.zro != nullptr;
+  // Largest K range per CTA within the shared-memory budget and the chunk
+  // count.
+  int max_ktc = kMaxTilesPerCta;
+  while (max_ktc > 1 && gemv_smem(a.M, max_ktc, NG, zeros).total > kSmemBudget) max_ktc--;
+  int C = (a.KT + max_ktc - 1) / max_ktc;
+  // Few row tiles: split K further (up to a portable cluster of 8) until the
+  // grid covers the SMs `ctas_per_sm` times, keeping at least one tile per
+  // warp. WG_GEMV_CTAS_PER_SM overrides the target (tuning).
+  static int ctas_per_sm = -1;
+  if (ctas_per_sm < 0) {
+    const char *e = getenv("WG_GEMV_CTAS_PER_SM");
+    ctas_per_sm = e ? atoi(e) : 1;
+    if (ctas_per_sm < 1) ctas_per_sm = 1;
+  }
+  while (C < 8 && a.NT * C < ctas_per_sm * num_sms && (a.KT + C) / (C + 1) >= kWarps) C++;
+  if (C > 16) return false;
+  const int ktc = (a.KT + C - 1) / C;
+  C = (a.KT + ktc - 1) / ktc;
+  a.kt_per_cta = ktc;
+  a.cluster = C;
+  return true;
+}
+
+cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl) {
+  const int NG = (a.M + 7) / 8;
+  const bool z = a.zro != nullptr;
+  switch (NG) {
+    case 1: return z ? launch_t<1, true>(a, stream, pdl) : launch_t<1, false>(a, stream, pdl);
+    case 2: return z ? launch_t<2, true>(a, stream, pdl) : launch_t<2, false>(a, stream, pdl);
+    case 3: return z ? launch_t<3, true>(a, stream, pdl) : launch_t<3, false>(a, stream, pdl);
+    case 4: return z ? launch_t<4, true>(a, stream, pdl) : launch_t<4, false>(a, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace wg

@@ -1,0 +1,58 @@
+// Kernel entry points of the Q4 library (internal; the C ABI is capi.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "q4_layout.cuh"
+
+namespace wg {
+
+// Source layouts the repack kernel reads.
+enum SrcKind : int {
+  kSrcGguf = 0,   // llama.cpp Q4_0 blocks (src/repack.ts:60-87)
+  kSrcNbits = 1,  // onnxruntime MatMulNBits (src/repack.ts:342-392)
+  kSrcQmat = 2,   // the reference's QuantMatrix (src/weights.ts:5-21)
+};
+
+struct RepackArgs {
+  Q4Dims d;
+  uint32_t *nib;
+  uint16_t *scl;
+  uint8_t *zro;               // null for matrices without zero points
+  const uint8_t *src;         // codes (and GGUF scales), on the device
+  const uint8_t *scale_src;   // Nbits: fp16 scale bytes; Qmat: u16 scales
+  const uint8_t *zero_src;    // Nbits: packed zero points; Qmat: u8 zeros
+  const int32_t *src_rows;    // nullable, device
+  int row0, rows;
+  int kind;
+};
+
+cudaError_t launch_repack(const RepackArgs &a, cudaStream_t stream);
+
+// The decode GEMV: y[M][N] = x[M][K] . W^T for M <= 32.
+struct GemvArgs {
+  const uint32_t *nib;
+  const uint16_t *scl;
+  const uint8_t *zro;  // nullable
+  const void *x;
+  void *y;
+  int M, N, K, NT, KT;
+  int x_dtype, y_dtype;
+  int kt_per_cta;  // K tiles per CTA (the cluster splits KT)
+  int cluster;     // CTAs per cluster along K
+  unsigned *flags; // device error flags (kFlagTimeout)
+  // Tracing (wg_trace): records of WG_TRACE_WORDS u64, or null.
+  unsigned long long *trace;
+  unsigned long long *trace_next;  // device counter of records claimed
+  unsigned long long trace_cap;    // records that fit
+  unsigned launch_index;
+  int trigger_at;  // when dependents may launch: 0 entry, 1 x staged, 2 multiplies done
+};
+
+constexpr int kGemvMaxTokens = 32;
+cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl);
+// Plans kt_per_cta / cluster for a shape; false if the shape is too large.
+bool plan_gemv(GemvArgs &a, int num_sms);
+
+}  // namespace wg
