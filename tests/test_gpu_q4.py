@@ -205,3 +205,56 @@ def test_config1_sweep(s, M):
     check_close(y, ref, f"config 1 M={M} vs fp64")
     emul = O.c_split_emulate(host, x16) if M <= 8 else O.c_prefill_emulate(host, x16)
     check_close(y, emul, f"config 1 M={M} vs emulation")
+
+
+# ---------------------------------------------------------------- prefill GEMM (tcgen05)
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (33, 128, 128),      # smallest GEMM row count, one CTA
+    (64, 128, 128),
+    (64, 512, 4096),     # few tiles: K split across CTAs (fp32 workspace)
+    (65, 128, 256),      # second token tile, partial
+    (129, 100, 96),      # N not a multiple of 128 (TMA fills), K % 64 == 32
+    (300, 1024, 2048),
+    (1024, 512, 512),
+    (96, 2560, 2048),    # a q|k|v-shaped matrix
+])
+def test_gemm_parity(M, N, K):
+    blocks, m, host = make(N, K, M + N + K)
+    y, x16 = run(m, O.config_activations(M, K, M))
+    check_close(y, O.c_ref_f64(blocks, x16, N, K), f"GEMM {M}x{N}x{K} vs fp64")
+    check_close(y, O.c_prefill_emulate(host, x16), f"GEMM {M}x{N}x{K} vs f16 route")
+
+
+def test_gemm_zero_points():
+    N, K, M = 256, 1024, 100
+    quant, scales, zp = _nbits(N, K, 8)
+    m = wg.newQuantMatrix(N, K, withZeros=True)
+    wg.packMatMulNBits(m, 0, quant, scales, zp, N)
+    host = O.HostQuantMatrix(N, K, with_zeros=True)
+    O.c_pack_matmulnbits(host, 0, quant, scales, zp, N)
+    W = np.stack([O.c_matrix_row(host, n) for n in range(N)]).astype(np.float64)
+    y, x16 = run(m, O.config_activations(M, K, 5))
+    check_close(y, x16.astype(np.float64) @ W.T, "GEMM zeros vs fp64")
+
+
+@pytest.mark.parametrize("xd,yd", [("float32", "float16"), ("bfloat16", "float32"), ("float16", "bfloat16")])
+def test_gemm_dtypes(xd, yd):
+    N, K, M = 384, 512, 70
+    blocks, m, host = make(N, K, 21)
+    y, xq = run(m, O.config_activations(M, K, 2), getattr(torch, xd), getattr(torch, yd))
+    ref = O.c_ref_f64(blocks, xq, N, K)
+    tol = 4e-3 if yd == "bfloat16" else TOL
+    l2, mx = O.rel_errors(y, ref)
+    assert l2 <= tol and mx <= tol, f"{xd}->{yd}: {l2:.2e} {mx:.2e}"
+
+
+def test_gemm_repeated_calls_are_deterministic():
+    N, K, M = 512, 1024, 256
+    _, m, _ = make(N, K, 3)
+    x = torch.from_numpy(O.config_activations(M, K, 3)).to("cuda", torch.float16)
+    a = wg.matmul(x, m, out_dtype=torch.float32)
+    b = wg.matmul(x, m, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)

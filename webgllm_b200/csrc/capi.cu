@@ -25,6 +25,8 @@ struct wg_ctx {
   unsigned *d_flags = nullptr;  // device error flags (kFlag*)
   uint8_t *staging = nullptr;   // device copy of a repack's source bytes
   size_t staging_bytes = 0;
+  uint8_t *work = nullptr;      // matmul scratch: fp16 copy of x, split-K sums
+  size_t work_bytes = 0;
   bool pdl = true;              // programmatic dependent launch for the GEMV
   int trigger_at = 1;           // GemvArgs::trigger_at (WG_GEMV_TRIGGER overrides)
   unsigned long long *trace = nullptr;       // wg_trace buffer (device) or null
@@ -90,6 +92,21 @@ int ensure_staging(wg_ctx *ctx, size_t bytes) {
 }
 
 bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Grows the matmul scratch to `bytes` (stream-ordered, as ensure_staging).
+// It only grows, so a shape that has run once never allocates again (and
+// may then be captured into a CUDA graph).
+int ensure_work(wg_ctx *ctx, size_t bytes) {
+  if (bytes <= ctx->work_bytes) return WG_OK;
+  WG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if (ctx->work) WG_CUDA(ctx, cudaFree(ctx->work));
+  ctx->work = nullptr;
+  ctx->work_bytes = 0;
+  size_t want = align_up(bytes, 1 << 20);
+  WG_CUDA(ctx, cudaMalloc(&ctx->work, want));
+  ctx->work_bytes = want;
+  return WG_OK;
+}
 
 int check_shape(wg_ctx *ctx, int N, int K) {
   if (N <= 0 || K <= 0)
@@ -200,6 +217,7 @@ int wg_destroy(wg_ctx *ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->staging) cudaFree(ctx->staging);
+  if (ctx->work) cudaFree(ctx->work);
   if (ctx->d_flags) cudaFree(ctx->d_flags);
   if (ctx->d_trace_next) cudaFree(ctx->d_trace_next);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -454,9 +472,37 @@ int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int
                 ctx->device);
   int st = use_device(ctx);
   if (st) return st;
+  // Many rows: the tcgen05 GEMM (src/engine.ts:4684: more rows than the
+  // split path takes go to the prompt matmul).
+  if (M > wg::kGemvMaxTokens && wg::gemm_supported()) {
+    wg::GemmArgs g{};
+    g.nib = m->nib;
+    g.scl = m->scl;
+    g.zro = m->zro;
+    g.y = y;
+    g.M = M;
+    g.N = m->d.N;
+    g.K = m->d.K;
+    g.NT = m->d.NT;
+    g.KT = m->d.KT;
+    g.y_dtype = y_dtype;
+    g.flags = ctx->d_flags;
+    const size_t ws_bytes = wg::plan_gemm(g, ctx->num_sms);
+    const size_t xh_bytes = x_dtype == WG_F16 ? 0 : align_up((size_t)M * m->d.K * 2, 256);
+    st = ensure_work(ctx, xh_bytes + ws_bytes);
+    if (st) return st;
+    const void *xh = x;
+    if (x_dtype != WG_F16) {
+      WG_CUDA(ctx, wg::launch_to_f16(x, x_dtype, ctx->work, (size_t)M * m->d.K, ctx->stream));
+      xh = ctx->work;
+    }
+    g.ws = ws_bytes ? reinterpret_cast<float *>(ctx->work + xh_bytes) : nullptr;
+    WG_CUDA(ctx, wg::launch_gemm(g, xh, ctx->stream));
+    return WG_OK;
+  }
   const size_t xsz = x_dtype == WG_F32 ? 4 : 2, ysz = y_dtype == WG_F32 ? 4 : 2;
-  // Rows beyond what one GEMV launch holds go in chunks (until the
-  // tensor-core GEMM takes them).
+  // Rows beyond one GEMV launch go in chunks (only where the GEMM is
+  // unavailable).
   for (int m0 = 0; m0 < M; m0 += wg::kGemvMaxTokens) {
     const int mc = M - m0 < wg::kGemvMaxTokens ? M - m0 : wg::kGemvMaxTokens;
     wg::GemvArgs a{};

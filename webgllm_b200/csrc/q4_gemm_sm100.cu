@@ -1,0 +1,441 @@
+// The Q4 prefill GEMM on Blackwell tensor cores: y = x . W^T for many rows.
+//
+// Replaces the reference's prompt matmuls (src/engine.ts:4969-5234:
+// matmulQuad, src/gpu/kernels.ts:370-429; the f16 route dequantRgba4 /
+// dequantBytes + matmulF16, kernels.ts:436-735), whose weights are first
+// dequantised to an fp16 scratch texture (`(q - z) * d` rounded to half,
+// kernels.ts:467, :562) and then multiplied with fp32 sums. Here the
+// dequantisation is fused: the fp16 weights never leave the SM.
+//
+// One CTA computes a 128-row (weights) x BM-row (tokens) tile over a range
+// of K, in stages of 64 K:
+//   warp 0     TMA producer: the x tile (tensor map, 128-byte swizzle, the
+//              MMA's B operand) and the stage's 8 code tiles, scales and
+//              zero points (3-D tensor maps over the tiled planes) into a
+//              shared-memory ring;
+//   warps 2-9  dequantisers: codes -> fp16 (q - z) * d with the scale rounded
+//              in as the reference's f16 route does, written straight into
+//              tensor memory with tcgen05.st.16x256b, whose thread layout is
+//              the tile layout's (q4_layout.cuh): the MMA's A operand lives in
+//              TMEM, so dequantised weights cost no shared-memory bandwidth;
+//   warp 1     one thread issues tcgen05.mma (kind::f16, A from TMEM, B from
+//              shared memory, fp32 accumulator in TMEM) and commits each
+//              stage back to the ring;
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator, stored as y (or,
+//              when K is split across CTAs for parallelism, as this split's
+//              fp32 slab of a workspace that a second kernel sums in a fixed
+//              order: deterministic, no atomics).
+// Every wait is bounded (mbar_wait_bounded) and TMEM is freed on every path.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "device_utils.cuh"
+#include "q4_kernels.cuh"
+
+namespace wg {
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kBN = 128;          // weight rows per CTA = MMA M
+constexpr int kDequantWarps = 8;  // warps 2..9
+constexpr int kGemmThreads = (2 + kDequantWarps) * 32;
+constexpr int kXStageBytes(int BM) { return BM * 128; }
+constexpr int kNibStageBytes = 8 * kTileNibBytes;  // 4096
+constexpr int kSclStageBytes = 8 * kTileSclBytes;  // 512
+constexpr int kZroStageBytes = 8 * kTileZroBytes;  // 256
+constexpr int kTmemACol = 128;                     // A stages at columns [128, 256)
+constexpr int kTmemCols = 256;                     // accumulator [0, BM <= 128) + A ring
+// At most two CTAs an SM (2 x 256 TMEM columns = all 512): the launch asks
+// for at least this much shared memory so that a third never waits in
+// tcgen05.alloc.
+constexpr int kMinSmemPerCta = 100 * 1024;
+
+struct GemmSmem {
+  int x, nib, scl, zro, bar, tmem_slot, total;
+};
+
+__host__ __device__ inline GemmSmem gemm_smem(int BM) {
+  GemmSmem s;
+  s.x = 0;  // 1024-aligned (SW128 atoms)
+  s.nib = s.x + kStages * kXStageBytes(BM);
+  s.scl = s.nib + kStages * kNibStageBytes;
+  s.zro = s.scl + kStages * kSclStageBytes;
+  s.bar = s.zro + kStages * kZroStageBytes;
+  // full[S], empty[S], afull[S], accfull
+  s.tmem_slot = s.bar + (3 * kStages + 1) * 8;
+  s.total = s.tmem_slot + 16;
+  return s;
+}
+
+
+// ---- tcgen05 / TMA wrappers ------------------------------------------------
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_16x256b_x4(uint32_t taddr, const uint32_t v[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float v[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory descriptor of a K-major operand tile in the canonical
+// 128-byte-swizzled layout (8-row atoms of 128-byte rows, 1024 bytes apart).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) /* LBO (unused) */ |
+         ((uint64_t)(1024 >> 4) << 32) /* SBO */ | ((uint64_t)1 << 46) /* version */ |
+         ((uint64_t)2 << 61) /* SWIZZLE_128B */;
+}
+
+// Instruction descriptor: kind::f16, A and B fp16, K-major, fp32 accumulator,
+// M = 128, N = BM.
+__host__ __device__ constexpr uint32_t idesc_f16(int BM) {
+  return (1u << 4) | ((uint32_t)(BM >> 3) << 17) | ((uint32_t)(kBN >> 4) << 24);
+}
+
+template <int BM, bool ZEROS>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_nib,
+                const __grid_constant__ CUtensorMap tm_scl, const __grid_constant__ CUtensorMap tm_zro,
+                const GemmArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte-swizzled tiles (the launch adds
+  // 1024 bytes of slack).
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const GemmSmem L = gemm_smem(BM);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
+  uint64_t *empty = full + kStages;
+  uint64_t *afull = empty + kStages;
+  uint64_t *accfull = afull + kStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
+  __shared__ int aborted;
+
+  const int nt0 = blockIdx.x * (kBN / kTileRows);  // first 16-row tile
+  const int m0 = blockIdx.y * BM;
+  const int kpc = a.kt_per_split;  // K tiles per split
+  const int kt_begin = blockIdx.z * kpc;
+  const int kt_end = min(a.KT, kt_begin + kpc);
+  const int nk = kt_end - kt_begin;  // >= 1
+
+  if (threadIdx.x == 0) {
+    aborted = 0;
+    for (int i = 0; i < kStages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      mbar_init(&afull[i], kDequantWarps * 32);
+    }
+    mbar_init(accfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_d = tmem;               // accumulator columns [0, BM)
+  const uint32_t tmem_a = tmem + kTmemACol;   // A stage s at columns + 32 s
+
+  auto wait = [&](uint64_t *bar, uint32_t parity) {
+    if (aborted) return;
+    if (!mbar_wait_bounded(bar, parity, a.flags)) aborted = 1;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t bytes = kXStageBytes(BM) + kNibStageBytes + kSclStageBytes + (ZEROS ? kZroStageBytes : 0);
+      for (int it = 0; it < nk; it++) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        wait(&empty[s], ph ^ 1);
+        const int kt = kt_begin + it;
+        mbar_expect_tx(&full[s], bytes);
+        tma_load_2d(smem + L.x + s * kXStageBytes(BM), &tm_x, kt * kTileK, m0, &full[s]);
+        tma_load_3d(smem + L.nib + s * kNibStageBytes, &tm_nib, 0, kt, nt0, &full[s]);
+        tma_load_3d(smem + L.scl + s * kSclStageBytes, &tm_scl, 0, kt, nt0, &full[s]);
+        if (ZEROS) tma_load_3d(smem + L.zro + s * kZroStageBytes, &tm_zro, 0, kt, nt0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(BM);
+      for (int it = 0; it < nk; it++) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        wait(&full[s], ph);
+        wait(&afull[s], ph);
+        tc_fence_after();
+        const uint64_t bdesc = sw128_desc(smem_u32(smem + L.x + s * kXStageBytes(BM)));
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          mma_f16_tmem_a(tmem_d, tmem_a + s * 32 + kk * 8, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(accfull);
+    }
+  } else {
+    // Dequantisers: warp w handles tile 2q + sub of each stage (16 rows),
+    // q = w % 4 its TMEM lane quarter.
+    const int q = warp & 3;
+    const int sub = (warp - 2) >> 2;
+    const int tile = 2 * q + sub;
+    const int g = lane >> 2;
+    for (int it = 0; it < nk; it++) {
+      const int s = it % kStages;
+      const uint32_t ph = (it / kStages) & 1;
+      wait(&full[s], ph);
+      wait(&empty[s], ph ^ 1);  // the MMA that last read A stage s is done
+      tc_fence_after();
+      const uint4 wv = *reinterpret_cast<const uint4 *>(smem + L.nib + s * kNibStageBytes + tile * kTileNibBytes +
+                                                        lane * 16);
+      const uint2 sv =
+          *reinterpret_cast<const uint2 *>(smem + L.scl + s * kSclStageBytes + tile * kTileSclBytes + g * 8);
+      uint32_t zv = 0x08080808u;
+      if (ZEROS)
+        zv = *reinterpret_cast<const uint32_t *>(smem + L.zro + s * kZroStageBytes + tile * kTileZroBytes + g * 4);
+      const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t v[16];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int bsel = j >> 1;
+        const uint32_t zz = zv >> (16 * bsel);
+        const uint32_t z_g = zz & 15u, z_g8 = (zz >> 8) & 15u;
+        uint32_t P[4];
+        unpack_codes(w[j], zp_lo(z_g), zp_hi(z_g), zp_lo(z_g8), zp_hi(z_g8), P);
+        const uint32_t sp = bsel ? sv.y : sv.x;  // (d_g, d_g8)
+        const uint32_t d_g = (sp & 0xFFFFu) * 0x00010001u;
+        const uint32_t d_g8 = (sp >> 16) * 0x00010001u;
+        // (q - z) * d rounded to fp16, as the reference's dequant pass.
+        v[4 * j + 0] = hmul2_u(P[0], d_g);
+        v[4 * j + 1] = hmul2_u(P[1], d_g);
+        v[4 * j + 2] = hmul2_u(P[2], d_g8);
+        v[4 * j + 3] = hmul2_u(P[3], d_g8);
+      }
+      tmem_st_16x256b_x4(tmem_a + ((uint32_t)(32 * q + 16 * sub) << 16) + s * 32, v);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&afull[s]);
+    }
+
+    // Epilogue: this warp's 32 TMEM lanes (weight rows 32q..32q+31) and half
+    // of the token columns.
+    wait(accfull, 0);
+    tc_fence_after();
+    const int n = nt0 * kTileRows + 32 * q + lane;
+    const int c_begin = sub * (BM / 2), c_end = c_begin + BM / 2;
+    for (int c = c_begin; c < c_end; c += 16) {
+      float v[16];
+      tmem_ld_32x32b_x16(tmem_d + ((uint32_t)(32 * q) << 16) + c, v);
+      if (n < a.N) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int tok = m0 + c + i;
+          if (tok < a.M) {
+            if (a.ws) a.ws[((size_t)blockIdx.z * a.M + tok) * a.N + n] = v[i];  // this split's slab
+            else store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, v[i]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  // No TMA may still be writing this CTA's shared memory when it exits (only
+  // possible after a timed-out wait): wait for the last round of each stage.
+  if (threadIdx.x == 0 && aborted) {
+    for (int it = nk > kStages ? nk - kStages : 0; it < nk; it++)
+      mbar_wait_bounded(&full[it % kStages], (it / kStages) & 1, a.flags);
+  }
+}
+
+// Sums the K splits' slabs in split order (deterministic) into y.
+__global__ void finalize_kernel(const float *ws, int splits, void *y, int dtype, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int z = 0; z < splits; z++) s += ws[(size_t)z * n + i];
+    store_out(y, dtype, i, s);
+  }
+}
+
+// ---- host side -------------------------------------------------------------
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  return fn;
+}
+
+bool encode_x(CUtensorMap *m, const void *x, int M, int K, int BM) {
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)BM};
+  cuuint32_t elem[2] = {1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(x), dims, strides, box, elem,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// A tiled plane (q4_layout.cuh) as a 3-D u32 tensor [NT][KT][words].
+bool encode_plane(CUtensorMap *m, const void *base, int words, int KT, int NT) {
+  cuuint64_t dims[3] = {(cuuint64_t)words, (cuuint64_t)KT, (cuuint64_t)NT};
+  cuuint64_t strides[2] = {(cuuint64_t)words * 4, (cuuint64_t)words * 4 * KT};
+  cuuint32_t box[3] = {(cuuint32_t)words, 1, 8};
+  cuuint32_t elem[3] = {1, 1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(base), dims, strides, box, elem,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BM, bool ZEROS>
+cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream) {
+  const GemmSmem L = gemm_smem(BM);
+  auto kern = gemm_kernel<BM, ZEROS>;
+  static_assert(BM <= kTmemACol, "accumulator columns overlap the A ring");
+  const int smem_bytes = L.total + 1024 > kMinSmemPerCta ? L.total + 1024 : kMinSmemPerCta;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  CUtensorMap tx, tn, ts, tz;
+  if (!encode_x(&tx, x, a.M, a.K, BM) || !encode_plane(&tn, a.nib, kTileNibBytes / 4, a.KT, a.NT) ||
+      !encode_plane(&ts, a.scl, kTileSclBytes / 4, a.KT, a.NT))
+    return cudaErrorInvalidValue;
+  tz = ts;
+  if (ZEROS && !encode_plane(&tz, a.zro, kTileZroBytes / 4, a.KT, a.NT)) return cudaErrorInvalidValue;
+  dim3 grid((unsigned)((a.NT + 7) / 8), (unsigned)((a.M + BM - 1) / BM), (unsigned)a.splits);
+  kern<<<grid, kGemmThreads, smem_bytes, stream>>>(tx, tn, ts, tz, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_supported() { return encode_fn() != nullptr; }
+
+static int gemm_tile_m(int M) { return M <= 64 ? 64 : 128; }
+
+size_t plan_gemm(GemmArgs &a, int num_sms) {
+  const int BM = gemm_tile_m(a.M);
+  const int tiles = ((a.NT + 7) / 8) * ((a.M + BM - 1) / BM);
+  // Split K until the grid covers the SMs, keeping >= 4 stages per split.
+  int splits = 1;
+  while (tiles * splits < num_sms && a.KT / (splits + 1) >= 4) splits++;
+  a.kt_per_split = (a.KT + splits - 1) / splits;
+  a.splits = (a.KT + a.kt_per_split - 1) / a.kt_per_split;
+  return a.splits > 1 ? (size_t)a.splits * a.M * a.N * sizeof(float) : 0;
+}
+
+cudaError_t launch_gemm(const GemmArgs &args, const void *x_f16, cudaStream_t stream) {
+  if (!encode_fn()) return cudaErrorNotSupported;
+  GemmArgs a = args;
+  const int BM = gemm_tile_m(a.M);
+  cudaError_t e;
+  if (a.splits > 1) {
+    if (!a.ws) return cudaErrorInvalidValue;
+  } else {
+    a.ws = nullptr;
+  }
+  const bool z = a.zro != nullptr;
+  if (BM == 64) e = z ? launch_bm<64, true>(a, x_f16, stream) : launch_bm<64, false>(a, x_f16, stream);
+  else e = z ? launch_bm<128, true>(a, x_f16, stream) : launch_bm<128, false>(a, x_f16, stream);
+  if (e != cudaSuccess || a.splits == 1) return e;
+  const size_t n = (size_t)a.M * a.N;
+  const size_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+  finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a.ws, a.splits, a.y, a.y_dtype, n);
+  return cudaGetLastError();
+}
+
+namespace {
+__global__ void to_f16_kernel(const void *x, int dtype, uint4 *out, size_t n8) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = load_x8_f16(x, dtype, i * 8);
+}
+}  // namespace
+
+cudaError_t launch_to_f16(const void *x, int dtype, void *out, size_t n, cudaStream_t stream) {
+  const size_t n8 = n / 8;
+  const size_t blocks = (n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096;
+  to_f16_kernel<<<(unsigned)(blocks ? blocks : 1), 256, 0, stream>>>(x, dtype, reinterpret_cast<uint4 *>(out), n8);
+  return cudaGetLastError();
+}
+
+}  // namespace wg

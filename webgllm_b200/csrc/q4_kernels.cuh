@@ -55,4 +55,25 @@ cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl);
 // Plans kt_per_cta / cluster for a shape; false if the shape is too large.
 bool plan_gemv(GemvArgs &a, int num_sms);
 
+// The prefill GEMM (tcgen05): y[M][N] = x[M][K] . W^T for M > 32, x fp16.
+struct GemmArgs {
+  const uint32_t *nib;
+  const uint16_t *scl;
+  const uint8_t *zro;  // nullable
+  void *y;
+  float *ws;           // fp32 [splits][M][N] workspace when K is split, else null
+  int M, N, K, NT, KT;
+  int y_dtype;
+  int splits, kt_per_split;
+  unsigned *flags;
+};
+
+bool gemm_supported();
+// Chooses the K split (splits, kt_per_split); returns the workspace bytes
+// it needs (0 when K is not split).
+size_t plan_gemm(GemmArgs &a, int num_sms);
+cudaError_t launch_gemm(const GemmArgs &a, const void *x_f16, cudaStream_t stream);
+// x (f32 / bf16) -> fp16, saturating like packH2; n a multiple of 8.
+cudaError_t launch_to_f16(const void *x, int dtype, void *out, size_t n, cudaStream_t stream);
+
 }  // namespace wg
