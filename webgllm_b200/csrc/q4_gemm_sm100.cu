@@ -7,8 +7,8 @@
 // kernels.ts:467, :562) and then multiplied with fp32 sums. Here the
 // dequantisation is fused: the fp16 weights never leave the SM.
 //
-// One CTA computes a 128-row (weights) x BM-row (tokens) tile over a range
-// of K, in stages of 64 K:
+// One CTA computes a 128-row (weights) x BM-row (tokens, 64 / 128 / 256)
+// tile over a range of K, in stages of 64 K:
 //   warp 0     TMA producer: the x tile (tensor map, 128-byte swizzle, the
 //              MMA's B operand) and the stage's 8 code tiles, scales and
 //              zero points (3-D tensor maps over the tiled planes) into a
@@ -28,6 +28,8 @@
 // Every wait is bounded (mbar_wait_bounded) and TMEM is freed on every path.
 #include <cuda.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "device_utils.cuh"
 #include "q4_kernels.cuh"
@@ -44,12 +46,15 @@ constexpr int kXStageBytes(int BM) { return BM * 128; }
 constexpr int kNibStageBytes = 8 * kTileNibBytes;  // 4096
 constexpr int kSclStageBytes = 8 * kTileSclBytes;  // 512
 constexpr int kZroStageBytes = 8 * kTileZroBytes;  // 256
-constexpr int kTmemACol = 128;                     // A stages at columns [128, 256)
-constexpr int kTmemCols = 256;                     // accumulator [0, BM <= 128) + A ring
-// At most two CTAs an SM (2 x 256 TMEM columns = all 512): the launch asks
-// for at least this much shared memory so that a third never waits in
-// tcgen05.alloc.
-constexpr int kMinSmemPerCta = 100 * 1024;
+// TMEM: the fp32 accumulator at columns [0, BM), the A ring (4 stages x 32
+// columns) after it. BM <= 128: 256 columns a CTA, two CTAs an SM; BM = 256:
+// all 512 columns, one CTA an SM.
+__host__ __device__ constexpr int tmem_a_col(int BM) { return BM <= 128 ? 128 : 256; }
+__host__ __device__ constexpr int tmem_cols(int BM) { return BM <= 128 ? 256 : 512; }
+// The launch asks for at least this much shared memory so that no more CTAs
+// share an SM than its 512 TMEM columns hold (a surplus CTA would wait in
+// tcgen05.alloc).
+__host__ __device__ constexpr int min_smem(int BM) { return BM <= 128 ? 100 * 1024 : 120 * 1024; }
 
 struct GemmSmem {
   int x, nib, scl, zro, bar, tmem_slot, total;
@@ -191,13 +196,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(accfull, 1);
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) tmem_alloc(tmem_slot, tmem_cols(BM));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_d = tmem;               // accumulator columns [0, BM)
-  const uint32_t tmem_a = tmem + kTmemACol;   // A stage s at columns + 32 s
+  const uint32_t tmem_a = tmem + tmem_a_col(BM);   // A stage s at columns + 32 s
 
   auto wait = [&](uint64_t *bar, uint32_t parity) {
     if (aborted) return;
@@ -306,7 +311,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, tmem_cols(BM));
   }
   // No TMA may still be writing this CTA's shared memory when it exits (only
   // possible after a timed-out wait): wait for the last round of each stage.
@@ -368,8 +373,8 @@ template <int BM, bool ZEROS>
 cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream) {
   const GemmSmem L = gemm_smem(BM);
   auto kern = gemm_kernel<BM, ZEROS>;
-  static_assert(BM <= kTmemACol, "accumulator columns overlap the A ring");
-  const int smem_bytes = L.total + 1024 > kMinSmemPerCta ? L.total + 1024 : kMinSmemPerCta;
+  static_assert(BM <= tmem_a_col(BM) && tmem_a_col(BM) + kStages * 32 <= tmem_cols(BM), "TMEM columns");
+  const int smem_bytes = L.total + 1024 > min_smem(BM) ? L.total + 1024 : min_smem(BM);
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
@@ -391,7 +396,17 @@ cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream) {
 
 bool gemm_supported() { return encode_fn() != nullptr; }
 
-static int gemm_tile_m(int M) { return M <= 64 ? 64 : 128; }
+// Token rows per CTA; WG_GEMM_BM (64 / 128 / 256) overrides (tuning).
+static int gemm_tile_m(int M) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char *e = getenv("WG_GEMM_BM");
+    forced = e ? atoi(e) : 0;
+    if (forced != 64 && forced != 128 && forced != 256) forced = 0;
+  }
+  if (forced) return forced;
+  return M <= 64 ? 64 : 128;
+}
 
 size_t plan_gemm(GemmArgs &a, int num_sms) {
   const int BM = gemm_tile_m(a.M);
@@ -416,7 +431,8 @@ cudaError_t launch_gemm(const GemmArgs &args, const void *x_f16, cudaStream_t st
   }
   const bool z = a.zro != nullptr;
   if (BM == 64) e = z ? launch_bm<64, true>(a, x_f16, stream) : launch_bm<64, false>(a, x_f16, stream);
-  else e = z ? launch_bm<128, true>(a, x_f16, stream) : launch_bm<128, false>(a, x_f16, stream);
+  else if (BM == 128) e = z ? launch_bm<128, true>(a, x_f16, stream) : launch_bm<128, false>(a, x_f16, stream);
+  else e = z ? launch_bm<256, true>(a, x_f16, stream) : launch_bm<256, false>(a, x_f16, stream);
   if (e != cudaSuccess || a.splits == 1) return e;
   const size_t n = (size_t)a.M * a.N;
   const size_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
