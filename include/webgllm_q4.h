@@ -138,6 +138,22 @@ int wg_q4_matrix_row(wg_ctx *ctx, const wg_q4mat *m, int n, float *out);
 int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype,
                  int M, void *y, int y_dtype);
 
+/* The same product as wg_q4_matmul, allocating no device memory. It has no
+ * counterpart in the reference (WebGL allocates through textures). For
+ * callers that cannot let the library allocate: code capturing the call into
+ * a CUDA graph (no allocation is allowed during stream capture), engines that
+ * budget device memory up front, and decode loops that cannot afford the
+ * device synchronisation of cudaMalloc / cudaFree. Its scratch (the fp16
+ * copy of an f32 / bf16 x and the GEMM's split-K partial sums) is one fixed
+ * 32 MiB array in the library's device memory, held on every GPU that loads
+ * the library until the process exits; a call that would need more returns
+ * WG_UNSUPPORTED and says how much. The first call on a device looks up the
+ * array's device address: make it before capturing a stream. All calls on a
+ * device share the array, so calls whose work overlaps on the GPU (other
+ * streams or contexts of the same device) race on it. */
+int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x,
+                        int x_dtype, int M, void *y, int y_dtype);
+
 /* ---- tracing ------------------------------------------------------------- */
 
 /* Gpu.trace / drawTrace (src/gpu/gl.ts:553-598), per CTA instead of per

@@ -50,6 +50,7 @@ SIGNATURES = {
     "wg_q4_write_quantmatrix": (_I, [_P, _P, _P, _P, _P]),
     "wg_q4_matrix_row": (_I, [_P, _P, _I, _P]),
     "wg_q4_matmul": (_I, [_P, _P, _P, _I, _I, _P, _I]),
+    "wg_q4_matmul_static": (_I, [_P, _P, _P, _I, _I, _P, _I]),
     "wg_trace": (_I, [_P, _P, _SZ]),
     "wg_trace_count": (_I, [_P, ctypes.POINTER(_SZ)]),
     "wg_error_string": (ctypes.c_char_p, [_I]),

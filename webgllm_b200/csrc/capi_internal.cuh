@@ -1,0 +1,40 @@
+// The C ABI's opaque types (include/webgllm_q4.h), shared by the files that
+// implement its entry points.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "common.cuh"
+#include "q4_layout.cuh"
+
+struct wg_ctx {
+  int device = 0;
+  int num_sms = wg::kB200Sms;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  unsigned *d_flags = nullptr;  // device error flags (kFlag*)
+  uint8_t *staging = nullptr;   // device copy of a repack's source bytes
+  size_t staging_bytes = 0;
+  uint8_t *work = nullptr;      // matmul scratch: fp16 copy of x, split-K sums
+  size_t work_bytes = 0;
+  bool pdl = true;              // programmatic dependent launch for the GEMV
+  int trigger_at = 1;           // GemvArgs::trigger_at (WG_GEMV_TRIGGER overrides)
+  unsigned long long *trace = nullptr;       // wg_trace buffer (device) or null
+  unsigned long long trace_cap = 0;          // records that fit
+  unsigned long long *d_trace_next = nullptr;  // device record counter
+  unsigned launch_index = 0;
+  std::string last_error;
+};
+
+struct wg_q4mat {
+  wg::Q4Dims d;
+  int device;
+  uint8_t *base;  // one allocation: nib | scl | zro
+  uint32_t *nib;
+  uint16_t *scl;
+  uint8_t *zro;
+  size_t bytes;
+};
+
