@@ -1,0 +1,84 @@
+/*
+ * webgllm_decoder.h: the decoder-layer kernels around the Q4 matmuls
+ * (libwebgllm_b200.so), standing in for the engine's other per-layer passes
+ * (src/engine.ts:8875-9304 forwardBatch) on the B200. Paths are inside the
+ * webgllm package (packages/webgllm/). Conventions as webgllm_q4.h: status
+ * returns, device pointers, work enqueued on the context's stream.
+ *
+ * Layouts: row-major [rows][features]. The residual stream is fp32; matmul
+ * inputs fp16 (WG_F16); caches fp16. `pos` is a device int32 holding the
+ * position of row 0 (rows are consecutive positions), so a decode step can
+ * be replayed from a CUDA graph while the position advances on the device.
+ */
+#ifndef WEBGLLM_DECODER_H
+#define WEBGLLM_DECODER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "webgllm_q4.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Embedding rows (src/gpu/kernels.ts:1092; engine.ts:8961-9030): out[r] =
+ * table[ids[r]] as fp32, table fp16 [V][D]; ids outside [0, V) read row 0. */
+int wg_embed(wg_ctx *ctx, const int32_t *ids, int rows, const void *table, int V, int D, float *out);
+
+/* Residual add + RMS norm (addNormed, src/engine.ts:5695; RMS passes
+ * src/gpu/kernels.ts:1158-1372): x += add (if add is not NULL; x keeps the
+ * sum), out = x / sqrt(mean(x^2) + eps) * weight in out_dtype. */
+int wg_rmsnorm(wg_ctx *ctx, float *x, const float *add, const float *weight, float eps, int rows, int D,
+               void *out, int out_dtype);
+
+/* qk-norm + RoPE + KV append (headPrep, src/gpu/kernels.ts:2196-2322):
+ * qkv fp32 [rows][(H + 2 Hkv) Dh] (q | k | v). Per head, optional RMS norm
+ * over Dh with q_norm / k_norm weights (NULL: none), then rotate-half RoPE
+ * of the pairs (j, j + Dh/2) by (pos + r) * theta^(-2j/Dh). q_out fp16
+ * [rows][H][Dh] scaled by 1/sqrt(Dh); k (rotated) and v appended to the fp16
+ * caches [Hkv][cache_len][Dh] at positions pos..pos+rows-1. Dh % 64 == 0.
+ * A position past cache_len is skipped and reported by wg_sync. */
+int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int H, int Hkv, int Dh, const int32_t *pos, float theta,
+               const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache, void *v_cache,
+               int cache_len);
+
+/* Causal GQA attention over the fp16 caches (scores / attend,
+ * src/gpu/kernels.ts:2386-2579): query row r (position pos + r) of head h
+ * attends keys 0..pos+r of KV head h / (H / Hkv). q fp16 [rows][H][Dh]
+ * (already scaled), out fp16 [rows][H][Dh]. Dh % 8 == 0, Dh <= 256,
+ * H / Hkv <= 16. Each (row, KV head) is served by a cluster of 8 CTAs that
+ * split the keys and merge through distributed shared memory. */
+int wg_attention(wg_ctx *ctx, const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
+                 const void *v_cache, int cache_len, const int32_t *pos, void *out);
+
+/* SwiGLU (REDUCE_SWIGLU, src/gpu/kernels.ts:1066-1077): gate_up fp32
+ * [rows][2I] (gate | up) -> out[r][i] = silu(gate) * up, in out_dtype. */
+int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int out_dtype);
+
+/* LFM2 gated short convolution (shortConv / convState,
+ * src/gpu/kernels.ts:1380-1437): bcx fp32 [rows][3D] = B | C | x,
+ * y = B * x, out[t] = C[t] * sum_k weight[c][k] * y[t - (W-1-k)] (weight fp32
+ * [D][W]); y before the batch comes from state fp16 [W-1][D] (oldest first),
+ * which is updated to the batch's last W-1 values of y. W <= 8. */
+int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const float *weight, void *state,
+                  void *out, int out_dtype);
+
+/* fp16 output head (head, src/engine.ts:8557): logits fp32 [rows][V] =
+ * x fp16 [rows][D] . W^T, W fp16 [V][D]; rows <= 8, D % 8 == 0,
+ * rows * D <= 51200. */
+int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits);
+
+/* Greedy pick (src/engine.ts:8271 argmax): out[r] = index of the largest
+ * logit of row r (the lowest index on ties). */
+int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out);
+
+/* *counter += delta on the device (advances the position of a replayed
+ * decode step). */
+int wg_add_i32(wg_ctx *ctx, int32_t *counter, int delta);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WEBGLLM_DECODER_H */

@@ -102,7 +102,8 @@ int wg_q4_info(const wg_q4mat *m, int *N, int *K, size_t *device_bytes);
  * of nibbles, byte j = weight j low, weight j + 16 high; K / 32 blocks a
  * row) from host memory into rows [row0, row0 + rows) of `m`. `src_rows`
  * (nullable, `rows` entries) gives each destination row's source row, for
- * head permutations (src/repack.ts:5-6). The repack runs on the device. */
+ * head permutations (src/repack.ts:5-6). The repack runs on the device;
+ * `src` may also be device memory. */
 int wg_q4_pack_q4_0(wg_ctx *ctx, wg_q4mat *m, int row0, const uint8_t *src,
                     size_t src_len, int rows, const int32_t *src_rows);
 

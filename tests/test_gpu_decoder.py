@@ -1,0 +1,272 @@
+"""Parity of the decoder-layer kernels (include/webgllm_decoder.h) with plain
+PyTorch fp32 references of the same ops (tests/decoder_reference.py), and of
+a whole random-init decoder (webgllm_b200.model) with the reference forward.
+
+Tolerances: fp16 outputs within 2e-3 relative to the output's scale
+(fp16 rounding is 4.9e-4 relative; the rest is accumulation order);
+integer outputs (embedding copies, argmax, positions) exact.
+"""
+import math
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+import ctypes  # noqa: E402
+
+import decoder_reference as R  # noqa: E402
+import webgllm_b200 as wg  # noqa: E402
+from webgllm_b200 import _lib  # noqa: E402
+from webgllm_b200._lib import WG_F16, WG_F32  # noqa: E402
+
+P = ctypes.c_void_p
+
+
+def lib():
+    return _lib.lib()
+
+
+def ctx():
+    c = wg.context()
+    c.use_torch_stream()
+    return c
+
+
+def call(fn, *args):
+    c = ctx()
+    _lib.check(fn(P(c.handle), *args), c.handle)
+    torch.cuda.synchronize()
+
+
+def ptr(t):
+    return P(t.data_ptr()) if t is not None else P(None)
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+
+def gen(seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    return g
+
+
+# ------------------------------------------------------------------ kernels
+
+
+def test_embed_copies_rows_exactly():
+    V, D = 1000, 256
+    g = gen(1)
+    table = torch.randn((V, D), generator=g, device="cuda").half()
+    ids = torch.tensor([5, 0, 999, 5, -3, 1000], dtype=torch.int32, device="cuda")
+    out = torch.empty((ids.numel(), D), device="cuda")
+    call(lib().wg_embed, ptr(ids), ids.numel(), ptr(table), V, D, ptr(out))
+    want = table[ids.clamp(0, V - 1).long()].float()
+    want[4] = table[0].float()  # out of range reads row 0
+    want[5] = table[0].float()
+    assert torch.equal(out, want)
+
+
+@pytest.mark.parametrize("rows,D,with_add", [(1, 2048, True), (7, 1536, False), (64, 4096, True), (3, 100, True)])
+def test_rmsnorm_fused_add(rows, D, with_add):
+    g = gen(rows + D)
+    x = torch.randn((rows, D), generator=g, device="cuda")
+    add = torch.randn((rows, D), generator=g, device="cuda") if with_add else None
+    w = torch.rand(D, generator=g, device="cuda") + 0.5
+    x0 = x.clone()
+    out = torch.empty((rows, D), dtype=torch.float16, device="cuda")
+    call(lib().wg_rmsnorm, ptr(x), ptr(add), ptr(w), ctypes.c_float(1e-5), rows, D, ptr(out), WG_F16)
+    xr, want = R.rmsnorm(x0, add, w, 1e-5)
+    assert torch.allclose(x, xr, rtol=0, atol=1e-6 * xr.abs().max().item())
+    assert rel(out, want) < 2e-3
+
+
+@pytest.mark.parametrize("rows,H,Hkv,Dh,pos0,qk", [
+    (1, 32, 4, 64, 0, False), (1, 32, 4, 64, 777, False), (5, 24, 8, 64, 100, True), (3, 32, 8, 128, 4000, False),
+    (48, 8, 2, 64, 16, True),
+])
+def test_rope_kv_append(rows, H, Hkv, Dh, pos0, qk):
+    g = gen(rows * 31 + H + Dh)
+    cache_len = 4096 + 64
+    qkv = torch.randn((rows, (H + 2 * Hkv) * Dh), generator=g, device="cuda")
+    qn = torch.rand(Dh, generator=g, device="cuda") + 0.5 if qk else None
+    kn = torch.rand(Dh, generator=g, device="cuda") + 0.5 if qk else None
+    pos = torch.tensor([pos0], dtype=torch.int32, device="cuda")
+    q = torch.empty((rows, H, Dh), dtype=torch.float16, device="cuda")
+    kc = torch.zeros((Hkv, cache_len, Dh), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    call(lib().wg_rope_kv, ptr(qkv), rows, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4 if Dh == 64 else 5e5),
+         ptr(qn), ptr(kn), ctypes.c_float(1e-5), ptr(q), ptr(kc), ptr(vc), cache_len)
+    wq, wk, wv = R.rope_kv(qkv, H, Hkv, Dh, pos0, 1e4 if Dh == 64 else 5e5, qn, kn, 1e-5)
+    assert rel(q, wq) < 2e-3
+    assert rel(kc[:, pos0:pos0 + rows].transpose(0, 1), wk) < 2e-3
+    assert torch.equal(vc[:, pos0:pos0 + rows].transpose(0, 1), wv)
+    # nothing else in the caches was written
+    assert not kc[:, :pos0].any() and not kc[:, pos0 + rows:].any()
+
+
+def test_rope_kv_position_past_cache_is_reported():
+    H, Hkv, Dh, cache_len = 4, 2, 64, 16
+    qkv = torch.randn((2, (H + 2 * Hkv) * Dh), device="cuda")
+    pos = torch.tensor([15], dtype=torch.int32, device="cuda")  # row 1 lands at 16
+    q = torch.empty((2, H, Dh), dtype=torch.float16, device="cuda")
+    kc = torch.zeros((Hkv, cache_len, Dh), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    c = ctx()
+    assert lib().wg_rope_kv(P(c.handle), ptr(qkv), 2, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4), None, None,
+                            ctypes.c_float(1e-5), ptr(q), ptr(kc), ptr(vc), cache_len) == 0
+    with pytest.raises(wg.GpuError):
+        c.sync()
+    c.sync()  # the flag is cleared once reported
+    assert kc[:, 15].any()
+
+
+@pytest.mark.parametrize("rows,H,Hkv,Dh,pos0", [
+    (1, 32, 4, 64, 0), (1, 32, 4, 64, 1023), (1, 24, 8, 64, 300), (1, 32, 8, 128, 2047), (4, 16, 2, 64, 517),
+    (40, 8, 8, 64, 0), (1, 16, 1, 256, 130), (2, 6, 2, 32, 70),
+])
+def test_attention_causal_gqa(rows, H, Hkv, Dh, pos0):
+    g = gen(rows * 7 + H * 3 + pos0)
+    cache_len = 2048 + 16
+    L = pos0 + rows
+    kc = torch.zeros((Hkv, cache_len, Dh), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    kc[:, :L] = (torch.randn((Hkv, L, Dh), generator=g, device="cuda") * 2).half()
+    vc[:, :L] = torch.randn((Hkv, L, Dh), generator=g, device="cuda").half()
+    # a poisoned tail: keys past each row's position must not be read
+    kc[:, L:L + 8] = 1e4
+    vc[:, L:L + 8] = float("nan")
+    q = (torch.randn((rows, H, Dh), generator=g, device="cuda") / math.sqrt(Dh)).half()
+    pos = torch.tensor([pos0], dtype=torch.int32, device="cuda")
+    out = torch.empty((rows, H, Dh), dtype=torch.float16, device="cuda")
+    call(lib().wg_attention, ptr(q), rows, H, Hkv, Dh, ptr(kc), ptr(vc), cache_len, ptr(pos), ptr(out))
+    want = R.attention(q, kc, vc, pos0, H, Hkv)
+    assert torch.isfinite(out.float()).all()
+    assert (out.float() - want).abs().max().item() < 2e-3 * max(1.0, want.abs().max().item())
+
+
+@pytest.mark.parametrize("rows,I,dt", [(1, 5632, WG_F16), (33, 4608, WG_F16), (2, 100, WG_F32)])
+def test_swiglu(rows, I, dt):
+    gu = torch.randn((rows, 2 * I), generator=gen(I), device="cuda") * 3
+    out = torch.empty((rows, I), dtype=torch.float16 if dt == WG_F16 else torch.float32, device="cuda")
+    call(lib().wg_swiglu, ptr(gu), rows, I, ptr(out), dt)
+    assert rel(out, R.swiglu(gu, I)) < (2e-3 if dt == WG_F16 else 1e-5)
+
+
+@pytest.mark.parametrize("rows,D,W", [(1, 1536, 3), (17, 1536, 3), (5, 300, 4), (2, 64, 1)])
+def test_short_conv_and_state(rows, D, W):
+    g = gen(rows + D + W)
+    bcx = torch.randn((rows, 3 * D), generator=g, device="cuda")
+    w = torch.randn((D, W), generator=g, device="cuda") * 0.3
+    state = torch.randn((max(W - 1, 1), D), generator=g, device="cuda").half()
+    st0 = state.clone()
+    out = torch.empty((rows, D), dtype=torch.float16, device="cuda")
+    call(lib().wg_short_conv, ptr(bcx), rows, D, W, ptr(w), ptr(state), ptr(out), WG_F16)
+    want, want_state = R.short_conv(bcx, D, W, w, st0[: W - 1] if W > 1 else st0[:0])
+    assert rel(out, want) < 2e-3
+    if W > 1:
+        assert rel(state, want_state) < 1e-3
+    # a second call continues from the state: same as one call over both
+    bcx2 = torch.randn((3, 3 * D), generator=g, device="cuda")
+    out2 = torch.empty((3, D), dtype=torch.float16, device="cuda")
+    call(lib().wg_short_conv, ptr(bcx2), 3, D, W, ptr(w), ptr(state), ptr(out2), WG_F16)
+    both, _ = R.short_conv(torch.cat([bcx, bcx2]), D, W, w, st0[: W - 1] if W > 1 else st0[:0])
+    assert rel(out2, both[rows:]) < 2e-3
+
+
+@pytest.mark.parametrize("rows,D,V", [(1, 2048, 32000), (3, 1536, 65536), (8, 4096, 1000), (1, 64, 7)])
+def test_head_and_argmax(rows, D, V):
+    g = gen(rows + D + V)
+    x = torch.randn((rows, D), generator=g, device="cuda").half()
+    W = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
+    logits = torch.empty((rows, V), device="cuda")
+    call(lib().wg_head, ptr(x), rows, D, ptr(W), V, ptr(logits))
+    want = x.float() @ W.float().t()
+    assert rel(logits, want) < 1e-4
+    ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+    call(lib().wg_argmax, ptr(logits), rows, V, ptr(ids))
+    assert torch.equal(ids.long(), logits.argmax(dim=1))
+
+
+def test_argmax_picks_the_lowest_index_on_ties():
+    V = 50000
+    logits = torch.zeros((2, V), device="cuda")
+    logits[0, [7, 123, 40000]] = 5.0
+    logits[1, :] = -1.0
+    ids = torch.empty(2, dtype=torch.int32, device="cuda")
+    call(lib().wg_argmax, ptr(logits), 2, V, ptr(ids))
+    assert ids.tolist() == [7, 0]
+
+
+def test_add_i32():
+    c = torch.tensor([41], dtype=torch.int32, device="cuda")
+    call(lib().wg_add_i32, ptr(c), 1)
+    call(lib().wg_add_i32, ptr(c), -2)
+    assert c.item() == 40
+
+
+def test_decoder_shape_errors():
+    c = ctx()
+    x = torch.zeros(16, device="cuda")
+    assert lib().wg_attention(P(c.handle), ptr(x), 1, 33, 4, 64, ptr(x), ptr(x), 8, ptr(x), ptr(x)) == _lib.WG_INVALID_SHAPE
+    assert lib().wg_head(P(c.handle), ptr(x), 9, 64, ptr(x), 10, ptr(x)) == _lib.WG_INVALID_SHAPE
+    assert lib().wg_rope_kv(P(c.handle), ptr(x), 1, 4, 2, 48, ptr(x), ctypes.c_float(1e4), None, None,
+                            ctypes.c_float(1e-5), ptr(x), ptr(x), ptr(x), 8) == _lib.WG_INVALID_SHAPE
+    assert lib().wg_short_conv(P(c.handle), ptr(x), 1, 4, 9, ptr(x), ptr(x), ptr(x), WG_F16) == _lib.WG_INVALID_SHAPE
+
+
+# ------------------------------------------------------------------ a whole decoder
+
+
+def small_config(hybrid):
+    from webgllm_b200.model import DecoderConfig
+
+    if hybrid:
+        return DecoderConfig("tiny-hybrid", 4, 256, 8, 2, 64, 512, 1000, 1e-5, 1e6, ["conv", "attn", "conv", "attn"], 3,
+                             True)
+    return DecoderConfig("tiny-llama", 3, 256, 8, 2, 64, 768, 1000, 1e-5, 1e4)
+
+
+@pytest.mark.parametrize("hybrid", [False, True])
+def test_decoder_matches_reference_forward(hybrid):
+    """Prefill 40 tokens (the tcgen05 GEMM path) then 6 decode steps (the
+    GEMV path, replayed from a CUDA graph) against the torch fp32 forward:
+    logits within 2% of their scale, and the same greedy tokens wherever the
+    reference's top-2 margin is clear."""
+    from webgllm_b200.model import DecoderModel
+
+    cfg = small_config(hybrid)
+    torch.manual_seed(0)
+    m = DecoderModel(cfg, seed=3, max_ctx=128, max_rows=64, keep_blocks=True)
+    ref = R.ReferenceDecoder(m)
+    prompt = torch.randint(0, cfg.vocab, (40,), generator=gen(9), device="cuda").to(torch.int32)
+    m.prefill(prompt)
+    torch.cuda.synchronize()
+    want = ref.forward(prompt)
+    scale = want.abs().max().item()
+    assert (m.logits[0] - want).abs().max().item() < 2e-2 * scale
+    tok = m.next_id.clone()
+    m.decode_step()  # eager first step configures every kernel
+    m.capture_decode()
+    for step in range(6):
+        want_next = ref.forward(tok)
+        if step == 0:
+            pass  # the eager step above already ran this token
+        else:
+            m.graph.replay()
+        torch.cuda.synchronize()
+        got = m.logits[0]
+        s = want_next.abs().max().item()
+        assert (got - want_next).abs().max().item() < 2e-2 * s, step
+        top2 = torch.topk(want_next, 2).values
+        if (top2[0] - top2[1]).item() > 4e-2 * s:
+            assert m.next_id.item() == int(want_next.argmax().item()), step
+        # both continue from the library's token
+        tok = m.next_id.clone()
+    assert m.pos.item() == 40 + 6

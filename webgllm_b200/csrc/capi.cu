@@ -114,8 +114,9 @@ int stage(wg_ctx *ctx, std::vector<Part> &parts) {
   for (auto &p : parts) {
     p.dev = nullptr;
     if (p.host && p.bytes) {
-      WG_CUDA(ctx, cudaMemcpyAsync(ctx->staging + off, p.host, p.bytes, cudaMemcpyHostToDevice,
-                                   ctx->stream));
+      // cudaMemcpyDefault: the source may be host memory (a file's bytes) or
+      // device memory (bytes produced on the GPU).
+      WG_CUDA(ctx, cudaMemcpyAsync(ctx->staging + off, p.host, p.bytes, cudaMemcpyDefault, ctx->stream));
       p.dev = ctx->staging + off;
     }
     off += align_up(p.bytes, 256);

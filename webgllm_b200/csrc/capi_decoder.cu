@@ -1,0 +1,135 @@
+// The C ABI of include/webgllm_decoder.h: argument checks and launches.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/webgllm_decoder.h"
+#include "capi_internal.cuh"
+#include "decoder_kernels.cuh"
+
+namespace {
+
+int dfail(wg_ctx *ctx, int status, const char *fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->last_error = buf;
+  }
+  return status;
+}
+
+int finish(wg_ctx *ctx, cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return WG_OK;
+  return dfail(ctx, wg::status_of(e), "%s: %s", what, cudaGetErrorString(e));
+}
+
+int begin(wg_ctx *ctx) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  cudaError_t e = cudaSetDevice(ctx->device);
+  return e == cudaSuccess ? WG_OK : finish(ctx, e, "cudaSetDevice");
+}
+
+bool dtype_ok(int d) { return d >= WG_F32 && d <= WG_BF16; }
+
+}  // namespace
+
+#define WG_BEGIN(ctx)          \
+  do {                         \
+    int st_ = begin(ctx);      \
+    if (st_) return st_;       \
+  } while (0)
+
+extern "C" {
+
+int wg_embed(wg_ctx *ctx, const int32_t *ids, int rows, const void *table, int V, int D, float *out) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || V <= 0 || D <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_embed: bad shape");
+  if (!rows) return WG_OK;
+  if (!ids || !table || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_embed: null argument");
+  return finish(ctx, wg::launch_embed(ids, rows, table, V, D, out, ctx->stream), "wg_embed");
+}
+
+int wg_rmsnorm(wg_ctx *ctx, float *x, const float *add, const float *weight, float eps, int rows, int D,
+               void *out, int out_dtype) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || D <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_rmsnorm: bad shape");
+  if (!rows) return WG_OK;
+  if (!x || !weight || !out || !dtype_ok(out_dtype)) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_rmsnorm: argument");
+  return finish(ctx, wg::launch_rmsnorm(x, add, weight, eps, rows, D, out, out_dtype, ctx->stream), "wg_rmsnorm");
+}
+
+int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int H, int Hkv, int Dh, const int32_t *pos, float theta,
+               const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache, void *v_cache,
+               int cache_len) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh <= 0 || Dh % 64 || cache_len <= 0)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_rope_kv: bad shape (H %d, Hkv %d, Dh %d)", H, Hkv, Dh);
+  if (!rows) return WG_OK;
+  if (!qkv || !pos || !q_out || !k_cache || !v_cache) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_rope_kv: null");
+  return finish(ctx,
+                wg::launch_rope_kv(qkv, rows, H, Hkv, Dh, pos, theta, q_norm, k_norm, eps, q_out, k_cache, v_cache,
+                                   cache_len, ctx->d_flags, ctx->stream),
+                "wg_rope_kv");
+}
+
+int wg_attention(wg_ctx *ctx, const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
+                 const void *v_cache, int cache_len, const int32_t *pos, void *out) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || H <= 0 || Hkv <= 0 || H % Hkv || H / Hkv > 16 || Dh <= 0 || Dh % 8 || Dh > 256 ||
+      cache_len <= 0)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_attention: bad shape (H %d, Hkv %d, Dh %d, cache_len %d)", H, Hkv, Dh,
+                 cache_len);
+  if (!rows) return WG_OK;
+  if (!q || !k_cache || !v_cache || !pos || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_attention: null");
+  return finish(ctx, wg::launch_attention(q, rows, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->stream),
+                "wg_attention");
+}
+
+int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int out_dtype) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || I <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_swiglu: bad shape");
+  if (!rows) return WG_OK;
+  if (!gate_up || !out || !dtype_ok(out_dtype)) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_swiglu: argument");
+  return finish(ctx, wg::launch_swiglu(gate_up, rows, I, out, out_dtype, ctx->stream), "wg_swiglu");
+}
+
+int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const float *weight, void *state,
+                  void *out, int out_dtype) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || D <= 0 || W < 1 || W > 8) return dfail(ctx, WG_INVALID_SHAPE, "wg_short_conv: bad shape");
+  if (!rows) return WG_OK;
+  if (!bcx || !weight || !state || !out || !dtype_ok(out_dtype))
+    return dfail(ctx, WG_INVALID_ARGUMENT, "wg_short_conv: argument");
+  return finish(ctx, wg::launch_short_conv(bcx, rows, D, W, weight, state, out, out_dtype, ctx->stream),
+                "wg_short_conv");
+}
+
+int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || rows > 8 || D <= 0 || D % 8 || V <= 0 || (size_t)rows * D * 4 > 200 * 1024)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_head: rows %d (<= 8), D %d (multiple of 8, rows * D <= 51200)", rows,
+                 D);
+  if (!rows) return WG_OK;
+  if (!x || !W || !logits) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_head: null");
+  return finish(ctx, wg::launch_head(x, rows, D, W, V, logits, ctx->num_sms, ctx->stream), "wg_head");
+}
+
+int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || V <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_argmax: bad shape");
+  if (!rows) return WG_OK;
+  if (!logits || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_argmax: null");
+  return finish(ctx, wg::launch_argmax(logits, rows, V, out, ctx->stream), "wg_argmax");
+}
+
+int wg_add_i32(wg_ctx *ctx, int32_t *counter, int delta) {
+  WG_BEGIN(ctx);
+  if (!counter) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_add_i32: null");
+  return finish(ctx, wg::launch_add_i32(counter, delta, ctx->stream), "wg_add_i32");
+}
+
+}  // extern "C"

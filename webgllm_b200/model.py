@@ -1,0 +1,258 @@
+"""Random-init decoders of BASELINE configs 2-4 on the B200 kernels.
+
+The reference's engine runs a layer loop of matmul and non-matmul passes
+(src/engine.ts:8875-9304 forwardBatch; per layer normInput -> attend |
+convolve -> add + norm -> gate|up -> REDUCE_SWIGLU -> down -> add). This module
+runs the same structure on the library's kernels: every linear is a Q4_0
+matrix through wg_q4_matmul (decode GEMV or tcgen05 GEMM), the rest through
+include/webgllm_decoder.h. Weights are random (BASELINE: "random init"),
+quantised to Q4_0 by the llama.cpp rule on the device.
+
+A decode step is captured once as a CUDA graph and replayed: the token id
+(argmax) and the position live on the device, so no host round trip is
+needed between tokens.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from .q4 import QuantMatrix, context, newQuantMatrix, packQ4_0
+from ._lib import WG_F16, WG_F32
+
+P = ctypes.c_void_p
+
+
+@dataclass
+class DecoderConfig:
+    name: str
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    eps: float = 1e-5
+    theta: float = 1e4
+    layer_types: list = field(default_factory=list)  # "attn" | "conv"
+    conv_width: int = 3
+    qk_norm: bool = False
+
+    def __post_init__(self):
+        if not self.layer_types:
+            self.layer_types = ["attn"] * self.layers
+        assert len(self.layer_types) == self.layers
+
+
+# Llama-style 1.1B.
+CONFIG2 = DecoderConfig("llama-1.1b", 22, 2048, 32, 4, 64, 5632, 32000, 1e-5, 1e4)
+# hybrid conv/attention (LFM2-style): 10 gated short-conv
+# layers (kernel 3) and 6 GQA attention layers, placed as in LFM2-350M.
+_HYBRID = ["conv", "conv", "attn", "conv", "conv", "attn", "conv", "conv", "attn", "conv", "attn", "conv",
+           "attn", "conv", "attn", "conv"]
+CONFIG3 = DecoderConfig("hybrid-350m", 16, 1536, 24, 8, 64, 4608, 65536, 1e-5, 1e6, _HYBRID, 3, True)
+# BASELINE config 4's target model (Llama-3-8B shape).
+CONFIG4 = DecoderConfig("llama3-8b-shape", 32, 4096, 32, 8, 128, 14336, 128256, 1e-5, 5e5)
+CONFIGS = {"2": CONFIG2, "3": CONFIG3, "4": CONFIG4}
+
+
+def quantize_q4_0(w: torch.Tensor) -> torch.Tensor:
+    """Float rows [N][K] (device) -> llama.cpp Q4_0 blocks, uint8 [N*K/32*18]
+    on the device. Per 32 weights, with max the element of largest magnitude:
+    d = max / -8, q = min(15, floor(w / d + 8.5)), d stored as fp16 (round to
+    nearest even); byte j holds q[j] low and q[j+16] high."""
+    N, K = w.shape
+    b = w.float().reshape(N, K // 32, 32)
+    idx = b.abs().argmax(dim=2, keepdim=True)
+    mx = torch.gather(b, 2, idx)
+    d = mx / -8.0
+    inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+    q = torch.clamp(torch.floor(b * inv + 8.5), 0, 15).to(torch.uint8)
+    out = torch.empty((N, K // 32, 18), dtype=torch.uint8, device=w.device)
+    out[:, :, 0:2] = d.to(torch.float16).view(torch.uint8).reshape(N, K // 32, 2)
+    out[:, :, 2:] = q[:, :, :16] | (q[:, :, 16:] << 4)
+    return out.reshape(-1)
+
+
+def dequantize_q4_0(blocks: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """GGUF Q4_0 blocks -> float32 [N][K], d * (q - 8)."""
+    b = blocks.reshape(N, K // 32, 18)
+    d = b[:, :, 0:2].contiguous().view(torch.float16).float()
+    q = b[:, :, 2:]
+    w = torch.cat([(q & 15), (q >> 4)], dim=2).float() - 8.0
+    return (w * d).reshape(N, K)
+
+
+class Linear:
+    """A Q4_0 matrix on the device (and its GGUF bytes, for references)."""
+
+    def __init__(self, ctx, N: int, K: int, gen: torch.Generator, std: float = 0.02, keep_blocks=False):
+        w = torch.randn((N, K), generator=gen, device="cuda") * std
+        blocks = quantize_q4_0(w)
+        del w
+        self.N, self.K = N, K
+        self.m: QuantMatrix = newQuantMatrix(N, K, ctx=ctx)
+        ctx.use_torch_stream()
+        packQ4_0(self.m, 0, blocks, N)
+        torch.cuda.synchronize()
+        self.blocks = blocks if keep_blocks else None
+
+
+
+
+class DecoderModel:
+    """Weights, caches and the forward pass of one decoder on one GPU."""
+
+    def __init__(self, cfg: DecoderConfig, seed: int = 0, max_ctx: int = 1024, max_rows: int = 512,
+                 keep_blocks: bool = False, device: int | None = None):
+        self.cfg = cfg
+        self.ctx = context(device)
+        self.max_ctx, self.max_rows = max_ctx, max_rows
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        D, H, Hkv, Dh, I, V = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab
+        self.embed = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
+        self.head = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
+        self.final_norm = torch.ones(D, device="cuda")
+        self.layers = []
+        n_attn = n_conv = 0
+        for t in cfg.layer_types:
+            L = {"type": t, "norm1": torch.ones(D, device="cuda"), "norm2": torch.ones(D, device="cuda")}
+            if t == "attn":
+                L["qkv"] = Linear(self.ctx, (H + 2 * Hkv) * Dh, D, g, keep_blocks=keep_blocks)
+                L["o"] = Linear(self.ctx, D, H * Dh, g, keep_blocks=keep_blocks)
+                if cfg.qk_norm:
+                    L["q_norm"] = torch.ones(Dh, device="cuda")
+                    L["k_norm"] = torch.ones(Dh, device="cuda")
+                L["slot"] = n_attn
+                n_attn += 1
+            else:
+                L["in"] = Linear(self.ctx, 3 * D, D, g, keep_blocks=keep_blocks)
+                L["conv_w"] = torch.randn((D, cfg.conv_width), generator=g, device="cuda") * 0.1
+                L["out"] = Linear(self.ctx, D, D, g, keep_blocks=keep_blocks)
+                L["slot"] = n_conv
+                n_conv += 1
+            L["gu"] = Linear(self.ctx, 2 * I, D, g, keep_blocks=keep_blocks)
+            L["down"] = Linear(self.ctx, D, I, g, keep_blocks=keep_blocks)
+            self.layers.append(L)
+        self.k_cache = torch.zeros((max(n_attn, 1), Hkv, max_ctx, Dh), dtype=torch.float16, device="cuda")
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.conv_state = torch.zeros((max(n_conv, 1), cfg.conv_width - 1, D), dtype=torch.float16, device="cuda")
+        # activations for up to max_rows rows
+        R = max_rows
+        self.x = torch.zeros((R, D), device="cuda")                      # residual stream
+        self.h = torch.zeros((R, D), dtype=torch.float16, device="cuda")  # normed input of a matmul
+        self.qkv = torch.zeros((R, (H + 2 * Hkv) * Dh), device="cuda")
+        self.q = torch.zeros((R, H * Dh), dtype=torch.float16, device="cuda")
+        self.att = torch.zeros((R, H * Dh), dtype=torch.float16, device="cuda")
+        self.bcx = torch.zeros((R, 3 * D), device="cuda")
+        self.cv = torch.zeros((R, D), dtype=torch.float16, device="cuda")
+        self.o = torch.zeros((R, D), device="cuda")
+        self.gu = torch.zeros((R, 2 * I), device="cuda")
+        self.act = torch.zeros((R, I), dtype=torch.float16, device="cuda")
+        self.logits = torch.zeros((1, V), device="cuda")
+        self.pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.ids = torch.zeros(R, dtype=torch.int32, device="cuda")
+        self.next_id = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.graph = None
+
+    # -- low level ---------------------------------------------------------
+
+    def _c(self, st):
+        _lib.check(st, self.ctx.handle)
+
+    def _mm(self, lin: Linear, x: torch.Tensor, y: torch.Tensor, rows: int):
+        L = _lib.lib()
+        xd = WG_F16 if x.dtype == torch.float16 else WG_F32
+        yd = WG_F16 if y.dtype == torch.float16 else WG_F32
+        self._c(L.wg_q4_matmul(P(self.ctx.handle), P(lin.m.handle), P(x.data_ptr()), xd, rows, P(y.data_ptr()), yd))
+
+    def reset(self):
+        self.pos.zero_()
+        self.k_cache.zero_()
+        self.v_cache.zero_()
+        self.conv_state.zero_()
+
+    def forward(self, ids: torch.Tensor, rows: int):
+        """Runs `rows` tokens (device int32 ids) at the current position; leaves
+        the last row's logits in self.logits and its greedy next token in
+        self.next_id, and advances the position."""
+        cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
+        D, H, Hkv, Dh, I, V = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab
+        self.ctx.use_torch_stream()
+        self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), V, D, P(self.x.data_ptr())))
+        add = None
+        for lay in self.layers:
+            self._c(L.wg_rmsnorm(c, P(self.x.data_ptr()), P(add), P(lay["norm1"].data_ptr()), cfg.eps, rows, D,
+                                 P(self.h.data_ptr()), WG_F16))
+            if lay["type"] == "attn":
+                s = lay["slot"]
+                kc, vc = self.k_cache[s], self.v_cache[s]
+                self._mm(lay["qkv"], self.h, self.qkv, rows)
+                qn = lay.get("q_norm")
+                kn = lay.get("k_norm")
+                self._c(L.wg_rope_kv(c, P(self.qkv.data_ptr()), rows, H, Hkv, Dh, P(self.pos.data_ptr()), cfg.theta,
+                                     P(qn.data_ptr() if qn is not None else None),
+                                     P(kn.data_ptr() if kn is not None else None), cfg.eps, P(self.q.data_ptr()),
+                                     P(kc.data_ptr()), P(vc.data_ptr()), self.max_ctx))
+                self._c(L.wg_attention(c, P(self.q.data_ptr()), rows, H, Hkv, Dh, P(kc.data_ptr()), P(vc.data_ptr()),
+                                       self.max_ctx, P(self.pos.data_ptr()), P(self.att.data_ptr())))
+                self._mm(lay["o"], self.att, self.o, rows)
+            else:
+                s = lay["slot"]
+                self._mm(lay["in"], self.h, self.bcx, rows)
+                self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, D, cfg.conv_width, P(lay["conv_w"].data_ptr()),
+                                        P(self.conv_state[s].data_ptr()), P(self.cv.data_ptr()), WG_F16))
+                self._mm(lay["out"], self.cv, self.o, rows)
+            self._c(L.wg_rmsnorm(c, P(self.x.data_ptr()), P(self.o.data_ptr()), P(lay["norm2"].data_ptr()), cfg.eps,
+                                 rows, D, P(self.h.data_ptr()), WG_F16))
+            self._mm(lay["gu"], self.h, self.gu, rows)
+            self._c(L.wg_swiglu(c, P(self.gu.data_ptr()), rows, I, P(self.act.data_ptr()), WG_F16))
+            self._mm(lay["down"], self.act, self.o, rows)
+            add = self.o.data_ptr()
+        # final norm and head for the last row only
+        last = rows - 1
+        xl = self.x[last:last + 1]
+        ol = self.o[last:last + 1]
+        self._c(L.wg_rmsnorm(c, P(xl.data_ptr()), P(ol.data_ptr()), P(self.final_norm.data_ptr()), cfg.eps, 1, D,
+                             P(self.h.data_ptr()), WG_F16))
+        self._c(L.wg_head(c, P(self.h.data_ptr()), 1, D, P(self.head.data_ptr()), V, P(self.logits.data_ptr())))
+        self._c(L.wg_argmax(c, P(self.logits.data_ptr()), 1, V, P(self.next_id.data_ptr())))
+        self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), rows))
+
+    def prefill(self, prompt: torch.Tensor):
+        rows = prompt.numel()
+        assert rows <= self.max_rows
+        self.ids[:rows].copy_(prompt.to(torch.int32))
+        self.forward(self.ids, rows)
+
+    def decode_step(self):
+        """One greedy token: input = the last argmax (on the device)."""
+        self.forward(self.next_id, 1)
+
+    def capture_decode(self):
+        """Records decode_step as a CUDA graph (after one eager step, so that
+        every kernel is configured)."""
+        s = torch.cuda.current_stream()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self.decode_step()
+
+    def generate(self, prompt: torch.Tensor, n_new: int, use_graph: bool = True) -> torch.Tensor:
+        """Greedy continuation of `prompt` (device ids): returns n_new ids."""
+        out = torch.zeros(n_new, dtype=torch.int32, device="cuda")
+        self.prefill(prompt)
+        if n_new == 0:
+            return out
+        out[0:1].copy_(self.next_id)
+        for i in range(1, n_new):
+            if use_graph and self.graph is not None:
+                self.graph.replay()
+            else:
+                self.decode_step()
+            out[i:i + 1].copy_(self.next_id)
+        return out

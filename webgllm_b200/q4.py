@@ -163,9 +163,17 @@ def newQuantMatrix(N: int, K: int, bits: int = 4, withZeros: bool = False, ctx: 
 
 def packQ4_0(m: QuantMatrix, row0: int, src, rows: int, srcRows=None) -> None:
     """src/repack.ts:60-87: `rows` rows of Q4_0 blocks into rows
-    [row0, row0 + rows) of m; srcRows[i] names destination row i's source."""
-    s = _u8(src)
+    [row0, row0 + rows) of m; srcRows[i] names destination row i's source.
+    `src` is host bytes or a contiguous uint8 CUDA tensor (read in place)."""
     perm = None if srcRows is None else np.ascontiguousarray(np.asarray(srcRows, dtype=np.int32))
+    if getattr(src, "is_cuda", False):
+        if not src.is_contiguous():
+            raise GpuError(_lib.WG_INVALID_ARGUMENT, "device Q4_0 source must be contiguous")
+        nbytes = src.numel() * src.element_size()
+        m.ctx._check(_lib.lib().wg_q4_pack_q4_0(m.ctx.handle, ctypes.c_void_p(m.handle), row0,
+                                                ctypes.c_void_p(src.data_ptr()), nbytes, rows, _ptr(perm)))
+        return
+    s = _u8(src)
     m.ctx._check(_lib.lib().wg_q4_pack_q4_0(m.ctx.handle, ctypes.c_void_p(m.handle), row0, _ptr(s), s.nbytes, rows, _ptr(perm)))
 
 
