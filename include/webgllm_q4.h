@@ -65,7 +65,9 @@ int wg_init(int device, wg_ctx **out);
 /* Gpu.dispose (src/gpu/gl.ts:316). Frees the context's own buffers. */
 int wg_destroy(wg_ctx *ctx);
 /* Run the context's work on `stream` (a cudaStream_t; NULL: the context's
- * own stream). No reference counterpart: WebGL has one implicit queue. */
+ * own non-blocking stream, which is not ordered with the legacy default
+ * stream: to share that one, pass cudaStreamLegacy). No reference
+ * counterpart: WebGL has one implicit queue. */
 int wg_set_stream(wg_ctx *ctx, void *stream);
 /* Gpu.texture (src/gpu/gl.ts:263): `bytes` of device memory. */
 int wg_alloc(wg_ctx *ctx, size_t bytes, void **dptr);

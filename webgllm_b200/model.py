@@ -237,9 +237,8 @@ class DecoderModel:
     def capture_decode(self):
         """Records decode_step as a CUDA graph (after one eager step, so that
         every kernel is configured)."""
-        s = torch.cuda.current_stream()
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=s):
+        with torch.cuda.graph(self.graph):  # captures on a side stream of torch's
             self.decode_step()
 
     def generate(self, prompt: torch.Tensor, n_new: int, use_graph: bool = True) -> torch.Tensor:

@@ -59,7 +59,11 @@ class Context:
     def use_torch_stream(self) -> None:
         import torch
 
-        self._check(_lib.lib().wg_set_stream(self.handle, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        # torch's default stream is the legacy NULL stream; NULL would select
+        # the context's own (non-blocking, unordered) stream, so name the
+        # legacy stream by its handle, cudaStreamLegacy.
+        self._check(_lib.lib().wg_set_stream(self.handle, ctypes.c_void_p(s if s else _CUDA_STREAM_LEGACY)))
 
     def set_stream(self, stream: int | None) -> None:
         self._check(_lib.lib().wg_set_stream(self.handle, ctypes.c_void_p(stream or 0)))
@@ -90,6 +94,8 @@ class Context:
     def read(self, host: int, src: int, nbytes: int) -> None:
         self._check(_lib.lib().wg_read(self.handle, ctypes.c_void_p(host), ctypes.c_void_p(src), nbytes))
 
+
+_CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
 
 _contexts: dict[int, Context] = {}
 _ctx_lock = threading.Lock()
