@@ -46,7 +46,7 @@ int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int H, int Hkv, int Dh, 
 /* Causal GQA attention over the fp16 caches (scores / attend,
  * src/gpu/kernels.ts:2386-2579): query row r (position pos + r) of head h
  * attends keys 0..pos+r of KV head h / (H / Hkv). q fp16 [rows][H][Dh]
- * (already scaled), out fp16 [rows][H][Dh]. Dh % 8 == 0, Dh <= 256,
+ * (already scaled), out fp16 [rows][H][Dh]. Dh in {32, 64, 128, 256},
  * H / Hkv <= 16. Each (row, KV head) is served by a cluster of 8 CTAs that
  * split the keys and merge through distributed shared memory. */
 int wg_attention(wg_ctx *ctx, const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
@@ -66,8 +66,17 @@ int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const f
 
 /* fp16 output head (head, src/engine.ts:8557): logits fp32 [rows][V] =
  * x fp16 [rows][D] . W^T, W fp16 [V][D]; rows <= 8, D % 8 == 0,
- * rows * D <= 51200. */
-int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits);
+ * rows * D <= 51200. If `argmax` is not NULL it also receives each row's
+ * greedy token as wg_argmax would (same launch). Calls that pass `argmax`
+ * must not overlap on one context (they share its reduction buffer). */
+int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits, int32_t *argmax);
+
+/* wg_head on the final norm of the residual stream, in one launch: x =
+ * rmsnorm(resid + add) * weight (add may be NULL), rounded to fp16 as
+ * wg_rmsnorm would store it; resid and add are fp32 [rows][D] and are not
+ * written. (The engine's last addNormed before head, src/engine.ts:9304.) */
+int wg_head_rmsnorm(wg_ctx *ctx, const float *resid, const float *add, const float *weight, float eps, int rows,
+                    int D, const void *W, int V, float *logits, int32_t *argmax);
 
 /* Greedy pick (src/engine.ts:8271 argmax): out[r] = index of the largest
  * logit of row r (the lowest index on ties). */

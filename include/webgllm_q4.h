@@ -157,6 +157,34 @@ int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype,
 int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x,
                         int x_dtype, int M, void *y, int y_dtype);
 
+/* ---- matmul with its input pass fused in ------------------------------- */
+
+/* Prologue kinds of wg_q4_matmul_fused. */
+#define WG_PRO_RMSNORM 1 /* x = rmsnorm(a + b) * weight (addNormed, src/engine.ts:5695) */
+#define WG_PRO_SWIGLU 2  /* x = silu(gate) * up (REDUCE_SWIGLU, src/gpu/kernels.ts:1066) */
+
+typedef struct wg_prologue {
+  int kind;             /* WG_PRO_* */
+  const float *a;       /* RMSNORM: residual [M][K]; SWIGLU: gate | up [M][2K] */
+  const float *b;       /* RMSNORM: added to the residual [M][K], or NULL */
+  const float *weight;  /* RMSNORM: norm weight [K] */
+  float eps;            /* RMSNORM: x / sqrt(mean(x^2) + eps) */
+  float *resid_out;     /* RMSNORM: receives a + b [M][K], or NULL; must not
+                           alias a or b */
+} wg_prologue;
+
+/* y = x . W^T where x (fp16, as the reference rounds matmul inputs) is made
+ * from `pro` inside the matmul's own launch for M <= 8 rows (the decode
+ * GEMV stages x in shared memory; each CTA computes the row statistics of
+ * the norm itself): the engine's norm / SwiGLU pass and the matmul that
+ * consumes it become one kernel. More rows run the prologue as its own
+ * kernel into the context's scratch (it may allocate, as wg_q4_matmul).
+ * Tensors are device pointers, 16-byte aligned. No reference counterpart as
+ * one call: the engine runs the two passes back to back
+ * (src/engine.ts:8875-9304). */
+int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro,
+                       int M, void *y, int y_dtype);
+
 /* ---- tracing ------------------------------------------------------------- */
 
 /* Gpu.trace / drawTrace (src/gpu/gl.ts:553-598), per CTA instead of per

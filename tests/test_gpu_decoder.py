@@ -186,12 +186,19 @@ def test_head_and_argmax(rows, D, V):
     x = torch.randn((rows, D), generator=g, device="cuda").half()
     W = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
     logits = torch.empty((rows, V), device="cuda")
-    call(lib().wg_head, ptr(x), rows, D, ptr(W), V, ptr(logits))
+    fused = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+    call(lib().wg_head, ptr(x), rows, D, ptr(W), V, ptr(logits), ptr(fused))
     want = x.float() @ W.float().t()
     assert rel(logits, want) < 1e-4
     ids = torch.empty(rows, dtype=torch.int32, device="cuda")
     call(lib().wg_argmax, ptr(logits), rows, V, ptr(ids))
     assert torch.equal(ids.long(), logits.argmax(dim=1))
+    assert torch.equal(fused, ids)
+    # again (the fused pick's counter must have been reset), without argmax
+    fused.fill_(-1)
+    call(lib().wg_head, ptr(x), rows, D, ptr(W), V, ptr(logits), ptr(fused))
+    assert torch.equal(fused, ids)
+    call(lib().wg_head, ptr(x), rows, D, ptr(W), V, ptr(logits), None)
 
 
 def test_argmax_picks_the_lowest_index_on_ties():
@@ -202,6 +209,39 @@ def test_argmax_picks_the_lowest_index_on_ties():
     ids = torch.empty(2, dtype=torch.int32, device="cuda")
     call(lib().wg_argmax, ptr(logits), 2, V, ptr(ids))
     assert ids.tolist() == [7, 0]
+
+
+@pytest.mark.parametrize("rows,D,V,with_add", [(1, 2048, 32000, True), (3, 1536, 5000, False)])
+def test_head_rmsnorm_is_norm_then_head(rows, D, V, with_add):
+    g = gen(rows * D + V)
+    resid = torch.randn((rows, D), generator=g, device="cuda")
+    add = torch.randn((rows, D), generator=g, device="cuda") if with_add else None
+    w = torch.rand(D, generator=g, device="cuda") + 0.5
+    W = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
+    r0 = resid.clone()
+    logits = torch.empty((rows, V), device="cuda")
+    ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+    call(lib().wg_head_rmsnorm, ptr(resid), ptr(add), ptr(w), ctypes.c_float(1e-5), rows, D, ptr(W), V, ptr(logits),
+         ptr(ids))
+    assert torch.equal(resid, r0)  # not written
+    _, h = R.rmsnorm(r0, add, w, 1e-5)
+    want = h.half().float() @ W.float().t()
+    assert rel(logits, want) < 2e-3
+    assert torch.equal(ids.long(), logits.argmax(dim=1))
+
+
+def test_head_fused_argmax_ties_pick_the_lowest_index():
+    D, V = 64, 5000
+    x = torch.ones((1, D), dtype=torch.float16, device="cuda")
+    W = torch.zeros((V, D), dtype=torch.float16, device="cuda")
+    logits = torch.empty((1, V), device="cuda")
+    ids = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    call(lib().wg_head, ptr(x), 1, D, ptr(W), V, ptr(logits), ptr(ids))
+    assert ids.item() == 0  # all logits equal
+    W[4000] = 0.5
+    W[10] = 0.5
+    call(lib().wg_head, ptr(x), 1, D, ptr(W), V, ptr(logits), ptr(ids))
+    assert ids.item() == 10
 
 
 def test_add_i32():
@@ -215,7 +255,7 @@ def test_decoder_shape_errors():
     c = ctx()
     x = torch.zeros(16, device="cuda")
     assert lib().wg_attention(P(c.handle), ptr(x), 1, 33, 4, 64, ptr(x), ptr(x), 8, ptr(x), ptr(x)) == _lib.WG_INVALID_SHAPE
-    assert lib().wg_head(P(c.handle), ptr(x), 9, 64, ptr(x), 10, ptr(x)) == _lib.WG_INVALID_SHAPE
+    assert lib().wg_head(P(c.handle), ptr(x), 9, 64, ptr(x), 10, ptr(x), None) == _lib.WG_INVALID_SHAPE
     assert lib().wg_rope_kv(P(c.handle), ptr(x), 1, 4, 2, 48, ptr(x), ctypes.c_float(1e4), None, None,
                             ctypes.c_float(1e-5), ptr(x), ptr(x), ptr(x), 8) == _lib.WG_INVALID_SHAPE
     assert lib().wg_short_conv(P(c.handle), ptr(x), 1, 4, 9, ptr(x), ptr(x), ptr(x), WG_F16) == _lib.WG_INVALID_SHAPE
@@ -233,8 +273,9 @@ def small_config(hybrid):
     return DecoderConfig("tiny-llama", 3, 256, 8, 2, 64, 768, 1000, 1e-5, 1e4)
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("hybrid", [False, True])
-def test_decoder_matches_reference_forward(hybrid):
+def test_decoder_matches_reference_forward(hybrid, fused):
     """Prefill 40 tokens (the tcgen05 GEMM path) then 6 decode steps (the
     GEMV path, replayed from a CUDA graph) against the torch fp32 forward:
     logits within 2% of their scale, and the same greedy tokens wherever the
@@ -243,7 +284,7 @@ def test_decoder_matches_reference_forward(hybrid):
 
     cfg = small_config(hybrid)
     torch.manual_seed(0)
-    m = DecoderModel(cfg, seed=3, max_ctx=128, max_rows=64, keep_blocks=True)
+    m = DecoderModel(cfg, seed=3, max_ctx=128, max_rows=64, keep_blocks=True, fused=fused)
     ref = R.ReferenceDecoder(m)
     prompt = torch.randint(0, cfg.vocab, (40,), generator=gen(9), device="cuda").to(torch.int32)
     m.prefill(prompt)
@@ -270,3 +311,75 @@ def test_decoder_matches_reference_forward(hybrid):
         # both continue from the library's token
         tok = m.next_id.clone()
     assert m.pos.item() == 40 + 6
+
+
+# ------------------------------------------------------------------ fused matmul prologues
+
+
+def _q4(N, K, seed):
+    from webgllm_b200.model import dequantize_q4_0, quantize_q4_0
+
+    w = torch.randn((N, K), generator=gen(seed), device="cuda") * 0.02
+    blocks = quantize_q4_0(w)
+    m = wg.newQuantMatrix(N, K)
+    wg.packQ4_0(m, 0, blocks, N)
+    torch.cuda.synchronize()
+    return m, dequantize_q4_0(blocks, N, K)
+
+
+def _fused(m, pro, rows, y):
+    c = ctx()
+    _lib.check(lib().wg_q4_matmul_fused(P(c.handle), P(m.handle), ctypes.byref(pro), rows, ptr(y), WG_F32), c.handle)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("rows", [1, 3, 8, 12, 40])
+@pytest.mark.parametrize("N,K", [(3072, 2048), (2048, 5632), (512, 4096)])
+def test_matmul_fused_rmsnorm(rows, N, K):
+    """rmsnorm(a + b) * w feeds the matmul in the same launch (rows <= 8) or
+    through the standalone prologue (more rows): y within rel 1e-3 of the
+    fp32 product of the fp16-rounded normed input, resid_out == a + b."""
+    m, Wd = _q4(N, K, N + K)
+    g = gen(rows + K)
+    a = torch.randn((rows, K), generator=g, device="cuda")
+    b = torch.randn((rows, K), generator=g, device="cuda")
+    w = torch.rand(K, generator=g, device="cuda") + 0.5
+    out = torch.full((rows, K), float("nan"), device="cuda")
+    y = torch.empty((rows, N), device="cuda")
+    pro = _lib.wg_prologue(_lib.WG_PRO_RMSNORM, a.data_ptr(), b.data_ptr(), w.data_ptr(), 1e-5, out.data_ptr())
+    _fused(m, pro, rows, y)
+    assert torch.equal(out, a + b)
+    _, h = R.rmsnorm(a, b, w, 1e-5)
+    want = h.half().float() @ Wd.t()
+    assert rel(y, want) < 1e-3
+    # no addend, no residual output
+    pro = _lib.wg_prologue(_lib.WG_PRO_RMSNORM, a.data_ptr(), None, w.data_ptr(), 1e-5, None)
+    _fused(m, pro, rows, y)
+    _, h = R.rmsnorm(a, None, w, 1e-5)
+    assert rel(y, h.half().float() @ Wd.t()) < 1e-3
+
+
+@pytest.mark.parametrize("rows", [1, 8, 33])
+def test_matmul_fused_swiglu(rows):
+    N, K = 2048, 5632
+    m, Wd = _q4(N, K, 77)
+    gu = torch.randn((rows, 2 * K), generator=gen(rows), device="cuda") * 2
+    y = torch.empty((rows, N), device="cuda")
+    pro = _lib.wg_prologue(_lib.WG_PRO_SWIGLU, gu.data_ptr(), None, None, 0.0, None)
+    _fused(m, pro, rows, y)
+    want = R.swiglu(gu, K).half().float() @ Wd.t()
+    assert rel(y, want) < 1e-3
+
+
+def test_matmul_fused_rejects_aliasing_and_bad_kind():
+    m, _ = _q4(64, 256, 1)
+    a = torch.zeros((1, 256), device="cuda")
+    w = torch.ones(256, device="cuda")
+    y = torch.empty((1, 64), device="cuda")
+    c = ctx()
+    pro = _lib.wg_prologue(_lib.WG_PRO_RMSNORM, a.data_ptr(), None, w.data_ptr(), 1e-5, a.data_ptr())
+    assert lib().wg_q4_matmul_fused(P(c.handle), P(m.handle), ctypes.byref(pro), 1, ptr(y), WG_F32) == \
+        _lib.WG_INVALID_ARGUMENT
+    pro = _lib.wg_prologue(7, a.data_ptr(), None, w.data_ptr(), 1e-5, None)
+    assert lib().wg_q4_matmul_fused(P(c.handle), P(m.handle), ctypes.byref(pro), 1, ptr(y), WG_F32) == \
+        _lib.WG_INVALID_ARGUMENT

@@ -24,6 +24,13 @@ WG_UNSUPPORTED = 9
 WG_NO_DEVICE = 10
 
 WG_F32, WG_F16, WG_BF16 = 0, 1, 2
+WG_PRO_RMSNORM, WG_PRO_SWIGLU = 1, 2
+
+
+class wg_prologue(ctypes.Structure):
+    """include/webgllm_q4.h wg_prologue."""
+    _fields_ = [("kind", ctypes.c_int), ("a", ctypes.c_void_p), ("b", ctypes.c_void_p),
+                ("weight", ctypes.c_void_p), ("eps", ctypes.c_float), ("resid_out", ctypes.c_void_p)]
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -51,6 +58,7 @@ SIGNATURES = {
     "wg_q4_matrix_row": (_I, [_P, _P, _I, _P]),
     "wg_q4_matmul": (_I, [_P, _P, _P, _I, _I, _P, _I]),
     "wg_q4_matmul_static": (_I, [_P, _P, _P, _I, _I, _P, _I]),
+    "wg_q4_matmul_fused": (_I, [_P, _P, _P, _I, _P, _I]),
     "wg_trace": (_I, [_P, _P, _SZ]),
     "wg_trace_count": (_I, [_P, ctypes.POINTER(_SZ)]),
     # include/webgllm_decoder.h
@@ -60,7 +68,8 @@ SIGNATURES = {
     "wg_attention": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _I, _P, _P]),
     "wg_swiglu": (_I, [_P, _P, _I, _I, _P, _I]),
     "wg_short_conv": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _I]),
-    "wg_head": (_I, [_P, _P, _I, _I, _P, _I, _P]),
+    "wg_head": (_I, [_P, _P, _I, _I, _P, _I, _P, _P]),
+    "wg_head_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _P, _I, _P, _P]),
     "wg_argmax": (_I, [_P, _P, _I, _I, _P]),
     "wg_add_i32": (_I, [_P, _P, _I]),
     "wg_error_string": (ctypes.c_char_p, [_I]),

@@ -168,14 +168,17 @@ int wg_init(int device, wg_ctx **out) {
       (e = cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device)) !=
           cudaSuccess ||
       (e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking)) != cudaSuccess ||
-      (e = cudaMalloc(&ctx->d_flags, sizeof(unsigned))) != cudaSuccess ||
-      (e = cudaMemset(ctx->d_flags, 0, sizeof(unsigned))) != cudaSuccess) {
+      (e = cudaMalloc(&ctx->d_flags, 256)) != cudaSuccess ||
+      (e = cudaMemset(ctx->d_flags, 0, 256)) != cudaSuccess ||
+      (e = cudaMalloc(&ctx->d_reduce, wg::kReduceBytes)) != cudaSuccess) {
     st = wg::status_of(e);
+    if (ctx->d_reduce) cudaFree(ctx->d_reduce);
     if (ctx->d_flags) cudaFree(ctx->d_flags);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return st;
   }
+  ctx->d_count = ctx->d_flags + 32;  // its own 128-byte line of the flags block
   ctx->stream = ctx->own_stream;
   const char *pdl = getenv("WG_PDL");
   if (pdl && pdl[0] == '0') ctx->pdl = false;
@@ -192,6 +195,7 @@ int wg_destroy(wg_ctx *ctx) {
   if (ctx->staging) cudaFree(ctx->staging);
   if (ctx->work) cudaFree(ctx->work);
   if (ctx->d_flags) cudaFree(ctx->d_flags);
+  if (ctx->d_reduce) cudaFree(ctx->d_reduce);
   if (ctx->d_trace_next) cudaFree(ctx->d_trace_next);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
@@ -430,21 +434,17 @@ int wg_q4_matrix_row(wg_ctx *ctx, const wg_q4mat *m, int n, float *out) {
   return WG_OK;
 }
 
-int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y,
-                 int y_dtype) {
-  if (!ctx || !m) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul: null argument");
-  if (M < 0) return fail(ctx, WG_INVALID_ARGUMENT, "negative row count %d", M);
-  if (M == 0) return WG_OK;
-  if (!x || !y) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul: null x or y");
-  if (x_dtype < WG_F32 || x_dtype > WG_BF16 || y_dtype < WG_F32 || y_dtype > WG_BF16)
-    return fail(ctx, WG_INVALID_ARGUMENT, "unknown dtype (x %d, y %d)", x_dtype, y_dtype);
-  if (!aligned16(x) || !aligned16(y))
-    return fail(ctx, WG_INVALID_ARGUMENT, "x and y must be 16-byte aligned");
-  if (m->device != ctx->device)
-    return fail(ctx, WG_INVALID_ARGUMENT, "matrix lives on device %d, context on %d", m->device,
-                ctx->device);
+}  // extern "C"
+
+namespace {
+
+// The matmul behind wg_q4_matmul and wg_q4_matmul_fused: y = x . W^T, with
+// x given (pro == null) or made by a prologue. Arguments are checked.
+int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y, int y_dtype,
+               const wg::Prologue *pro) {
   int st = use_device(ctx);
   if (st) return st;
+  const size_t K = m->d.K;
   // Many rows: the tcgen05 GEMM (src/engine.ts:4684: more rows than the
   // split path takes go to the prompt matmul).
   if (M > wg::kGemvMaxTokens && wg::gemm_supported()) {
@@ -461,17 +461,29 @@ int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int
     g.y_dtype = y_dtype;
     g.flags = ctx->d_flags;
     const size_t ws_bytes = wg::plan_gemm(g, ctx->num_sms);
-    const size_t xh_bytes = x_dtype == WG_F16 ? 0 : align_up((size_t)M * m->d.K * 2, 256);
+    const size_t xh_bytes = (x_dtype == WG_F16 && !pro) ? 0 : align_up((size_t)M * K * 2, 256);
     st = ensure_work(ctx, xh_bytes + ws_bytes);
     if (st) return st;
     const void *xh = x;
-    if (x_dtype != WG_F16) {
-      WG_CUDA(ctx, wg::launch_to_f16(x, x_dtype, ctx->work, (size_t)M * m->d.K, ctx->stream));
+    if (pro) {
+      WG_CUDA(ctx, wg::launch_prologue(*pro, M, (int)K, ctx->work, ctx->stream));
+      xh = ctx->work;
+    } else if (x_dtype != WG_F16) {
+      WG_CUDA(ctx, wg::launch_to_f16(x, x_dtype, ctx->work, (size_t)M * K, ctx->stream));
       xh = ctx->work;
     }
     g.ws = ws_bytes ? reinterpret_cast<float *>(ctx->work + xh_bytes) : nullptr;
     WG_CUDA(ctx, wg::launch_gemm(g, xh, ctx->stream));
     return WG_OK;
+  }
+  // A prologue over more rows than one fused GEMV takes runs on its own.
+  if (pro && M > wg::kProMaxTokens) {
+    st = ensure_work(ctx, (size_t)M * K * 2);
+    if (st) return st;
+    WG_CUDA(ctx, wg::launch_prologue(*pro, M, (int)K, ctx->work, ctx->stream));
+    x = ctx->work;
+    x_dtype = WG_F16;
+    pro = nullptr;
   }
   const size_t xsz = x_dtype == WG_F32 ? 4 : 2, ysz = y_dtype == WG_F32 ? 4 : 2;
   // Rows beyond one GEMV launch go in chunks (only where the GEMM is
@@ -482,14 +494,14 @@ int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int
     a.nib = m->nib;
     a.scl = m->scl;
     a.zro = m->zro;
-    a.x = reinterpret_cast<const uint8_t *>(x) + (size_t)m0 * m->d.K * xsz;
+    a.x = pro ? nullptr : reinterpret_cast<const uint8_t *>(x) + (size_t)m0 * K * xsz;
     a.y = reinterpret_cast<uint8_t *>(y) + (size_t)m0 * m->d.N * ysz;
     a.M = mc;
     a.N = m->d.N;
     a.K = m->d.K;
     a.NT = m->d.NT;
     a.KT = m->d.KT;
-    a.x_dtype = x_dtype;
+    a.x_dtype = pro ? WG_F16 : x_dtype;
     a.y_dtype = y_dtype;
     a.flags = ctx->d_flags;
     a.trace = ctx->trace;
@@ -497,11 +509,65 @@ int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int
     a.trace_cap = ctx->trace_cap;
     a.launch_index = ctx->launch_index++;
     a.trigger_at = ctx->trigger_at;
+    if (pro) a.pro = *pro;  // M <= kProMaxTokens: one launch
     if (!wg::plan_gemv(a, ctx->num_sms))
       return fail(ctx, WG_UNSUPPORTED, "K = %d is beyond the GEMV's largest cluster split", m->d.K);
     WG_CUDA(ctx, wg::launch_gemv(a, ctx->stream, ctx->pdl));
   }
   return WG_OK;
+}
+
+int check_matmul(wg_ctx *ctx, const wg_q4mat *m, int M, const void *y, int y_dtype) {
+  if (M < 0) return fail(ctx, WG_INVALID_ARGUMENT, "negative row count %d", M);
+  if (!y && M) return fail(ctx, WG_INVALID_ARGUMENT, "null y");
+  if (y_dtype < WG_F32 || y_dtype > WG_BF16) return fail(ctx, WG_INVALID_ARGUMENT, "unknown y dtype %d", y_dtype);
+  if (!aligned16(y)) return fail(ctx, WG_INVALID_ARGUMENT, "x and y must be 16-byte aligned");
+  if (m->device != ctx->device)
+    return fail(ctx, WG_INVALID_ARGUMENT, "matrix lives on device %d, context on %d", m->device, ctx->device);
+  return WG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y,
+                 int y_dtype) {
+  if (!ctx || !m) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul: null argument");
+  if (M < 0) return fail(ctx, WG_INVALID_ARGUMENT, "negative row count %d", M);
+  if (M == 0) return WG_OK;
+  if (!x || !y) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul: null x or y");
+  if (x_dtype < WG_F32 || x_dtype > WG_BF16 || y_dtype < WG_F32 || y_dtype > WG_BF16)
+    return fail(ctx, WG_INVALID_ARGUMENT, "unknown dtype (x %d, y %d)", x_dtype, y_dtype);
+  if (!aligned16(x) || !aligned16(y))
+    return fail(ctx, WG_INVALID_ARGUMENT, "x and y must be 16-byte aligned");
+  int st = check_matmul(ctx, m, M, y, y_dtype);
+  if (st) return st;
+  return run_matmul(ctx, m, x, x_dtype, M, y, y_dtype, nullptr);
+}
+
+int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, int M, void *y, int y_dtype) {
+  if (!ctx || !m || !pro) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_fused: null argument");
+  int st = check_matmul(ctx, m, M, y, y_dtype);
+  if (st) return st;
+  if (M == 0) return WG_OK;
+  wg::Prologue p{};
+  p.kind = pro->kind;
+  p.a = pro->a;
+  p.b = pro->b;
+  p.w = pro->weight;
+  p.eps = pro->eps;
+  p.out = pro->resid_out;
+  if (p.kind != WG_PRO_RMSNORM && p.kind != WG_PRO_SWIGLU)
+    return fail(ctx, WG_INVALID_ARGUMENT, "unknown prologue kind %d", p.kind);
+  if (!p.a || (p.kind == WG_PRO_RMSNORM && !p.w))
+    return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_fused: null prologue input");
+  if (!aligned16(p.a) || !aligned16(p.b) || !aligned16(p.w) || !aligned16(p.out))
+    return fail(ctx, WG_INVALID_ARGUMENT, "prologue tensors must be 16-byte aligned");
+  if (p.out && (p.out == p.a || (p.b && p.out == p.b)))
+    return fail(ctx, WG_INVALID_ARGUMENT, "resid_out must not alias the residual or the addend");
+  if (p.kind == WG_PRO_SWIGLU) p.b = nullptr, p.w = nullptr, p.out = nullptr;
+  return run_matmul(ctx, m, nullptr, WG_F16, M, y, y_dtype, &p);
 }
 
 int wg_trace(wg_ctx *ctx, void *buf, size_t bytes) {

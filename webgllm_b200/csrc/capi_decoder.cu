@@ -50,7 +50,7 @@ int wg_embed(wg_ctx *ctx, const int32_t *ids, int rows, const void *table, int V
   if (rows < 0 || V <= 0 || D <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_embed: bad shape");
   if (!rows) return WG_OK;
   if (!ids || !table || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_embed: null argument");
-  return finish(ctx, wg::launch_embed(ids, rows, table, V, D, out, ctx->stream), "wg_embed");
+  return finish(ctx, wg::launch_embed(ids, rows, table, V, D, out, ctx->stream, ctx->pdl), "wg_embed");
 }
 
 int wg_rmsnorm(wg_ctx *ctx, float *x, const float *add, const float *weight, float eps, int rows, int D,
@@ -59,7 +59,7 @@ int wg_rmsnorm(wg_ctx *ctx, float *x, const float *add, const float *weight, flo
   if (rows < 0 || D <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_rmsnorm: bad shape");
   if (!rows) return WG_OK;
   if (!x || !weight || !out || !dtype_ok(out_dtype)) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_rmsnorm: argument");
-  return finish(ctx, wg::launch_rmsnorm(x, add, weight, eps, rows, D, out, out_dtype, ctx->stream), "wg_rmsnorm");
+  return finish(ctx, wg::launch_rmsnorm(x, add, weight, eps, rows, D, out, out_dtype, ctx->stream, ctx->pdl), "wg_rmsnorm");
 }
 
 int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int H, int Hkv, int Dh, const int32_t *pos, float theta,
@@ -72,20 +72,20 @@ int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int H, int Hkv, int Dh, 
   if (!qkv || !pos || !q_out || !k_cache || !v_cache) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_rope_kv: null");
   return finish(ctx,
                 wg::launch_rope_kv(qkv, rows, H, Hkv, Dh, pos, theta, q_norm, k_norm, eps, q_out, k_cache, v_cache,
-                                   cache_len, ctx->d_flags, ctx->stream),
+                                   cache_len, ctx->d_flags, ctx->stream, ctx->pdl),
                 "wg_rope_kv");
 }
 
 int wg_attention(wg_ctx *ctx, const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
                  const void *v_cache, int cache_len, const int32_t *pos, void *out) {
   WG_BEGIN(ctx);
-  if (rows < 0 || H <= 0 || Hkv <= 0 || H % Hkv || H / Hkv > 16 || Dh <= 0 || Dh % 8 || Dh > 256 ||
-      cache_len <= 0)
+  if (rows < 0 || H <= 0 || Hkv <= 0 || H % Hkv || H / Hkv > 16 ||
+      !(Dh == 32 || Dh == 64 || Dh == 128 || Dh == 256) || cache_len <= 0)
     return dfail(ctx, WG_INVALID_SHAPE, "wg_attention: bad shape (H %d, Hkv %d, Dh %d, cache_len %d)", H, Hkv, Dh,
                  cache_len);
   if (!rows) return WG_OK;
   if (!q || !k_cache || !v_cache || !pos || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_attention: null");
-  return finish(ctx, wg::launch_attention(q, rows, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->stream),
+  return finish(ctx, wg::launch_attention(q, rows, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->stream, ctx->pdl),
                 "wg_attention");
 }
 
@@ -94,7 +94,7 @@ int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int
   if (rows < 0 || I <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_swiglu: bad shape");
   if (!rows) return WG_OK;
   if (!gate_up || !out || !dtype_ok(out_dtype)) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_swiglu: argument");
-  return finish(ctx, wg::launch_swiglu(gate_up, rows, I, out, out_dtype, ctx->stream), "wg_swiglu");
+  return finish(ctx, wg::launch_swiglu(gate_up, rows, I, out, out_dtype, ctx->stream, ctx->pdl), "wg_swiglu");
 }
 
 int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const float *weight, void *state,
@@ -104,18 +104,35 @@ int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const f
   if (!rows) return WG_OK;
   if (!bcx || !weight || !state || !out || !dtype_ok(out_dtype))
     return dfail(ctx, WG_INVALID_ARGUMENT, "wg_short_conv: argument");
-  return finish(ctx, wg::launch_short_conv(bcx, rows, D, W, weight, state, out, out_dtype, ctx->stream),
+  return finish(ctx, wg::launch_short_conv(bcx, rows, D, W, weight, state, out, out_dtype, ctx->stream, ctx->pdl),
                 "wg_short_conv");
 }
 
-int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits) {
+int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits, int32_t *argmax) {
   WG_BEGIN(ctx);
   if (rows < 0 || rows > 8 || D <= 0 || D % 8 || V <= 0 || (size_t)rows * D * 4 > 200 * 1024)
     return dfail(ctx, WG_INVALID_SHAPE, "wg_head: rows %d (<= 8), D %d (multiple of 8, rows * D <= 51200)", rows,
                  D);
   if (!rows) return WG_OK;
   if (!x || !W || !logits) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_head: null");
-  return finish(ctx, wg::launch_head(x, rows, D, W, V, logits, ctx->num_sms, ctx->stream), "wg_head");
+  return finish(ctx,
+                wg::launch_head(x, nullptr, nullptr, nullptr, 0.0f, rows, D, W, V, logits, argmax, ctx->d_reduce,
+                                wg::kReduceBytes, ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
+                "wg_head");
+}
+
+int wg_head_rmsnorm(wg_ctx *ctx, const float *resid, const float *add, const float *weight, float eps, int rows,
+                    int D, const void *W, int V, float *logits, int32_t *argmax) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || rows > 8 || D <= 0 || D % 8 || V <= 0 || (size_t)rows * D * 4 > 200 * 1024)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_head_rmsnorm: rows %d (<= 8), D %d (multiple of 8, rows * D <= 51200)",
+                 rows, D);
+  if (!rows) return WG_OK;
+  if (!resid || !weight || !W || !logits) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_head_rmsnorm: null");
+  return finish(ctx,
+                wg::launch_head(nullptr, resid, add, weight, eps, rows, D, W, V, logits, argmax, ctx->d_reduce,
+                                wg::kReduceBytes, ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
+                "wg_head_rmsnorm");
 }
 
 int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out) {
@@ -123,13 +140,13 @@ int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out) {
   if (rows < 0 || V <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_argmax: bad shape");
   if (!rows) return WG_OK;
   if (!logits || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_argmax: null");
-  return finish(ctx, wg::launch_argmax(logits, rows, V, out, ctx->stream), "wg_argmax");
+  return finish(ctx, wg::launch_argmax(logits, rows, V, out, ctx->stream, ctx->pdl), "wg_argmax");
 }
 
 int wg_add_i32(wg_ctx *ctx, int32_t *counter, int delta) {
   WG_BEGIN(ctx);
   if (!counter) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_add_i32: null");
-  return finish(ctx, wg::launch_add_i32(counter, delta, ctx->stream), "wg_add_i32");
+  return finish(ctx, wg::launch_add_i32(counter, delta, ctx->stream, ctx->pdl), "wg_add_i32");
 }
 
 }  // extern "C"

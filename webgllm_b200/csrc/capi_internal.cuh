@@ -9,12 +9,18 @@
 #include "common.cuh"
 #include "q4_layout.cuh"
 
+namespace wg {
+constexpr size_t kReduceBytes = 64 * 1024;
+}
+
 struct wg_ctx {
   int device = 0;
   int num_sms = wg::kB200Sms;
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
   unsigned *d_flags = nullptr;  // device error flags (kFlag*)
+  unsigned *d_count = nullptr;  // last-CTA counter of wg_head's argmax (rests at 0)
+  unsigned long long *d_reduce = nullptr;  // wg_head's per-CTA argmax keys (kReduceBytes)
   uint8_t *staging = nullptr;   // device copy of a repack's source bytes
   size_t staging_bytes = 0;
   uint8_t *work = nullptr;      // matmul scratch: fp16 copy of x, split-K sums

@@ -41,6 +41,8 @@ __device__ float block_sum(float v, float *red) {
 // ---- embedding (src/gpu/kernels.ts:1092, embed pass engine.ts:8961) ------
 
 __global__ void embed_kernel(const int32_t *ids, int rows, const __half *table, int V, int D, float *out) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
   const int r = blockIdx.x;
   int id = ids[r];
   if (id < 0 || id >= V) id = 0;
@@ -53,6 +55,8 @@ __global__ void embed_kernel(const int32_t *ids, int rows, const __half *table, 
 
 __global__ void rmsnorm_kernel(float *x, const float *add, const float *w, float eps, int D, void *out,
                                int out_dtype) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
   __shared__ float red[32];
   const int r = blockIdx.x;
   float *xr = x + (size_t)r * D;
@@ -78,6 +82,8 @@ __global__ void rmsnorm_kernel(float *x, const float *add, const float *w, float
 __global__ void rope_kv_kernel(const float *qkv, int H, int Hkv, int Dh, const int *pos0, float theta,
                                const float *q_norm, const float *k_norm, float eps, __half *q_out,
                                __half *k_cache, __half *v_cache, int cache_len, unsigned *flags) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
   __shared__ float red[32];
   const int r = blockIdx.x, h = blockIdx.y;  // h < H: query head; else kv head h - H
   const int half = Dh / 2, j = threadIdx.x;
@@ -121,23 +127,30 @@ __global__ void rope_kv_kernel(const float *qkv, int H, int Hkv, int Dh, const i
 // Split-K ("flash decoding") over a thread-block cluster: the cluster of
 // kAttnCluster CTAs serves one (query row, KV head) pair and every query
 // head of its group; CTA c takes the c-th slice of the row's keys 0..pos.
-// Per slice, 64-key tiles of K and V are staged in shared memory (16-byte
-// loads, K rows padded by 16 bytes so that a warp's row-strided reads hit
-// distinct banks), scores for all G = H / Hkv heads are formed from shared
-// memory, and an online softmax keeps (max, sum, acc) per head. The slices
-// are merged through distributed shared memory: CTA c finishes outputs c,
-// c + C, ... of the group's G * Dh. No global scratch, so one launch per
-// step and nothing to allocate.
+// Per slice, tiles of 128 keys (64 for Dh = 256) of K and V are staged in shared memory with
+// cp.async (all copies in flight at once; K rows padded by 16 bytes so that
+// row-strided reads hit distinct banks). Scores: one thread per (head, key).
+// An online softmax keeps (max, sum, acc) per head. P.V: warp w takes the
+// w-th quarter of the tile's keys, lane l the head dims l*DPL .. +DPL-1,
+// and each V element it loads serves four heads at once; the warps' sums
+// meet in shared memory. The slices are merged through distributed shared
+// memory: CTA c finishes outputs c*128 + i (mod 8*128) of the group's
+// G * Dh. No global scratch: one launch per step and nothing to allocate.
 
 constexpr int kAttnCluster = 8;
 constexpr int kAttnThreads = 128;
-constexpr int kAttnTile = 64;
+constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxGroup = 16;
+constexpr int kAttnHeadChunk = 4;
+
+// Keys per tile: 128 (one tile covers a decode step's slice up to 1024
+// positions) while shared memory allows, 64 for Dh = 256.
+__host__ __device__ constexpr int attn_tile(int Dh) { return Dh <= 128 ? 128 : 64; }
 
 struct AttnSmem {
-  int Dh, G;
-  size_t q, k, v, p, corr, m, l, acc, total;  // byte offsets
-  __host__ __device__ AttnSmem(int Dh_, int G_) : Dh(Dh_), G(G_) {
+  size_t q, k, v, p, corr, m, l, acc, red, total;  // byte offsets
+  __host__ __device__ AttnSmem(int Dh, int G) {
+    const int kAttnTile = attn_tile(Dh);
     size_t o = 0;
     q = o;
     o += (size_t)G * Dh * 4;
@@ -155,6 +168,8 @@ struct AttnSmem {
     o += (size_t)G * 4;
     acc = o;
     o += (size_t)G * Dh * 4;
+    red = o;
+    o += (size_t)kAttnWarps * G * Dh * 4;
     total = o;
   }
 };
@@ -170,9 +185,43 @@ __device__ __forceinline__ float dot8(uint4 k, const float *q) {
   return s;
 }
 
+// DPL consecutive halves from shared memory as floats.
+template <int DPL>
+__device__ __forceinline__ void load_halves(const __half *p, float v[DPL]) {
+  if constexpr (DPL == 1) {
+    v[0] = __half2float(*p);
+  } else if constexpr (DPL == 2) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(p));
+    v[0] = f.x;
+    v[1] = f.y;
+  } else if constexpr (DPL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4 *>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <int DPL>  // head dims per lane: Dh = 32 * DPL
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThreads)
-    attention_kernel(const __half *q, int H, int Hkv, int Dh, const __half *k_cache, const __half *v_cache,
-                     int cache_len, const int *pos0, __half *out) {
+    attention_kernel(const __half *q, int H, int Hkv, const __half *k_cache, const __half *v_cache, int cache_len,
+                     const int *pos0, __half *out) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
+  constexpr int Dh = 32 * DPL;
+  constexpr int kAttnTile = attn_tile(Dh);
+  constexpr int kPerLane = kAttnTile / 32;  // scores per lane in the softmax
+  constexpr int vecs = Dh / 8;  // 16-byte vectors per key row
+  constexpr int kstride = Dh + 8;
   extern __shared__ __align__(16) unsigned char smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int G = H / Hkv;
@@ -185,10 +234,11 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
   float *sm = reinterpret_cast<float *>(smem + lay.m);
   float *sl = reinterpret_cast<float *>(smem + lay.l);
   float *sacc = reinterpret_cast<float *>(smem + lay.acc);
+  float *sred = reinterpret_cast<float *>(smem + lay.red);
 
   const int c = (int)cluster.block_rank();
   const int hk = blockIdx.y, r = blockIdx.z;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = max(0, min(*pos0 + r + 1, cache_len));
   const int per = (L + kAttnCluster - 1) / kAttnCluster;
   const int t0 = min(L, c * per), t1 = min(L, t0 + per);
@@ -204,43 +254,54 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
 
   const __half *kb = k_cache + (size_t)hk * cache_len * Dh;
   const __half *vb = v_cache + (size_t)hk * cache_len * Dh;
-  const int vecs = Dh / 8;  // 16-byte vectors per key row
-  const int kstride = Dh + 8;
   for (int tt = t0; tt < t1; tt += kAttnTile) {
     const int nt = min(kAttnTile, t1 - tt);
     __syncthreads();  // previous tile fully consumed
-    for (int i = tid; i < nt * vecs; i += kAttnThreads) {
+    for (int i = tid; i < nt * vecs; i += kAttnThreads) {  // every copy in flight at once
       const int t = i / vecs, e = i - t * vecs;
-      const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(kb + (size_t)(tt + t) * Dh) + e);
-      const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(vb + (size_t)(tt + t) * Dh) + e);
-      *reinterpret_cast<uint4 *>(sk + t * kstride + e * 8) = kv;
-      *reinterpret_cast<uint4 *>(sv + t * Dh + e * 8) = vv;
+      cp_async16(sk + t * kstride + e * 8, kb + (size_t)(tt + t) * Dh + e * 8);
+      cp_async16(sv + t * Dh + e * 8, vb + (size_t)(tt + t) * Dh + e * 8);
     }
+    cp_async_wait_all();
     __syncthreads();
-    // scores: entry i = g * 64 + t
+    // scores: entry i = g * tile + t (a warp shares g: q reads broadcast)
     for (int i = tid; i < G * kAttnTile; i += kAttnThreads) {
       const int g = i / kAttnTile, t = i - g * kAttnTile;
-      float s = -INFINITY;
+      float sc = -INFINITY;
       if (t < nt) {
-        s = 0.0f;
         const uint4 *kr = reinterpret_cast<const uint4 *>(sk + t * kstride);
         const float *qr = sq + g * Dh;
-        for (int e = 0; e < vecs; e++) s += dot8(kr[e], qr + e * 8);
+        float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+        for (int e = 0; e < vecs; e += 2) {
+          a0 += dot8(kr[e], qr + e * 8);
+          if (e + 1 < vecs) a1 += dot8(kr[e + 1], qr + e * 8 + 8);
+        }
+        sc = a0 + a1;
       }
-      sp[i] = s;
+      sp[i] = sc;
     }
     __syncthreads();
     // per head: new max, rescale factor, probabilities (one warp per head)
-    for (int g = tid >> 5; g < G; g += kAttnThreads / 32) {
-      const int lane = tid & 31;
-      float mx = fmaxf(sp[g * kAttnTile + lane], sp[g * kAttnTile + lane + 32]);
+    for (int g = warp; g < G; g += kAttnWarps) {
+      float *pg = sp + g * kAttnTile;
+      float sv_[kPerLane];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kPerLane; j++) {
+        sv_[j] = pg[lane + 32 * j];
+        mx = fmaxf(mx, sv_[j]);
+      }
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float mold = sm[g], mnew = fmaxf(mold, mx);
-      const float p0 = expf(sp[g * kAttnTile + lane] - mnew), p1 = expf(sp[g * kAttnTile + lane + 32] - mnew);
-      sp[g * kAttnTile + lane] = p0;
-      sp[g * kAttnTile + lane + 32] = p1;
-      const float ps = warp_sum(p0 + p1);
-      __syncwarp();
+      float psum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kPerLane; j++) {
+        const float pj = expf(sv_[j] - mnew);
+        pg[lane + 32 * j] = pj;
+        psum += pj;
+      }
+      const float ps = warp_sum(psum);
       if (lane == 0) {
         const float corr = mold == -INFINITY ? 0.0f : expf(mold - mnew);
         sl[g] = sl[g] * corr + ps;
@@ -249,31 +310,59 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
       }
     }
     __syncthreads();
-    // acc[g][d] = acc * corr + sum_t p[g][t] v[t][d]; thread owns entries tid, tid + 128, ...
+    // P.V for this warp's quarter of the keys, four heads per pass over V
+    {
+      const int kw0 = warp * (kAttnTile / kAttnWarps);
+      const int kw1 = min(nt, kw0 + kAttnTile / kAttnWarps);
+      for (int g0 = 0; g0 < G; g0 += kAttnHeadChunk) {
+        float a[kAttnHeadChunk][DPL];
+#pragma unroll
+        for (int gg = 0; gg < kAttnHeadChunk; gg++)
+#pragma unroll
+          for (int d = 0; d < DPL; d++) a[gg][d] = 0.0f;
+        for (int t = kw0; t < kw1; t++) {
+          float v[DPL];
+          load_halves<DPL>(sv + t * Dh + lane * DPL, v);
+#pragma unroll
+          for (int gg = 0; gg < kAttnHeadChunk; gg++) {
+            const float pr = g0 + gg < G ? sp[(g0 + gg) * kAttnTile + t] : 0.0f;
+#pragma unroll
+            for (int d = 0; d < DPL; d++) a[gg][d] += pr * v[d];
+          }
+        }
+#pragma unroll
+        for (int gg = 0; gg < kAttnHeadChunk; gg++)
+          if (g0 + gg < G) {
+#pragma unroll
+            for (int d = 0; d < DPL; d++) sred[((size_t)warp * G + g0 + gg) * Dh + lane * DPL + d] = a[gg][d];
+          }
+      }
+    }
+    __syncthreads();
     for (int i = tid; i < G * Dh; i += kAttnThreads) {
-      const int g = i / Dh, d = i - g * Dh;
-      const float *pg = sp + g * kAttnTile;
-      float a = 0.0f;
-      for (int t = 0; t < nt; t++) a += pg[t] * __half2float(sv[t * Dh + d]);
-      sacc[i] = sacc[i] * scorr[g] + a;
+      const int g = i / Dh;
+      float s = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; w++) s += sred[(size_t)w * G * Dh + i];
+      sacc[i] = sacc[i] * scorr[g] + s;
     }
   }
   cluster.sync();
-  // merge the slices: this CTA finishes outputs c, c + C, ... (in units of
-  // 128-entry chunks, so each thread finishes whole entries)
+  // merge the slices: this CTA finishes outputs c * 128 + tid, + 8 * 128, ...
   for (int i = c * kAttnThreads + tid; i < G * Dh; i += kAttnCluster * kAttnThreads) {
     const int g = i / Dh;
+    float mj[kAttnCluster];
     float M = -INFINITY;
+#pragma unroll
     for (int j = 0; j < kAttnCluster; j++) {
-      const float *rm = cluster.map_shared_rank(sm, j);
-      M = fmaxf(M, rm[g]);
+      mj[j] = cluster.map_shared_rank(sm, j)[g];
+      M = fmaxf(M, mj[j]);
     }
     float lsum = 0.0f, a = 0.0f;
     if (M != -INFINITY) {
+#pragma unroll
       for (int j = 0; j < kAttnCluster; j++) {
-        const float mj = cluster.map_shared_rank(sm, j)[g];
-        if (mj == -INFINITY) continue;
-        const float w = expf(mj - M);
+        const float w = mj[j] == -INFINITY ? 0.0f : expf(mj[j] - M);
         lsum += cluster.map_shared_rank(sl, j)[g] * w;
         a += cluster.map_shared_rank(sacc, j)[i] * w;
       }
@@ -286,6 +375,8 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
 // ---- SwiGLU (REDUCE_SWIGLU kernels.ts:1066-1077) ---------------------------
 
 __global__ void swiglu_kernel(const float *gu, int rows, int I, void *out, int out_dtype) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
   const size_t n = (size_t)rows * I;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / I, c = i - r * I;
@@ -296,77 +387,222 @@ __global__ void swiglu_kernel(const float *gu, int rows, int I, void *out, int o
 
 // ---- gated short conv (shortConv / convState kernels.ts:1380-1437) --------
 // bcx [rows][3D] = B | C | x; y_t = B_t x_t; out_t = C_t * sum_k w[c][k]
-// y_{t - (W-1-k)}; y before the batch from the fp16 state [W-1][D] (oldest
-// first), which then holds the batch's last W-1 values of y.
+// y_{t - (W-1-k)}; y before the batch comes from the fp16 state [W-1][D]
+// (oldest first), which then holds the batch's last W-1 values of y.
+// Every output is independent, so the grid covers (channel block, row
+// block); each thread takes one channel over kConvRows rows, loading all of
+// them before use. Only the threads of row block 0 touch the state: they
+// read the old state first and write the new one last (recomputing the
+// batch's last W-1 values of y from bcx), so no other thread races with
+// them, and blocks > 0 only look back into bcx (kConvRows >= W - 1).
 
 constexpr int kMaxConvWidth = 8;
+constexpr int kConvRows = 16;
 
 __global__ void short_conv_kernel(const float *bcx, int rows, int D, int W, const float *w, __half *state,
                                   void *out, int out_dtype) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= D) return;
-  float hist[kMaxConvWidth];  // hist[i]: y_{t - (W-1) + i} for the taps before t
-  for (int i = 0; i < W - 1; i++) hist[i] = __half2float(state[(size_t)i * D + c]);
-  float wk[kMaxConvWidth];
-  for (int k = 0; k < W; k++) wk[k] = w[(size_t)c * W + k];
-  for (int t = 0; t < rows; t++) {
-    const float *row = bcx + (size_t)t * 3 * D;
-    const float y = row[c] * row[2 * D + c];
-    float a = wk[W - 1] * y;
-    for (int k = 0; k < W - 1; k++) a += wk[k] * hist[k];
-    store_out(out, out_dtype, (size_t)t * D + c, row[D + c] * a);
-    for (int k = 0; k < W - 2; k++) hist[k] = hist[k + 1];
-    if (W > 1) hist[W - 2] = y;
+  const int r0 = blockIdx.y * kConvRows;
+  const int nr = min(kConvRows, rows - r0);
+  // y over rows r0 - (W-1) .. r0 + nr - 1
+  float y[kConvRows + kMaxConvWidth - 1];
+  float cg_[kConvRows];
+#pragma unroll
+  for (int i = 0; i < kConvRows + kMaxConvWidth - 1; i++) {
+    const int t = r0 - (W - 1) + i;
+    if (i >= nr + W - 1) break;
+    if (t >= 0) {
+      const float *row = bcx + (size_t)t * 3 * D;
+      y[i] = row[c] * row[2 * D + c];
+    } else {
+      y[i] = __half2float(state[(size_t)(W - 1 + t) * D + c]);  // only row block 0 gets here
+    }
   }
-  for (int i = 0; i < W - 1; i++) state[(size_t)i * D + c] = __float2half_rn(hist[i]);
+#pragma unroll
+  for (int i = 0; i < kConvRows; i++)
+    if (i < nr) cg_[i] = bcx[(size_t)(r0 + i) * 3 * D + D + c];
+  float wk[kMaxConvWidth];
+#pragma unroll
+  for (int k = 0; k < kMaxConvWidth; k++) wk[k] = k < W ? w[(size_t)c * W + k] : 0.0f;
+#pragma unroll
+  for (int i = 0; i < kConvRows; i++) {
+    if (i >= nr) break;
+    float a = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kMaxConvWidth; k++)
+      if (k < W) a += wk[k] * y[i + k];
+    store_out(out, out_dtype, (size_t)(r0 + i) * D + c, cg_[i] * a);
+  }
+  if (blockIdx.y == 0 && W > 1) {
+    // new state: y at rows rows-(W-1) .. rows-1 (old state for negative rows)
+    float ns[kMaxConvWidth];
+#pragma unroll
+    for (int i = 0; i < kMaxConvWidth - 1; i++) {
+      if (i >= W - 1) break;
+      const int t = rows - (W - 1) + i;
+      if (t < 0) {
+        ns[i] = __half2float(state[(size_t)(W - 1 + t) * D + c]);
+      } else {
+        const float *row = bcx + (size_t)t * 3 * D;
+        ns[i] = row[c] * row[2 * D + c];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxConvWidth - 1; i++)
+      if (i < W - 1) state[(size_t)i * D + c] = __float2half_rn(ns[i]);
+  }
 }
 
 // ---- fp16 output head + argmax (head engine.ts:8557, pick :8352) -----------
-// logits[r][v] = x[r] . W[v]; warp per vocab row, 16-byte loads, x staged
-// in shared memory as fp32.
+// logits[r][v] = x[r] . W[v]; warp per vocab row, 16-byte loads issued
+// eight at a time, x staged in shared memory as fp32. With `amax`, each warp also
+// keeps its best (logit, index) per row, each CTA publishes its best, and
+// the last CTA to finish (a counter it resets) reduces them: the greedy
+// token without a second launch.
 
 constexpr int kHeadMaxRows = 8;
+constexpr int kHeadCtasPerSm = 3;
+constexpr int kHeadThreads = 256;
+constexpr int kHeadUnroll = 8;  // 16-byte loads in flight per lane (a 4 KB row per warp)
 
-__global__ void head_kernel(const __half *x, int rows, int D, const __half *W, int V, float *logits) {
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  // larger logit first, then the lower index
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned)(0xffffffffu - (unsigned)idx);
+}
+
+// Head input: x fp16 [rows][D] as given, or (with `nrm`) the final norm of
+// the residual stream, rmsnorm(a + b) * weight rounded to fp16 as the
+// separate norm pass would store it.
+struct HeadNorm {
+  const float *a, *b, *w;
+  float eps;
+};
+
+template <bool NORM, int kHeadMaxRows>  // kHeadMaxRows: 1 (decode) or 8
+__global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
+    head_kernel(const __half *x, HeadNorm nrm, int rows, int D, const __half *W, int V, float *logits, int32_t *amax,
+                unsigned long long *part, unsigned *count) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
   extern __shared__ float xs[];  // [rows][D]
-  for (int i = threadIdx.x; i < rows * D; i += blockDim.x) xs[i] = __half2float(x[i]);
+  __shared__ unsigned long long s_key[kHeadThreads / 32][8];
+  __shared__ bool s_last;
+  if (NORM) {
+    __shared__ float red[32];
+    for (int r = 0; r < rows; r++) {
+      float ss = 0.0f;
+      for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        float v = nrm.a[(size_t)r * D + i];
+        if (nrm.b) v += nrm.b[(size_t)r * D + i];
+        xs[r * D + i] = v;
+        ss += v * v;
+      }
+      const float inv = rsqrtf(block_sum(ss, red) / (float)D + nrm.eps);
+      for (int i = threadIdx.x; i < D; i += blockDim.x)
+        xs[r * D + i] = __half2float(__float2half_rn(clamp_half(xs[r * D + i] * inv * nrm.w[i])));
+    }
+  } else {
+    for (int i = threadIdx.x; i < rows * D; i += blockDim.x) xs[i] = __half2float(x[i]);
+  }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
-  for (int v = blockIdx.x * warps + (threadIdx.x >> 5); v < V; v += gridDim.x * warps) {
+  const int nvec = D / 8;
+  float bv[kHeadMaxRows];
+  int bi[kHeadMaxRows];
+#pragma unroll
+  for (int r = 0; r < kHeadMaxRows; r++) {
+    bv[r] = -INFINITY;
+    bi[r] = 0x7fffffff;
+  }
+  for (int v = blockIdx.x * warps + warp; v < V; v += gridDim.x * warps) {
     const uint4 *wr = reinterpret_cast<const uint4 *>(W + (size_t)v * D);
     float acc[kHeadMaxRows];
 #pragma unroll
     for (int r = 0; r < kHeadMaxRows; r++) acc[r] = 0.0f;
-    for (int c = lane; c < D / 8; c += 32) {
-      const uint4 u = __ldg(wr + c);
-      const __half2 *hp = reinterpret_cast<const __half2 *>(&u);
-      float wf[8];
+    for (int c0 = lane; c0 < nvec; c0 += 32 * kHeadUnroll) {
+      uint4 u[kHeadUnroll];
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const float2 f = __half22float2(hp[i]);
-        wf[2 * i] = f.x;
-        wf[2 * i + 1] = f.y;
-      }
+      for (int j = 0; j < kHeadUnroll; j++)
+        if (c0 + 32 * j < nvec) u[j] = __ldcs(wr + c0 + 32 * j);  // read once: stream past L2
 #pragma unroll
-      for (int r = 0; r < kHeadMaxRows; r++) {
-        if (r >= rows) break;
-        const float *xr = xs + r * D + c * 8;
+      for (int j = 0; j < kHeadUnroll; j++) {
+        const int c = c0 + 32 * j;
+        if (c >= nvec) break;
+        const __half2 *hp = reinterpret_cast<const __half2 *>(&u[j]);
+        float wf[8];
 #pragma unroll
-        for (int i = 0; i < 8; i++) acc[r] += wf[i] * xr[i];
+        for (int i = 0; i < 4; i++) {
+          const float2 f = __half22float2(hp[i]);
+          wf[2 * i] = f.x;
+          wf[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int r = 0; r < kHeadMaxRows; r++) {
+          if (r >= rows) break;
+          const float4 *xr = reinterpret_cast<const float4 *>(xs + r * D + c * 8);
+          const float4 x0 = xr[0], x1 = xr[1];
+          acc[r] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w + wf[4] * x1.x + wf[5] * x1.y +
+                    wf[6] * x1.z + wf[7] * x1.w;
+        }
       }
     }
 #pragma unroll
     for (int r = 0; r < kHeadMaxRows; r++) {
       if (r >= rows) break;
-      const float s = warp_sum(acc[r]);
-      if (lane == 0) logits[(size_t)r * V + v] = s;
+      const float sres = warp_sum(acc[r]);
+      if (lane == 0) logits[(size_t)r * V + v] = sres;
+      if (sres > bv[r]) {  // v grows along a warp's walk: ties keep the lower index
+        bv[r] = sres;
+        bi[r] = v;
+      }
     }
   }
+  if (!amax) return;
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kHeadMaxRows; r++)
+      if (r < rows) s_key[warp][r] = argmax_key(bv[r], bi[r]);
+  }
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    unsigned long long k = 0;
+    for (int w = 0; w < warps; w++) k = max(k, s_key[w][threadIdx.x]);
+    part[(size_t)blockIdx.x * rows + threadIdx.x] = k;
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(count, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // The last CTA: every thread takes a share of the CTAs' keys, per row.
+  for (int r = 0; r < rows; r++) {
+    unsigned long long k = 0;
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) k = max(k, __ldcg(part + (size_t)b * rows + r));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) k = max(k, __shfl_xor_sync(0xffffffffu, k, o));
+    if (lane == 0) s_key[warp][0] = k;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long kk = 0;
+      for (int w = 0; w < warps; w++) kk = max(kk, s_key[w][0]);
+      amax[r] = (int32_t)(0xffffffffu - (unsigned)(kk & 0xffffffffu));
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = 0;  // ready for the next launch (stream order)
 }
 
 // Per row: the index of the largest logit, the lowest index on ties.
 __global__ void argmax_kernel(const float *logits, int V, int32_t *out) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
   __shared__ float sv[32];
   __shared__ int si[32];
   const int r = blockIdx.x;
@@ -404,84 +640,125 @@ __global__ void argmax_kernel(const float *logits, int V, int32_t *out) {
   }
 }
 
-__global__ void add_i32_kernel(int32_t *p, int delta) { *p += delta; }
+__global__ void add_i32_kernel(int32_t *p, int delta) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
+  *p += delta;
+}
+
+// Launch with programmatic dependent launch when `pdl`: the kernel may start
+// while the previous one in the stream finishes (every kernel here waits
+// for it with griddepcontrol.wait before reading anything).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                     Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  if (pdl) {
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 }  // namespace
 
-cudaError_t launch_embed(const int32_t *ids, int rows, const void *table, int V, int D, float *out,
-                         cudaStream_t s) {
-  embed_kernel<<<rows, 256, 0, s>>>(ids, rows, reinterpret_cast<const __half *>(table), V, D, out);
-  return cudaGetLastError();
+cudaError_t launch_embed(const int32_t *ids, int rows, const void *table, int V, int D, float *out, cudaStream_t s,
+                         bool pdl) {
+  return launch_k(embed_kernel, dim3(rows), dim3(256), 0, s, pdl, ids, rows, reinterpret_cast<const __half *>(table),
+                  V, D, out);
 }
 
 cudaError_t launch_rmsnorm(float *x, const float *add, const float *w, float eps, int rows, int D, void *out,
-                           int out_dtype, cudaStream_t s) {
-  rmsnorm_kernel<<<rows, D >= 1024 ? 1024 : ((D + 31) / 32) * 32, 0, s>>>(x, add, w, eps, D, out, out_dtype);
-  return cudaGetLastError();
+                           int out_dtype, cudaStream_t s, bool pdl) {
+  const int threads = D >= 1024 ? 1024 : ((D + 31) / 32) * 32;
+  return launch_k(rmsnorm_kernel, dim3(rows), dim3(threads), 0, s, pdl, x, add, w, eps, D, out, out_dtype);
 }
 
 cudaError_t launch_rope_kv(const float *qkv, int rows, int H, int Hkv, int Dh, const int *pos0, float theta,
                            const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache,
-                           void *v_cache, int cache_len, unsigned *flags, cudaStream_t s) {
-  rope_kv_kernel<<<dim3(rows, H + Hkv), Dh / 2, 0, s>>>(qkv, H, Hkv, Dh, pos0, theta, q_norm, k_norm, eps,
-                                                       reinterpret_cast<__half *>(q_out),
-                                                       reinterpret_cast<__half *>(k_cache),
-                                                       reinterpret_cast<__half *>(v_cache), cache_len, flags);
-  return cudaGetLastError();
+                           void *v_cache, int cache_len, unsigned *flags, cudaStream_t s, bool pdl) {
+  return launch_k(rope_kv_kernel, dim3(rows, H + Hkv), dim3(Dh / 2), 0, s, pdl, qkv, H, Hkv, Dh, pos0, theta, q_norm,
+                  k_norm, eps, reinterpret_cast<__half *>(q_out), reinterpret_cast<__half *>(k_cache),
+                  reinterpret_cast<__half *>(v_cache), cache_len, flags);
+}
+
+template <int DPL>
+cudaError_t launch_attention_t(const void *q, int rows, int H, int Hkv, const void *k_cache, const void *v_cache,
+                               int cache_len, const int *pos0, void *out, cudaStream_t s, bool pdl) {
+  const AttnSmem lay(32 * DPL, H / Hkv);
+  const size_t smem = lay.total;
+  auto kern = attention_kernel<DPL>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_k(kern, dim3(kAttnCluster, Hkv, rows), dim3(kAttnThreads), smem, s, pdl,
+                  reinterpret_cast<const __half *>(q), H, Hkv, reinterpret_cast<const __half *>(k_cache),
+                  reinterpret_cast<const __half *>(v_cache), cache_len, pos0, reinterpret_cast<__half *>(out));
 }
 
 cudaError_t launch_attention(const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
-                             const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s) {
-  if (H % Hkv || H / Hkv > kAttnMaxGroup || Dh % 8 || Dh > 256) return cudaErrorInvalidValue;
-  const AttnSmem lay(Dh, H / Hkv);
-  const size_t smem = lay.total;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+                             const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s,
+                             bool pdl) {
+  if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
+  switch (Dh) {
+    case 32: return launch_attention_t<1>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 64: return launch_attention_t<2>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 128: return launch_attention_t<4>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 256: return launch_attention_t<8>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    default: return cudaErrorInvalidValue;
   }
-  attention_kernel<<<dim3(kAttnCluster, Hkv, rows), kAttnThreads, smem, s>>>(
-      reinterpret_cast<const __half *>(q), H, Hkv, Dh, reinterpret_cast<const __half *>(k_cache),
-      reinterpret_cast<const __half *>(v_cache), cache_len, pos0, reinterpret_cast<__half *>(out));
-  return cudaGetLastError();
 }
 
-cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s) {
+cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s, bool pdl) {
   const size_t n = (size_t)rows * I;
   const size_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
-  swiglu_kernel<<<(unsigned)(blocks ? blocks : 1), 256, 0, s>>>(gu, rows, I, out, out_dtype);
-  return cudaGetLastError();
+  return launch_k(swiglu_kernel, dim3((unsigned)(blocks ? blocks : 1)), dim3(256), 0, s, pdl, gu, rows, I, out,
+                  out_dtype);
 }
 
 cudaError_t launch_short_conv(const float *bcx, int rows, int D, int W, const float *w, void *state, void *out,
-                              int out_dtype, cudaStream_t s) {
+                              int out_dtype, cudaStream_t s, bool pdl) {
   if (W < 1 || W > kMaxConvWidth) return cudaErrorInvalidValue;
-  short_conv_kernel<<<(D + 127) / 128, 128, 0, s>>>(bcx, rows, D, W, w, reinterpret_cast<__half *>(state), out,
-                                                    out_dtype);
-  return cudaGetLastError();
+  const dim3 grid((D + 127) / 128, (rows + kConvRows - 1) / kConvRows);
+  return launch_k(short_conv_kernel, grid, dim3(128), 0, s, pdl, bcx, rows, D, W, w,
+                  reinterpret_cast<__half *>(state), out, out_dtype);
 }
 
-cudaError_t launch_head(const void *x, int rows, int D, const void *W, int V, float *logits, int num_sms,
-                        cudaStream_t s) {
+cudaError_t launch_head(const void *x, const float *na, const float *nb, const float *nw, float eps, int rows, int D,
+                        const void *W, int V, float *logits, int32_t *amax, unsigned long long *part,
+                        size_t part_bytes, unsigned *count, int num_sms, cudaStream_t s, bool pdl) {
   if (rows > kHeadMaxRows || D % 8) return cudaErrorInvalidValue;
   const size_t smem = (size_t)rows * D * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  const bool norm = na != nullptr;
+  auto kern = norm ? (rows == 1 ? head_kernel<true, 1> : head_kernel<true, kHeadMaxRows>)
+                   : (rows == 1 ? head_kernel<false, 1> : head_kernel<false, kHeadMaxRows>);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  head_kernel<<<num_sms * 4, 256, smem, s>>>(reinterpret_cast<const __half *>(x), rows, D,
-                                            reinterpret_cast<const __half *>(W), V, logits);
-  return cudaGetLastError();
+  int grid = num_sms * kHeadCtasPerSm;
+  const int max_grid = (int)(part_bytes / (sizeof(unsigned long long) * (rows ? rows : 1)));
+  if (grid > max_grid) grid = max_grid;
+  const HeadNorm hn{na, nb, nw, eps};
+  return launch_k(kern, dim3(grid), dim3(kHeadThreads), smem, s, pdl, reinterpret_cast<const __half *>(x), hn, rows,
+                  D, reinterpret_cast<const __half *>(W), V, logits, amax, part, count);
 }
 
-cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *out, cudaStream_t s) {
-  argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, out);
-  return cudaGetLastError();
+cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *out, cudaStream_t s, bool pdl) {
+  return launch_k(argmax_kernel, dim3(rows), dim3(1024), 0, s, pdl, logits, V, out);
 }
 
-cudaError_t launch_add_i32(int32_t *p, int delta, cudaStream_t s) {
-  add_i32_kernel<<<1, 1, 0, s>>>(p, delta);
-  return cudaGetLastError();
+cudaError_t launch_add_i32(int32_t *p, int delta, cudaStream_t s, bool pdl) {
+  return launch_k(add_i32_kernel, dim3(1), dim3(1), 0, s, pdl, p, delta);
 }
 
 }  // namespace wg

@@ -78,6 +78,13 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src, uint32
 
 // ---- programmatic dependent launch ----------------------------------------
 
+// 16-byte asynchronous global -> shared copy (cp.async, bypassing L1), and
+// the wait for all of this thread's outstanding ones.
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 

@@ -137,7 +137,80 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
   }
 }
 
-template <int NG, bool ZEROS>
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// Eight consecutive x values (row m, columns k..k+7) as fp16, made by the
+// prologue: (residual + b) * inv * w for the norm, silu(gate) * up for SwiGLU.
+template <int PRO>
+__device__ __forceinline__ uint4 prologue_x8(const Prologue &p, int K, int m, int k, float inv) {
+  float f[8];
+  if (PRO == kProRmsNorm) {
+    const float4 *r = reinterpret_cast<const float4 *>(p.a + (size_t)m * K + k);
+    float4 v0 = r[0], v1 = r[1];
+    if (p.b) {
+      const float4 *b = reinterpret_cast<const float4 *>(p.b + (size_t)m * K + k);
+      v0 = add4(v0, b[0]);
+      v1 = add4(v1, b[1]);
+    }
+    const float4 w0 = reinterpret_cast<const float4 *>(p.w + k)[0], w1 = reinterpret_cast<const float4 *>(p.w + k)[1];
+    f[0] = v0.x * inv * w0.x; f[1] = v0.y * inv * w0.y; f[2] = v0.z * inv * w0.z; f[3] = v0.w * inv * w0.w;
+    f[4] = v1.x * inv * w1.x; f[5] = v1.y * inv * w1.y; f[6] = v1.z * inv * w1.z; f[7] = v1.w * inv * w1.w;
+  } else {
+    const float4 *g = reinterpret_cast<const float4 *>(p.a + (size_t)m * 2 * K + k);
+    const float4 *u = reinterpret_cast<const float4 *>(p.a + (size_t)m * 2 * K + K + k);
+    const float4 g0 = g[0], g1 = g[1], u0 = u[0], u1 = u[1];
+    f[0] = silu_mul(g0.x, u0.x); f[1] = silu_mul(g0.y, u0.y); f[2] = silu_mul(g0.z, u0.z); f[3] = silu_mul(g0.w, u0.w);
+    f[4] = silu_mul(g1.x, u1.x); f[5] = silu_mul(g1.y, u1.y); f[6] = silu_mul(g1.z, u1.z); f[7] = silu_mul(g1.w, u1.w);
+  }
+  return make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+}
+
+// The norm prologue's row statistics: inv[m] = 1 / sqrt(mean((residual +
+// b)^2) + eps) over all of K, for every row (all threads of the CTA), and
+// the residual sum written out by a grid-strided share of every CTA.
+__device__ void rmsnorm_rows(const Prologue &p, int M, int K, float *s_part, float *s_inv) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K4 = K / 4;
+  for (int m = 0; m < M; m++) {
+    const float4 *r = reinterpret_cast<const float4 *>(p.a + (size_t)m * K);
+    const float4 *b = p.b ? reinterpret_cast<const float4 *>(p.b + (size_t)m * K) : nullptr;
+    float ss = 0.0f;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < K4; i += kThreads) {
+      float4 v = r[i];
+      if (b) v = add4(v, b[i]);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum_f(ss);
+    if (lane == 0) s_part[warp * kProMaxTokens + m] = ss;
+  }
+  if (p.out) {
+    const int ncta = gridDim.x * gridDim.y, cta = blockIdx.y * gridDim.x + blockIdx.x;
+    const float4 *r = reinterpret_cast<const float4 *>(p.a);
+    const float4 *b = reinterpret_cast<const float4 *>(p.b);
+    float4 *o = reinterpret_cast<float4 *>(p.out);
+    for (int i = cta * kThreads + threadIdx.x; i < M * K4; i += ncta * kThreads) o[i] = b ? add4(r[i], b[i]) : r[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < M) {
+    float t = 0.0f;
+    for (int w = 0; w < kWarps; w++) t += s_part[w * kProMaxTokens + threadIdx.x];
+    s_inv[threadIdx.x] = rsqrtf(t / (float)K + p.eps);
+  }
+  __syncthreads();
+}
+
+template <int NG, bool ZEROS, int PRO>
 __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -188,9 +261,15 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
   pdl_wait();
   if (a.trace && threadIdx.x == 0) ts[2] = globaltimer();
 
-  // 3. Each warp stages its own K slice of x[0..M) as fp16 (no CTA barrier).
+  // 3. Each warp stages its own K slice of x[0..M) as fp16 (no CTA barrier,
+  //    except for the norm prologue's row statistics).
   const int M = a.M;
   const int stride = L.x_stride;
+  __shared__ float s_inv[PRO == kProRmsNorm ? kProMaxTokens : 1];
+  if constexpr (PRO == kProRmsNorm) {
+    __shared__ float s_part[kWarps * kProMaxTokens];
+    rmsnorm_rows(a.pro, M, a.K, s_part, s_inv);
+  }
   {
     // Up to 4 loads in flight per lane before any store (one L2 round trip
     // for the usual M * 8 tiles <= 128 chunks).
@@ -205,7 +284,12 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
         if (idx < M * chunks) {
           const int m = idx / chunks, c = idx - m * chunks;
           const int k = kbase + c * 8;
-          if (k < a.K) v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
+          if (k < a.K) {
+            if constexpr (PRO == kProNone)
+              v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
+            else
+              v[u] = prologue_x8<PRO>(a.pro, a.K, m, k, PRO == kProRmsNorm ? s_inv[m] : 0.0f);
+          }
         }
       }
 #pragma unroll
@@ -291,10 +375,10 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
   }
 }
 
-template <int NG, bool ZEROS>
+template <int NG, bool ZEROS, int PRO = kProNone>
 cudaError_t launch_t(const GemvArgs &a, cudaStream_t stream, bool pdl) {
   const GemvSmem L = gemv_smem(a.M, a.kt_per_cta, NG, ZEROS);
-  auto kern = gemv_kernel<NG, ZEROS>;
+  auto kern = gemv_kernel<NG, ZEROS, PRO>;
   // Function attributes once per instantiation (not per launch: launches may
   // be captured into a CUDA graph).
   static bool configured = false;
@@ -330,7 +414,50 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t stream, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+// The prologue on its own, one CTA per row: x fp16 [M][K] for the GEMM path
+// (and the residual sum, as in the fused form).
+__global__ void __launch_bounds__(kThreads) prologue_kernel(const Prologue p, int K, __half *x) {
+  __shared__ float s_part[kWarps * kProMaxTokens];
+  __shared__ float s_inv;
+  const int m = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float inv = 0.0f;
+  if (p.kind == kProRmsNorm) {
+    const float4 *r = reinterpret_cast<const float4 *>(p.a + (size_t)m * K);
+    const float4 *b = p.b ? reinterpret_cast<const float4 *>(p.b + (size_t)m * K) : nullptr;
+    float4 *o = p.out ? reinterpret_cast<float4 *>(p.out + (size_t)m * K) : nullptr;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < K / 4; i += kThreads) {
+      float4 v = r[i];
+      if (b) v = add4(v, b[i]);
+      if (o) o[i] = v;
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum_f(ss);
+    if (lane == 0) s_part[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+      for (int w = 0; w < kWarps; w++) t += s_part[w];
+      s_inv = rsqrtf(t / (float)K + p.eps);
+    }
+    __syncthreads();
+    inv = s_inv;
+  }
+  for (int k = threadIdx.x * 8; k < K; k += kThreads * 8) {
+    const uint4 v = p.kind == kProRmsNorm ? prologue_x8<kProRmsNorm>(p, K, m, k, inv)
+                                          : prologue_x8<kProSwiglu>(p, K, m, k, 0.0f);
+    *reinterpret_cast<uint4 *>(x + (size_t)m * K + k) = v;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_prologue(const Prologue &p, int M, int K, void *x_f16, cudaStream_t stream) {
+  if (K % 8 || (p.kind != kProRmsNorm && p.kind != kProSwiglu)) return cudaErrorInvalidValue;
+  prologue_kernel<<<M, kThreads, 0, stream>>>(p, K, reinterpret_cast<__half *>(x_f16));
+  return cudaGetLastError();
+}
 
 bool plan_gemv(GemvArgs &a, int num_sms) {
   if (a.M < 1 || a.M > kGemvMaxTokens) return false;
@@ -362,6 +489,14 @@ bool plan_gemv(GemvArgs &a, int num_sms) {
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl) {
   const int NG = (a.M + 7) / 8;
   const bool z = a.zro != nullptr;
+  if (a.pro.kind != kProNone) {
+    if (a.M > kProMaxTokens) return cudaErrorInvalidValue;
+    if (a.pro.kind == kProRmsNorm)
+      return z ? launch_t<1, true, kProRmsNorm>(a, stream, pdl) : launch_t<1, false, kProRmsNorm>(a, stream, pdl);
+    if (a.pro.kind == kProSwiglu)
+      return z ? launch_t<1, true, kProSwiglu>(a, stream, pdl) : launch_t<1, false, kProSwiglu>(a, stream, pdl);
+    return cudaErrorInvalidValue;
+  }
   switch (NG) {
     case 1: return z ? launch_t<1, true>(a, stream, pdl) : launch_t<1, false>(a, stream, pdl);
     case 2: return z ? launch_t<2, true>(a, stream, pdl) : launch_t<2, false>(a, stream, pdl);

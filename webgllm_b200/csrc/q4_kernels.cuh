@@ -31,6 +31,23 @@ struct RepackArgs {
 cudaError_t launch_repack(const RepackArgs &a, cudaStream_t stream);
 
 // The decode GEMV: y[M][N] = x[M][K] . W^T for M <= 32.
+// A transform that produces the matmul's fp16 input from other tensors in
+// the same launch (the decoder's norm and SwiGLU passes fused into the
+// matmul that consumes them).
+enum ProKind { kProNone = 0, kProRmsNorm = 1, kProSwiglu = 2 };
+struct Prologue {
+  int kind;        // ProKind
+  const float *a;  // kProRmsNorm: residual [M][K]; kProSwiglu: gate | up [M][2K]
+  const float *b;  // kProRmsNorm: added to the residual [M][K], or null
+  const float *w;  // kProRmsNorm: norm weight [K]
+  float eps;
+  float *out;      // kProRmsNorm: receives residual + b [M][K], or null
+};
+// Rows of one fused GEMV launch (the prologue needs the whole row per CTA).
+constexpr int kProMaxTokens = 8;
+// The prologue alone: x fp16 [M][K] (for matmuls that do not fuse it).
+cudaError_t launch_prologue(const Prologue &p, int M, int K, void *x_f16, cudaStream_t stream);
+
 struct GemvArgs {
   const uint32_t *nib;
   const uint16_t *scl;
@@ -48,6 +65,7 @@ struct GemvArgs {
   unsigned long long trace_cap;    // records that fit
   unsigned launch_index;
   int trigger_at;  // when dependents may launch: 0 entry, 1 x staged, 2 multiplies done
+  Prologue pro;    // kProNone: x as given; else x is made from pro (M <= kProMaxTokens)
 };
 
 constexpr int kGemvMaxTokens = 32;

@@ -21,7 +21,7 @@ import torch
 
 from . import _lib
 from .q4 import QuantMatrix, context, newQuantMatrix, packQ4_0
-from ._lib import WG_F16, WG_F32
+from ._lib import WG_F16, WG_F32, WG_PRO_RMSNORM, WG_PRO_SWIGLU
 
 P = ctypes.c_void_p
 
@@ -108,8 +108,9 @@ class DecoderModel:
     """Weights, caches and the forward pass of one decoder on one GPU."""
 
     def __init__(self, cfg: DecoderConfig, seed: int = 0, max_ctx: int = 1024, max_rows: int = 512,
-                 keep_blocks: bool = False, device: int | None = None):
+                 keep_blocks: bool = False, device: int | None = None, fused: bool = True):
         self.cfg = cfg
+        self.fused = fused
         self.ctx = context(device)
         self.max_ctx, self.max_rows = max_ctx, max_rows
         g = torch.Generator(device="cuda")
@@ -145,6 +146,7 @@ class DecoderModel:
         # activations for up to max_rows rows
         R = max_rows
         self.x = torch.zeros((R, D), device="cuda")                      # residual stream
+        self.x2 = torch.zeros((R, D), device="cuda")                     # its other copy (fused path)
         self.h = torch.zeros((R, D), dtype=torch.float16, device="cuda")  # normed input of a matmul
         self.qkv = torch.zeros((R, (H + 2 * Hkv) * Dh), device="cuda")
         self.q = torch.zeros((R, H * Dh), dtype=torch.float16, device="cuda")
@@ -177,12 +179,83 @@ class DecoderModel:
         self.v_cache.zero_()
         self.conv_state.zero_()
 
+    def _mm_norm(self, lin: Linear, resid, add, w, resid_out, y: torch.Tensor, rows: int):
+        """y = rmsnorm(resid + add) * w . W^T in one launch (decode rows)."""
+        pro = _lib.wg_prologue(WG_PRO_RMSNORM, resid.data_ptr(), add.data_ptr() if add is not None else None,
+                               w.data_ptr(), self.cfg.eps, resid_out.data_ptr() if resid_out is not None else None)
+        self._c(_lib.lib().wg_q4_matmul_fused(P(self.ctx.handle), P(lin.m.handle), ctypes.byref(pro), rows,
+                                              P(y.data_ptr()), WG_F32))
+
+    def _mm_swiglu(self, lin: Linear, gu, y: torch.Tensor, rows: int):
+        pro = _lib.wg_prologue(WG_PRO_SWIGLU, gu.data_ptr(), None, None, 0.0, None)
+        self._c(_lib.lib().wg_q4_matmul_fused(P(self.ctx.handle), P(lin.m.handle), ctypes.byref(pro), rows,
+                                              P(y.data_ptr()), WG_F32))
+
     def forward(self, ids: torch.Tensor, rows: int):
         """Runs `rows` tokens (device int32 ids) at the current position; leaves
         the last row's logits in self.logits and its greedy next token in
         self.next_id, and advances the position."""
+        if self.fused:
+            return self._forward_fused(ids, rows)
+        return self._forward_passes(ids, rows)
+
+    def _attend(self, lay, rows):
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
-        D, H, Hkv, Dh, I, V = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab
+        H, Hkv, Dh = cfg.heads, cfg.kv_heads, cfg.head_dim
+        s = lay["slot"]
+        kc, vc = self.k_cache[s], self.v_cache[s]
+        qn, kn = lay.get("q_norm"), lay.get("k_norm")
+        self._c(L.wg_rope_kv(c, P(self.qkv.data_ptr()), rows, H, Hkv, Dh, P(self.pos.data_ptr()), cfg.theta,
+                             P(qn.data_ptr() if qn is not None else None), P(kn.data_ptr() if kn is not None else None),
+                             cfg.eps, P(self.q.data_ptr()), P(kc.data_ptr()), P(vc.data_ptr()), self.max_ctx))
+        self._c(L.wg_attention(c, P(self.q.data_ptr()), rows, H, Hkv, Dh, P(kc.data_ptr()), P(vc.data_ptr()),
+                               self.max_ctx, P(self.pos.data_ptr()), P(self.att.data_ptr())))
+        self._mm(lay["o"], self.att, self.o, rows)
+
+    def _convolve(self, lay, rows):
+        cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
+        self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, cfg.hidden, cfg.conv_width,
+                                P(lay["conv_w"].data_ptr()), P(self.conv_state[lay["slot"]].data_ptr()),
+                                P(self.cv.data_ptr()), WG_F16))
+        self._mm(lay["out"], self.cv, self.o, rows)
+
+    def _forward_fused(self, ids: torch.Tensor, rows: int):
+        """Each norm runs inside the matmul that consumes it, SwiGLU inside the
+        down projection and the final norm inside the head: per layer the
+        residual stream alternates between self.x and self.x2."""
+        cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
+        D, V = cfg.hidden, cfg.vocab
+        self.ctx.use_torch_stream()
+        self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), V, D, P(self.x.data_ptr())))
+        cur, other = self.x, self.x2
+        add = None
+        for lay in self.layers:
+            proj = self.qkv if lay["type"] == "attn" else self.bcx
+            lin = lay["qkv"] if lay["type"] == "attn" else lay["in"]
+            if add is None:
+                self._mm_norm(lin, cur, None, lay["norm1"], None, proj, rows)
+            else:
+                self._mm_norm(lin, cur, add, lay["norm1"], other, proj, rows)
+                cur, other = other, cur
+            if lay["type"] == "attn":
+                self._attend(lay, rows)
+            else:
+                self._convolve(lay, rows)
+            self._mm_norm(lay["gu"], cur, self.o, lay["norm2"], other, self.gu, rows)
+            cur, other = other, cur
+            self._mm_swiglu(lay["down"], self.gu, self.o, rows)
+            add = self.o
+        last = rows - 1
+        self._c(L.wg_head_rmsnorm(c, P(cur[last].data_ptr()), P(add[last].data_ptr()),
+                                  P(self.final_norm.data_ptr()), cfg.eps, 1, D, P(self.head.data_ptr()), V,
+                                  P(self.logits.data_ptr()), P(self.next_id.data_ptr())))
+        self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), rows))
+
+    def _forward_passes(self, ids: torch.Tensor, rows: int):
+        """One launch per engine pass (norm, matmul, SwiGLU, ... each on its
+        own)."""
+        cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
+        D, I, V = cfg.hidden, cfg.ffn, cfg.vocab
         self.ctx.use_torch_stream()
         self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), V, D, P(self.x.data_ptr())))
         add = None
@@ -190,24 +263,11 @@ class DecoderModel:
             self._c(L.wg_rmsnorm(c, P(self.x.data_ptr()), P(add), P(lay["norm1"].data_ptr()), cfg.eps, rows, D,
                                  P(self.h.data_ptr()), WG_F16))
             if lay["type"] == "attn":
-                s = lay["slot"]
-                kc, vc = self.k_cache[s], self.v_cache[s]
                 self._mm(lay["qkv"], self.h, self.qkv, rows)
-                qn = lay.get("q_norm")
-                kn = lay.get("k_norm")
-                self._c(L.wg_rope_kv(c, P(self.qkv.data_ptr()), rows, H, Hkv, Dh, P(self.pos.data_ptr()), cfg.theta,
-                                     P(qn.data_ptr() if qn is not None else None),
-                                     P(kn.data_ptr() if kn is not None else None), cfg.eps, P(self.q.data_ptr()),
-                                     P(kc.data_ptr()), P(vc.data_ptr()), self.max_ctx))
-                self._c(L.wg_attention(c, P(self.q.data_ptr()), rows, H, Hkv, Dh, P(kc.data_ptr()), P(vc.data_ptr()),
-                                       self.max_ctx, P(self.pos.data_ptr()), P(self.att.data_ptr())))
-                self._mm(lay["o"], self.att, self.o, rows)
+                self._attend(lay, rows)
             else:
-                s = lay["slot"]
                 self._mm(lay["in"], self.h, self.bcx, rows)
-                self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, D, cfg.conv_width, P(lay["conv_w"].data_ptr()),
-                                        P(self.conv_state[s].data_ptr()), P(self.cv.data_ptr()), WG_F16))
-                self._mm(lay["out"], self.cv, self.o, rows)
+                self._convolve(lay, rows)
             self._c(L.wg_rmsnorm(c, P(self.x.data_ptr()), P(self.o.data_ptr()), P(lay["norm2"].data_ptr()), cfg.eps,
                                  rows, D, P(self.h.data_ptr()), WG_F16))
             self._mm(lay["gu"], self.h, self.gu, rows)
@@ -220,8 +280,8 @@ class DecoderModel:
         ol = self.o[last:last + 1]
         self._c(L.wg_rmsnorm(c, P(xl.data_ptr()), P(ol.data_ptr()), P(self.final_norm.data_ptr()), cfg.eps, 1, D,
                              P(self.h.data_ptr()), WG_F16))
-        self._c(L.wg_head(c, P(self.h.data_ptr()), 1, D, P(self.head.data_ptr()), V, P(self.logits.data_ptr())))
-        self._c(L.wg_argmax(c, P(self.logits.data_ptr()), 1, V, P(self.next_id.data_ptr())))
+        self._c(L.wg_head(c, P(self.h.data_ptr()), 1, D, P(self.head.data_ptr()), V, P(self.logits.data_ptr()),
+                          P(self.next_id.data_ptr())))
         self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), rows))
 
     def prefill(self, prompt: torch.Tensor):
