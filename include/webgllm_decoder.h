@@ -6,9 +6,13 @@
  * returns, device pointers, work enqueued on the context's stream.
  *
  * Layouts: row-major [rows][features]. The residual stream is fp32; matmul
- * inputs fp16 (WG_F16); caches fp16. `pos` is a device int32 holding the
- * position of row 0 (rows are consecutive positions), so a decode step can
- * be replayed from a CUDA graph while the position advances on the device.
+ * inputs fp16 (WG_F16); caches fp16. Sequences: where a call takes `batch`,
+ * its `rows` are `batch` independent sequences of rows / batch consecutive
+ * tokens each (a decode step of 8 sequences: rows 8, batch 8; one prompt:
+ * rows = its length, batch 1); `pos` is a device int32 [batch] holding each
+ * sequence's position of its first row, and caches / states carry a leading
+ * [batch] dimension. Positions live on the device, so a decode step can be
+ * replayed from a CUDA graph while they advance.
  */
 #ifndef WEBGLLM_DECODER_H
 #define WEBGLLM_DECODER_H
@@ -35,21 +39,22 @@ int wg_rmsnorm(wg_ctx *ctx, float *x, const float *add, const float *weight, flo
 /* qk-norm + RoPE + KV append (headPrep, src/gpu/kernels.ts:2196-2322):
  * qkv fp32 [rows][(H + 2 Hkv) Dh] (q | k | v). Per head, optional RMS norm
  * over Dh with q_norm / k_norm weights (NULL: none), then rotate-half RoPE
- * of the pairs (j, j + Dh/2) by (pos + r) * theta^(-2j/Dh). q_out fp16
- * [rows][H][Dh] scaled by 1/sqrt(Dh); k (rotated) and v appended to the fp16
- * caches [Hkv][cache_len][Dh] at positions pos..pos+rows-1. Dh % 64 == 0.
- * A position past cache_len is skipped and reported by wg_sync. */
-int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int H, int Hkv, int Dh, const int32_t *pos, float theta,
-               const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache, void *v_cache,
-               int cache_len);
+ * of the pairs (j, j + Dh/2) by p * theta^(-2j/Dh), p the row's position.
+ * q_out fp16 [rows][H][Dh] scaled by 1/sqrt(Dh); k (rotated) and v appended
+ * to the fp16 caches [batch][Hkv][cache_len][Dh] at each row's position.
+ * Dh % 64 == 0. A position past cache_len is skipped and reported by
+ * wg_sync. */
+int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int batch, int H, int Hkv, int Dh, const int32_t *pos,
+               float theta, const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache,
+               void *v_cache, int cache_len);
 
-/* Causal GQA attention over the fp16 caches (scores / attend,
- * src/gpu/kernels.ts:2386-2579): query row r (position pos + r) of head h
- * attends keys 0..pos+r of KV head h / (H / Hkv). q fp16 [rows][H][Dh]
+/* Causal GQA attention over the fp16 caches [batch][Hkv][cache_len][Dh]
+ * (scores / attend, src/gpu/kernels.ts:2386-2579): a query row at position p
+ * of head h attends keys 0..p of its sequence's KV head h / (H / Hkv). q fp16 [rows][H][Dh]
  * (already scaled), out fp16 [rows][H][Dh]. Dh in {32, 64, 128, 256},
  * H / Hkv <= 16. Each (row, KV head) is served by a cluster of 8 CTAs that
  * split the keys and merge through distributed shared memory. */
-int wg_attention(wg_ctx *ctx, const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
+int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                  const void *v_cache, int cache_len, const int32_t *pos, void *out);
 
 /* SwiGLU (REDUCE_SWIGLU, src/gpu/kernels.ts:1066-1077): gate_up fp32
@@ -59,10 +64,11 @@ int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int
 /* LFM2 gated short convolution (shortConv / convState,
  * src/gpu/kernels.ts:1380-1437): bcx fp32 [rows][3D] = B | C | x,
  * y = B * x, out[t] = C[t] * sum_k weight[c][k] * y[t - (W-1-k)] (weight fp32
- * [D][W]); y before the batch comes from state fp16 [W-1][D] (oldest first),
- * which is updated to the batch's last W-1 values of y. W <= 8. */
-int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const float *weight, void *state,
-                  void *out, int out_dtype);
+ * [D][W]); per sequence, y before its rows comes from its state fp16
+ * [W-1][D] (oldest first; states [batch][W-1][D]), which is updated to the
+ * sequence's last W-1 values of y. W <= 8. */
+int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int batch, int D, int W, const float *weight,
+                  void *state, void *out, int out_dtype);
 
 /* fp16 output head (head, src/engine.ts:8557): logits fp32 [rows][V] =
  * x fp16 [rows][D] . W^T, W fp16 [V][D]; rows <= 8, D % 8 == 0,
@@ -71,20 +77,30 @@ int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const f
  * must not overlap on one context (they share its reduction buffer). */
 int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits, int32_t *argmax);
 
-/* wg_head on the final norm of the residual stream, in one launch: x =
- * rmsnorm(resid + add) * weight (add may be NULL), rounded to fp16 as
- * wg_rmsnorm would store it; resid and add are fp32 [rows][D] and are not
- * written. (The engine's last addNormed before head, src/engine.ts:9304.) */
+/* wg_head on the final norm of the residual stream, in one launch: input
+ * row r = rmsnorm(resid + add) * weight of row r * row_stride of resid /
+ * add (fp32, [.][D], not written; add may be NULL), rounded to fp16 as
+ * wg_rmsnorm would store it (the engine's last addNormed before head,
+ * src/engine.ts:9304). For a vocabulary shard W = rows vocab_offset ..
+ * vocab_offset + V - 1 of the full head: argmax receives global indices,
+ * and `keys` (NULL: not written) each row's packed key, an int64 that
+ * orders as (logit, then lower index): the maximum over shards (an
+ * all-reduce MAX on int64) is the full head's greedy pick; see
+ * wg_pick_keys. */
 int wg_head_rmsnorm(wg_ctx *ctx, const float *resid, const float *add, const float *weight, float eps, int rows,
-                    int D, const void *W, int V, float *logits, int32_t *argmax);
+                    int row_stride, int D, const void *W, int V, int vocab_offset, float *logits, int32_t *argmax,
+                    int64_t *keys);
+
+/* ids[r] = the token index packed in keys[r] (wg_head_rmsnorm). */
+int wg_pick_keys(wg_ctx *ctx, const int64_t *keys, int rows, int32_t *ids);
 
 /* Greedy pick (src/engine.ts:8271 argmax): out[r] = index of the largest
  * logit of row r (the lowest index on ties). */
 int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out);
 
-/* *counter += delta on the device (advances the position of a replayed
- * decode step). */
-int wg_add_i32(wg_ctx *ctx, int32_t *counter, int delta);
+/* counters[0..n) += delta on the device (advances the positions of a
+ * replayed decode step). */
+int wg_add_i32(wg_ctx *ctx, int32_t *counters, int n, int delta);
 
 #ifdef __cplusplus
 }

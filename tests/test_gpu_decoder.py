@@ -101,7 +101,7 @@ def test_rope_kv_append(rows, H, Hkv, Dh, pos0, qk):
     q = torch.empty((rows, H, Dh), dtype=torch.float16, device="cuda")
     kc = torch.zeros((Hkv, cache_len, Dh), dtype=torch.float16, device="cuda")
     vc = torch.zeros_like(kc)
-    call(lib().wg_rope_kv, ptr(qkv), rows, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4 if Dh == 64 else 5e5),
+    call(lib().wg_rope_kv, ptr(qkv), rows, 1, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4 if Dh == 64 else 5e5),
          ptr(qn), ptr(kn), ctypes.c_float(1e-5), ptr(q), ptr(kc), ptr(vc), cache_len)
     wq, wk, wv = R.rope_kv(qkv, H, Hkv, Dh, pos0, 1e4 if Dh == 64 else 5e5, qn, kn, 1e-5)
     assert rel(q, wq) < 2e-3
@@ -119,7 +119,7 @@ def test_rope_kv_position_past_cache_is_reported():
     kc = torch.zeros((Hkv, cache_len, Dh), dtype=torch.float16, device="cuda")
     vc = torch.zeros_like(kc)
     c = ctx()
-    assert lib().wg_rope_kv(P(c.handle), ptr(qkv), 2, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4), None, None,
+    assert lib().wg_rope_kv(P(c.handle), ptr(qkv), 2, 1, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4), None, None,
                             ctypes.c_float(1e-5), ptr(q), ptr(kc), ptr(vc), cache_len) == 0
     with pytest.raises(wg.GpuError):
         c.sync()
@@ -145,10 +145,88 @@ def test_attention_causal_gqa(rows, H, Hkv, Dh, pos0):
     q = (torch.randn((rows, H, Dh), generator=g, device="cuda") / math.sqrt(Dh)).half()
     pos = torch.tensor([pos0], dtype=torch.int32, device="cuda")
     out = torch.empty((rows, H, Dh), dtype=torch.float16, device="cuda")
-    call(lib().wg_attention, ptr(q), rows, H, Hkv, Dh, ptr(kc), ptr(vc), cache_len, ptr(pos), ptr(out))
+    call(lib().wg_attention, ptr(q), rows, 1, H, Hkv, Dh, ptr(kc), ptr(vc), cache_len, ptr(pos), ptr(out))
     want = R.attention(q, kc, vc, pos0, H, Hkv)
     assert torch.isfinite(out.float()).all()
     assert (out.float() - want).abs().max().item() < 2e-3 * max(1.0, want.abs().max().item())
+
+
+def test_rope_and_attention_batched_sequences():
+    """3 independent sequences of 2 rows each, at different positions, with
+    their own caches: each equals the single-sequence computation."""
+    B, rps, H, Hkv, Dh, cache_len = 3, 2, 8, 2, 64, 512
+    rows = B * rps
+    g = gen(31)
+    pos0 = [5, 200, 0]
+    qkv = torch.randn((rows, (H + 2 * Hkv) * Dh), generator=g, device="cuda")
+    kc = (torch.randn((B, Hkv, cache_len, Dh), generator=g, device="cuda")).half()
+    vc = torch.randn((B, Hkv, cache_len, Dh), generator=g, device="cuda").half()
+    kc0, vc0 = kc.clone(), vc.clone()
+    pos = torch.tensor(pos0, dtype=torch.int32, device="cuda")
+    q = torch.empty((rows, H, Dh), dtype=torch.float16, device="cuda")
+    out = torch.empty((rows, H, Dh), dtype=torch.float16, device="cuda")
+    call(lib().wg_rope_kv, ptr(qkv), rows, B, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4), None, None,
+         ctypes.c_float(1e-5), ptr(q), ptr(kc), ptr(vc), cache_len)
+    call(lib().wg_attention, ptr(q), rows, B, H, Hkv, Dh, ptr(kc), ptr(vc), cache_len, ptr(pos), ptr(out))
+    for b in range(B):
+        sl = slice(b * rps, (b + 1) * rps)
+        wq, wk, wv = R.rope_kv(qkv[sl], H, Hkv, Dh, pos0[b], 1e4)
+        assert rel(q[sl], wq) < 2e-3
+        ref_k, ref_v = kc0[b].clone(), vc0[b].clone()
+        ref_k[:, pos0[b]:pos0[b] + rps] = wk.transpose(0, 1)
+        ref_v[:, pos0[b]:pos0[b] + rps] = wv.transpose(0, 1)
+        assert rel(kc[b], ref_k) < 2e-3 and torch.equal(vc[b], ref_v)
+        want = R.attention(q[sl], kc[b], vc[b], pos0[b], H, Hkv)
+        assert (out[sl].float() - want).abs().max().item() < 2e-3 * max(1.0, want.abs().max().item())
+
+
+def test_short_conv_batched_states():
+    B, rps, D, W = 2, 5, 256, 3
+    g = gen(5)
+    bcx = torch.randn((B * rps, 3 * D), generator=g, device="cuda")
+    w = torch.randn((D, W), generator=g, device="cuda") * 0.3
+    state = torch.randn((B, W - 1, D), generator=g, device="cuda").half()
+    st0 = state.clone()
+    out = torch.empty((B * rps, D), dtype=torch.float16, device="cuda")
+    call(lib().wg_short_conv, ptr(bcx), B * rps, B, D, W, ptr(w), ptr(state), ptr(out), WG_F16)
+    for b in range(B):
+        want, want_state = R.short_conv(bcx[b * rps:(b + 1) * rps], D, W, w, st0[b])
+        assert rel(out[b * rps:(b + 1) * rps], want) < 2e-3
+        assert rel(state[b], want_state) < 1e-3
+
+
+def test_head_rmsnorm_shards_rows_and_keys():
+    """Two vocabulary shards of one head over 3 strided rows: the int64 MAX of
+    the shards' keys picks the full head's argmax; pick_keys decodes it."""
+    from webgllm_b200 import tp as TP
+
+    rows, stride, D, V = 3, 4, 512, 3000
+    g = gen(77)
+    resid = torch.randn((rows * stride, D), generator=g, device="cuda")
+    add = torch.randn((rows * stride, D), generator=g, device="cuda")
+    w = torch.rand(D, generator=g, device="cuda") + 0.5
+    W = (torch.randn((V, D), generator=g, device="cuda") * 0.05).half()
+    _, h = R.rmsnorm(resid[stride - 1::stride], add[stride - 1::stride], w, 1e-5)
+    full = h.half().float() @ W.float().t()
+    keys = []
+    for k0, k1 in [(0, 1700), (1700, 3000)]:
+        lg = torch.empty((rows, k1 - k0), device="cuda")
+        key = torch.empty(rows, dtype=torch.int64, device="cuda")
+        ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+        Ws = W[k0:k1].contiguous()
+        call(lib().wg_head_rmsnorm, ptr(resid[stride - 1]), ptr(add[stride - 1]), ptr(w), ctypes.c_float(1e-5), rows,
+             stride, D, ptr(Ws), k1 - k0, k0, ptr(lg), ptr(ids), ptr(key))
+        assert rel(lg, full[:, k0:k1]) < 2e-3
+        assert torch.equal(ids.long(), lg.argmax(dim=1) + k0)  # global indices
+        for r in range(rows):
+            v = lg[r, ids[r] - k0].item()
+            assert key[r].item() == TP.argmax_key(v, ids[r].item())
+        keys.append(key)
+    best = torch.maximum(keys[0], keys[1])
+    picked = torch.empty(rows, dtype=torch.int32, device="cuda")
+    call(lib().wg_pick_keys, ptr(best), rows, ptr(picked))
+    got_full = torch.cat([full[:, :1700], full[:, 1700:]], dim=1)
+    assert torch.equal(picked.long(), got_full.argmax(dim=1))
 
 
 @pytest.mark.parametrize("rows,I,dt", [(1, 5632, WG_F16), (33, 4608, WG_F16), (2, 100, WG_F32)])
@@ -167,7 +245,7 @@ def test_short_conv_and_state(rows, D, W):
     state = torch.randn((max(W - 1, 1), D), generator=g, device="cuda").half()
     st0 = state.clone()
     out = torch.empty((rows, D), dtype=torch.float16, device="cuda")
-    call(lib().wg_short_conv, ptr(bcx), rows, D, W, ptr(w), ptr(state), ptr(out), WG_F16)
+    call(lib().wg_short_conv, ptr(bcx), rows, 1, D, W, ptr(w), ptr(state), ptr(out), WG_F16)
     want, want_state = R.short_conv(bcx, D, W, w, st0[: W - 1] if W > 1 else st0[:0])
     assert rel(out, want) < 2e-3
     if W > 1:
@@ -175,7 +253,7 @@ def test_short_conv_and_state(rows, D, W):
     # a second call continues from the state: same as one call over both
     bcx2 = torch.randn((3, 3 * D), generator=g, device="cuda")
     out2 = torch.empty((3, D), dtype=torch.float16, device="cuda")
-    call(lib().wg_short_conv, ptr(bcx2), 3, D, W, ptr(w), ptr(state), ptr(out2), WG_F16)
+    call(lib().wg_short_conv, ptr(bcx2), 3, 1, D, W, ptr(w), ptr(state), ptr(out2), WG_F16)
     both, _ = R.short_conv(torch.cat([bcx, bcx2]), D, W, w, st0[: W - 1] if W > 1 else st0[:0])
     assert rel(out2, both[rows:]) < 2e-3
 
@@ -221,8 +299,8 @@ def test_head_rmsnorm_is_norm_then_head(rows, D, V, with_add):
     r0 = resid.clone()
     logits = torch.empty((rows, V), device="cuda")
     ids = torch.empty(rows, dtype=torch.int32, device="cuda")
-    call(lib().wg_head_rmsnorm, ptr(resid), ptr(add), ptr(w), ctypes.c_float(1e-5), rows, D, ptr(W), V, ptr(logits),
-         ptr(ids))
+    call(lib().wg_head_rmsnorm, ptr(resid), ptr(add), ptr(w), ctypes.c_float(1e-5), rows, 1, D, ptr(W), V, 0,
+         ptr(logits), ptr(ids), None)
     assert torch.equal(resid, r0)  # not written
     _, h = R.rmsnorm(r0, add, w, 1e-5)
     want = h.half().float() @ W.float().t()
@@ -246,19 +324,26 @@ def test_head_fused_argmax_ties_pick_the_lowest_index():
 
 def test_add_i32():
     c = torch.tensor([41], dtype=torch.int32, device="cuda")
-    call(lib().wg_add_i32, ptr(c), 1)
-    call(lib().wg_add_i32, ptr(c), -2)
+    call(lib().wg_add_i32, ptr(c), 1, 1)
+    call(lib().wg_add_i32, ptr(c), 1, -2)
     assert c.item() == 40
+    v = torch.arange(100, dtype=torch.int32, device="cuda")
+    call(lib().wg_add_i32, ptr(v), 100, 7)
+    assert torch.equal(v, torch.arange(100, dtype=torch.int32, device="cuda") + 7)
 
 
 def test_decoder_shape_errors():
     c = ctx()
     x = torch.zeros(16, device="cuda")
-    assert lib().wg_attention(P(c.handle), ptr(x), 1, 33, 4, 64, ptr(x), ptr(x), 8, ptr(x), ptr(x)) == _lib.WG_INVALID_SHAPE
+    assert lib().wg_attention(P(c.handle), ptr(x), 1, 1, 33, 4, 64, ptr(x), ptr(x), 8, ptr(x), ptr(x)) == \
+        _lib.WG_INVALID_SHAPE
+    assert lib().wg_attention(P(c.handle), ptr(x), 3, 2, 8, 4, 64, ptr(x), ptr(x), 8, ptr(x), ptr(x)) == \
+        _lib.WG_INVALID_SHAPE  # rows not a multiple of batch
     assert lib().wg_head(P(c.handle), ptr(x), 9, 64, ptr(x), 10, ptr(x), None) == _lib.WG_INVALID_SHAPE
-    assert lib().wg_rope_kv(P(c.handle), ptr(x), 1, 4, 2, 48, ptr(x), ctypes.c_float(1e4), None, None,
+    assert lib().wg_rope_kv(P(c.handle), ptr(x), 1, 1, 4, 2, 48, ptr(x), ctypes.c_float(1e4), None, None,
                             ctypes.c_float(1e-5), ptr(x), ptr(x), ptr(x), 8) == _lib.WG_INVALID_SHAPE
-    assert lib().wg_short_conv(P(c.handle), ptr(x), 1, 4, 9, ptr(x), ptr(x), ptr(x), WG_F16) == _lib.WG_INVALID_SHAPE
+    assert lib().wg_short_conv(P(c.handle), ptr(x), 1, 1, 4, 9, ptr(x), ptr(x), ptr(x), WG_F16) == \
+        _lib.WG_INVALID_SHAPE
 
 
 # ------------------------------------------------------------------ a whole decoder
@@ -311,6 +396,35 @@ def test_decoder_matches_reference_forward(hybrid, fused):
         # both continue from the library's token
         tok = m.next_id.clone()
     assert m.pos.item() == 40 + 6
+
+
+@pytest.mark.parametrize("hybrid", [False, True])
+def test_decoder_batched_sequences_match_single_runs(hybrid):
+    """Two sequences decoding together (per-sequence positions, caches and
+    conv states) give each sequence's single-sequence reference logits."""
+    from webgllm_b200.model import DecoderModel
+
+    cfg = small_config(hybrid)
+    m = DecoderModel(cfg, seed=5, max_ctx=128, max_rows=64, keep_blocks=True, batch=2)
+    refs = [R.ReferenceDecoder(m), R.ReferenceDecoder(m)]
+    prompts = torch.randint(0, cfg.vocab, (2, 20), generator=gen(4), device="cuda").to(torch.int32)
+    m.prefill(prompts)
+    torch.cuda.synchronize()
+    for b in range(2):
+        want = refs[b].forward(prompts[b])
+        assert (m.logits[b] - want).abs().max().item() < 2e-2 * want.abs().max().item(), b
+    toks = m.next_id.clone()
+    m.decode_step()
+    m.capture_decode()
+    for step in range(4):
+        if step:
+            m.graph.replay()
+        torch.cuda.synchronize()
+        for b in range(2):
+            want = refs[b].forward(toks[b:b + 1])
+            assert (m.logits[b] - want).abs().max().item() < 2e-2 * want.abs().max().item(), (step, b)
+        toks = m.next_id.clone()
+    assert m.pos.tolist() == [20 + 4, 20 + 4]
 
 
 # ------------------------------------------------------------------ fused matmul prologues

@@ -1,0 +1,88 @@
+"""Tensor parallelism on 2 GPUs (NCCL): a random-init decoder split across
+two ranks (webgllm_b200.tp) decodes the same greedy tokens as the unsharded
+model on one GPU, with logits (the two vocabulary shards side by side)
+within 2% of their scale, through prefill (GEMM), eager decode and CUDA-graph
+replays that contain the NCCL all-reduces. Needs >= 2 GPUs; skipped
+otherwise."""
+import os
+import random
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:  # pragma: no cover
+    pytest.skip("needs 2 CUDA GPUs", allow_module_level=True)
+
+import datetime  # noqa: E402
+
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+
+def _cfg():
+    from webgllm_b200.model import DecoderConfig
+
+    return DecoderConfig("tiny-tp", 3, 512, 8, 4, 64, 1024, 1000, 1e-5, 1e4)
+
+
+def _run(model, prompts, steps):
+    toks, logits = [], []
+    model.prefill(prompts)
+    toks.append(model.next_id.clone())
+    logits.append(model.logits.clone())
+    model.decode_step()
+    toks.append(model.next_id.clone())
+    logits.append(model.logits.clone())
+    model.capture_decode()
+    for _ in range(steps):
+        model.graph.replay()
+        toks.append(model.next_id.clone())
+        logits.append(model.logits.clone())
+    torch.cuda.synchronize()
+    return toks, logits
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from webgllm_b200.model import DecoderModel
+
+        cfg = _cfg()
+        m = DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=2, tp=(rank, world, None))
+        prompts = torch.randint(0, cfg.vocab, (2, 24), generator=torch.Generator().manual_seed(3)).cuda()
+        toks, logits = _run(m, prompts, 4)
+        # both vocabulary shards, side by side
+        full = []
+        for lg in logits:
+            parts = [torch.zeros_like(lg) for _ in range(world)]
+            dist.all_gather(parts, lg)
+            full.append(torch.cat(parts, dim=1))
+        m.graph = None
+        if rank == 0:
+            single = DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=2)
+            stoks, slog = _run(single, prompts, 4)
+            errs = [((a - b).abs().max() / b.abs().max()).item() for a, b in zip(full, slog)]
+            same = [torch.equal(a, b) for a, b in zip(toks, stoks)]
+            q.put((max(errs), same))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_decodes_like_one_gpu():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + random.Random().randrange(0, 2000)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    err, same = q.get(timeout=10)
+    assert err < 2e-2, err
+    assert all(same), same

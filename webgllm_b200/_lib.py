@@ -64,14 +64,15 @@ SIGNATURES = {
     # include/webgllm_decoder.h
     "wg_embed": (_I, [_P, _P, _I, _P, _I, _I, _P]),
     "wg_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _P, _I]),
-    "wg_rope_kv": (_I, [_P, _P, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, ctypes.c_float, _P, _P, _P, _I]),
-    "wg_attention": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _I, _P, _P]),
+    "wg_rope_kv": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, ctypes.c_float, _P, _P, _P, _I]),
+    "wg_attention": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P]),
     "wg_swiglu": (_I, [_P, _P, _I, _I, _P, _I]),
-    "wg_short_conv": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _I]),
+    "wg_short_conv": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
     "wg_head": (_I, [_P, _P, _I, _I, _P, _I, _P, _P]),
-    "wg_head_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _P, _I, _P, _P]),
+    "wg_head_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _I, _P, _I, _I, _P, _P, _P]),
+    "wg_pick_keys": (_I, [_P, _P, _I, _P]),
     "wg_argmax": (_I, [_P, _P, _I, _I, _P]),
-    "wg_add_i32": (_I, [_P, _P, _I]),
+    "wg_add_i32": (_I, [_P, _P, _I, _I]),
     "wg_error_string": (ctypes.c_char_p, [_I]),
     "wg_last_error": (ctypes.c_char_p, [_P]),
 }

@@ -62,21 +62,28 @@ int wg_rmsnorm(wg_ctx *ctx, float *x, const float *add, const float *weight, flo
   return finish(ctx, wg::launch_rmsnorm(x, add, weight, eps, rows, D, out, out_dtype, ctx->stream, ctx->pdl), "wg_rmsnorm");
 }
 
-int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int H, int Hkv, int Dh, const int32_t *pos, float theta,
-               const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache, void *v_cache,
-               int cache_len) {
+static int check_batch(wg_ctx *ctx, const char *what, int rows, int batch) {
+  if (batch <= 0 || rows % batch)
+    return dfail(ctx, WG_INVALID_SHAPE, "%s: rows (%d) must be a positive multiple of batch (%d)", what, rows, batch);
+  return WG_OK;
+}
+
+int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int batch, int H, int Hkv, int Dh, const int32_t *pos,
+               float theta, const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache,
+               void *v_cache, int cache_len) {
   WG_BEGIN(ctx);
-  if (rows < 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh <= 0 || Dh % 64 || cache_len <= 0)
+  if (rows < 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh <= 0 || Dh % 64 || Dh > 2048 || cache_len <= 0)
     return dfail(ctx, WG_INVALID_SHAPE, "wg_rope_kv: bad shape (H %d, Hkv %d, Dh %d)", H, Hkv, Dh);
   if (!rows) return WG_OK;
+  if (int st = check_batch(ctx, "wg_rope_kv", rows, batch)) return st;
   if (!qkv || !pos || !q_out || !k_cache || !v_cache) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_rope_kv: null");
   return finish(ctx,
-                wg::launch_rope_kv(qkv, rows, H, Hkv, Dh, pos, theta, q_norm, k_norm, eps, q_out, k_cache, v_cache,
-                                   cache_len, ctx->d_flags, ctx->stream, ctx->pdl),
+                wg::launch_rope_kv(qkv, rows, batch, H, Hkv, Dh, pos, theta, q_norm, k_norm, eps, q_out, k_cache,
+                                   v_cache, cache_len, ctx->d_flags, ctx->stream, ctx->pdl),
                 "wg_rope_kv");
 }
 
-int wg_attention(wg_ctx *ctx, const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
+int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                  const void *v_cache, int cache_len, const int32_t *pos, void *out) {
   WG_BEGIN(ctx);
   if (rows < 0 || H <= 0 || Hkv <= 0 || H % Hkv || H / Hkv > 16 ||
@@ -84,8 +91,11 @@ int wg_attention(wg_ctx *ctx, const void *q, int rows, int H, int Hkv, int Dh, c
     return dfail(ctx, WG_INVALID_SHAPE, "wg_attention: bad shape (H %d, Hkv %d, Dh %d, cache_len %d)", H, Hkv, Dh,
                  cache_len);
   if (!rows) return WG_OK;
+  if (int st = check_batch(ctx, "wg_attention", rows, batch)) return st;
   if (!q || !k_cache || !v_cache || !pos || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_attention: null");
-  return finish(ctx, wg::launch_attention(q, rows, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->stream, ctx->pdl),
+  return finish(ctx,
+                wg::launch_attention(q, rows, batch, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->stream,
+                                     ctx->pdl),
                 "wg_attention");
 }
 
@@ -97,42 +107,61 @@ int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int
   return finish(ctx, wg::launch_swiglu(gate_up, rows, I, out, out_dtype, ctx->stream, ctx->pdl), "wg_swiglu");
 }
 
-int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int D, int W, const float *weight, void *state,
-                  void *out, int out_dtype) {
+int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int batch, int D, int W, const float *weight,
+                  void *state, void *out, int out_dtype) {
   WG_BEGIN(ctx);
   if (rows < 0 || D <= 0 || W < 1 || W > 8) return dfail(ctx, WG_INVALID_SHAPE, "wg_short_conv: bad shape");
   if (!rows) return WG_OK;
+  if (int st = check_batch(ctx, "wg_short_conv", rows, batch)) return st;
   if (!bcx || !weight || !state || !out || !dtype_ok(out_dtype))
     return dfail(ctx, WG_INVALID_ARGUMENT, "wg_short_conv: argument");
-  return finish(ctx, wg::launch_short_conv(bcx, rows, D, W, weight, state, out, out_dtype, ctx->stream, ctx->pdl),
+  return finish(ctx,
+                wg::launch_short_conv(bcx, rows, batch, D, W, weight, state, out, out_dtype, ctx->stream, ctx->pdl),
                 "wg_short_conv");
+}
+
+static int check_head(wg_ctx *ctx, int rows, int D, int V) {
+  if (rows < 0 || rows > 8 || D <= 0 || D % 8 || V <= 0 || (size_t)rows * D * 4 > 200 * 1024)
+    return dfail(ctx, WG_INVALID_SHAPE, "head: rows %d (<= 8), D %d (multiple of 8, rows * D <= 51200)", rows, D);
+  return WG_OK;
 }
 
 int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, float *logits, int32_t *argmax) {
   WG_BEGIN(ctx);
-  if (rows < 0 || rows > 8 || D <= 0 || D % 8 || V <= 0 || (size_t)rows * D * 4 > 200 * 1024)
-    return dfail(ctx, WG_INVALID_SHAPE, "wg_head: rows %d (<= 8), D %d (multiple of 8, rows * D <= 51200)", rows,
-                 D);
+  if (int st = check_head(ctx, rows, D, V)) return st;
   if (!rows) return WG_OK;
   if (!x || !W || !logits) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_head: null");
   return finish(ctx,
-                wg::launch_head(x, nullptr, nullptr, nullptr, 0.0f, rows, D, W, V, logits, argmax, ctx->d_reduce,
-                                wg::kReduceBytes, ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
+                wg::launch_head(x, nullptr, nullptr, nullptr, 0.0f, rows, 1, D, W, V, 0, logits, argmax, nullptr,
+                                ctx->d_reduce, wg::kReduceBytes, ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
                 "wg_head");
 }
 
 int wg_head_rmsnorm(wg_ctx *ctx, const float *resid, const float *add, const float *weight, float eps, int rows,
-                    int D, const void *W, int V, float *logits, int32_t *argmax) {
+                    int row_stride, int D, const void *W, int V, int vocab_offset, float *logits, int32_t *argmax,
+                    int64_t *keys) {
   WG_BEGIN(ctx);
-  if (rows < 0 || rows > 8 || D <= 0 || D % 8 || V <= 0 || (size_t)rows * D * 4 > 200 * 1024)
-    return dfail(ctx, WG_INVALID_SHAPE, "wg_head_rmsnorm: rows %d (<= 8), D %d (multiple of 8, rows * D <= 51200)",
-                 rows, D);
+  if (int st = check_head(ctx, rows, D, V)) return st;
+  if (row_stride < 1 || vocab_offset < 0)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_head_rmsnorm: row_stride %d, vocab_offset %d", row_stride, vocab_offset);
   if (!rows) return WG_OK;
   if (!resid || !weight || !W || !logits) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_head_rmsnorm: null");
   return finish(ctx,
-                wg::launch_head(nullptr, resid, add, weight, eps, rows, D, W, V, logits, argmax, ctx->d_reduce,
-                                wg::kReduceBytes, ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
+                wg::launch_head(nullptr, resid, add, weight, eps, rows, row_stride, D, W, V, vocab_offset, logits,
+                                argmax, reinterpret_cast<unsigned long long *>(keys), ctx->d_reduce, wg::kReduceBytes,
+                                ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
                 "wg_head_rmsnorm");
+}
+
+int wg_pick_keys(wg_ctx *ctx, const int64_t *keys, int rows, int32_t *ids) {
+  WG_BEGIN(ctx);
+  if (rows < 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_pick_keys: rows %d", rows);
+  if (!rows) return WG_OK;
+  if (!keys || !ids) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_pick_keys: null");
+  return finish(ctx,
+                wg::launch_pick_keys(reinterpret_cast<const unsigned long long *>(keys), rows, ids, ctx->stream,
+                                     ctx->pdl),
+                "wg_pick_keys");
 }
 
 int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out) {
@@ -143,10 +172,12 @@ int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out) {
   return finish(ctx, wg::launch_argmax(logits, rows, V, out, ctx->stream, ctx->pdl), "wg_argmax");
 }
 
-int wg_add_i32(wg_ctx *ctx, int32_t *counter, int delta) {
+int wg_add_i32(wg_ctx *ctx, int32_t *counters, int n, int delta) {
   WG_BEGIN(ctx);
-  if (!counter) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_add_i32: null");
-  return finish(ctx, wg::launch_add_i32(counter, delta, ctx->stream, ctx->pdl), "wg_add_i32");
+  if (n < 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_add_i32: n %d", n);
+  if (!n) return WG_OK;
+  if (!counters) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_add_i32: null");
+  return finish(ctx, wg::launch_add_i32(counters, n, delta, ctx->stream, ctx->pdl), "wg_add_i32");
 }
 
 }  // extern "C"

@@ -79,7 +79,7 @@ __global__ void rmsnorm_kernel(float *x, const float *add, const float *w, float
 // H + Hkv), Dh/2 threads: thread j rotates the pair (j, j + Dh/2) by
 // pos * theta^(-2j/Dh) (rotate-half). Queries leave scaled by 1/sqrt(Dh).
 
-__global__ void rope_kv_kernel(const float *qkv, int H, int Hkv, int Dh, const int *pos0, float theta,
+__global__ void rope_kv_kernel(const float *qkv, int rps, int H, int Hkv, int Dh, const int *pos0, float theta,
                                const float *q_norm, const float *k_norm, float eps, __half *q_out,
                                __half *k_cache, __half *v_cache, int cache_len, unsigned *flags) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
@@ -87,8 +87,11 @@ __global__ void rope_kv_kernel(const float *qkv, int H, int Hkv, int Dh, const i
   __shared__ float red[32];
   const int r = blockIdx.x, h = blockIdx.y;  // h < H: query head; else kv head h - H
   const int half = Dh / 2, j = threadIdx.x;
-  const int pos = *pos0 + r;
+  const int seq = r / rps;  // sequence of this row (rps rows per sequence)
+  const int pos = pos0[seq] + (r - seq * rps);
   const size_t row = (size_t)r * (H + 2 * Hkv) * Dh;
+  k_cache += (size_t)seq * Hkv * cache_len * Dh;
+  v_cache += (size_t)seq * Hkv * cache_len * Dh;
   const bool is_q = h < H;
   const int hk = h - H;
   const float *src = qkv + row + (size_t)(is_q ? h : H + hk) * Dh;
@@ -213,8 +216,8 @@ __device__ __forceinline__ void load_halves(const __half *p, float v[DPL]) {
 
 template <int DPL>  // head dims per lane: Dh = 32 * DPL
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThreads)
-    attention_kernel(const __half *q, int H, int Hkv, const __half *k_cache, const __half *v_cache, int cache_len,
-                     const int *pos0, __half *out) {
+    attention_kernel(const __half *q, int rps, int H, int Hkv, const __half *k_cache, const __half *v_cache,
+                     int cache_len, const int *pos0, __half *out) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
   pdl_wait();     // inputs come from the previous kernel
   constexpr int Dh = 32 * DPL;
@@ -239,7 +242,8 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
   const int c = (int)cluster.block_rank();
   const int hk = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int L = max(0, min(*pos0 + r + 1, cache_len));
+  const int bseq = r / rps;  // sequence of this query row (rps rows per sequence)
+  const int L = max(0, min(pos0[bseq] + (r - bseq * rps) + 1, cache_len));
   const int per = (L + kAttnCluster - 1) / kAttnCluster;
   const int t0 = min(L, c * per), t1 = min(L, t0 + per);
 
@@ -252,8 +256,8 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
   }
   for (int i = tid; i < G * Dh; i += kAttnThreads) sacc[i] = 0.0f;
 
-  const __half *kb = k_cache + (size_t)hk * cache_len * Dh;
-  const __half *vb = v_cache + (size_t)hk * cache_len * Dh;
+  const __half *kb = k_cache + ((size_t)bseq * Hkv + hk) * cache_len * Dh;
+  const __half *vb = v_cache + ((size_t)bseq * Hkv + hk) * cache_len * Dh;
   for (int tt = t0; tt < t1; tt += kAttnTile) {
     const int nt = min(kAttnTile, t1 - tt);
     __syncthreads();  // previous tile fully consumed
@@ -399,13 +403,18 @@ __global__ void swiglu_kernel(const float *gu, int rows, int I, void *out, int o
 constexpr int kMaxConvWidth = 8;
 constexpr int kConvRows = 16;
 
-__global__ void short_conv_kernel(const float *bcx, int rows, int D, int W, const float *w, __half *state,
+__global__ void short_conv_kernel(const float *bcx, int rows, int cps, int D, int W, const float *w, __half *state,
                                   void *out, int out_dtype) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
   pdl_wait();     // inputs come from the previous kernel
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= D) return;
-  const int r0 = blockIdx.y * kConvRows;
+  // this block's sequence (rows consecutive rows each) and its row chunk
+  const int seq = blockIdx.y / cps, chunk = blockIdx.y - seq * cps;
+  bcx += (size_t)seq * rows * 3 * D;
+  state += (size_t)seq * (W - 1) * D;
+  out = reinterpret_cast<uint8_t *>(out) + (size_t)seq * rows * D * (out_dtype == WG_F32 ? 4 : 2);
+  const int r0 = chunk * kConvRows;
   const int nr = min(kConvRows, rows - r0);
   // y over rows r0 - (W-1) .. r0 + nr - 1
   float y[kConvRows + kMaxConvWidth - 1];
@@ -436,7 +445,7 @@ __global__ void short_conv_kernel(const float *bcx, int rows, int D, int W, cons
       if (k < W) a += wk[k] * y[i + k];
     store_out(out, out_dtype, (size_t)(r0 + i) * D + c, cg_[i] * a);
   }
-  if (blockIdx.y == 0 && W > 1) {
+  if (chunk == 0 && W > 1) {
     // new state: y at rows rows-(W-1) .. rows-1 (old state for negative rows)
     float ns[kMaxConvWidth];
 #pragma unroll
@@ -469,8 +478,8 @@ constexpr int kHeadThreads = 256;
 constexpr int kHeadUnroll = 8;  // 16-byte loads in flight per lane (a 4 KB row per warp)
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
-  // larger logit first, then the lower index
-  unsigned u = __float_as_uint(v);
+  // larger logit first, then the lower index (-0 counts as +0)
+  unsigned u = __float_as_uint(v == 0.0f ? 0.0f : v);
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   return ((unsigned long long)u << 32) | (unsigned)(0xffffffffu - (unsigned)idx);
 }
@@ -485,8 +494,9 @@ struct HeadNorm {
 
 template <bool NORM, int kHeadMaxRows>  // kHeadMaxRows: 1 (decode) or 8
 __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
-    head_kernel(const __half *x, HeadNorm nrm, int rows, int D, const __half *W, int V, float *logits, int32_t *amax,
-                unsigned long long *part, unsigned *count) {
+    head_kernel(const __half *x, HeadNorm nrm, int rows, int row_stride, int D, const __half *W, int V,
+                int vocab_offset, float *logits, int32_t *amax, unsigned long long *keys, unsigned long long *part,
+                unsigned *count) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
   pdl_wait();     // inputs come from the previous kernel
   extern __shared__ float xs[];  // [rows][D]
@@ -496,9 +506,10 @@ __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
     __shared__ float red[32];
     for (int r = 0; r < rows; r++) {
       float ss = 0.0f;
+      const size_t src = (size_t)r * row_stride * D;
       for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        float v = nrm.a[(size_t)r * D + i];
-        if (nrm.b) v += nrm.b[(size_t)r * D + i];
+        float v = nrm.a[src + i];
+        if (nrm.b) v += nrm.b[src + i];
         xs[r * D + i] = v;
         ss += v * v;
       }
@@ -507,7 +518,10 @@ __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
         xs[r * D + i] = __half2float(__float2half_rn(clamp_half(xs[r * D + i] * inv * nrm.w[i])));
     }
   } else {
-    for (int i = threadIdx.x; i < rows * D; i += blockDim.x) xs[i] = __half2float(x[i]);
+    for (int i = threadIdx.x; i < rows * D; i += blockDim.x) {
+      const int r = i / D;
+      xs[i] = __half2float(x[(size_t)r * row_stride * D + (i - r * D)]);
+    }
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -525,13 +539,14 @@ __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
     float acc[kHeadMaxRows];
 #pragma unroll
     for (int r = 0; r < kHeadMaxRows; r++) acc[r] = 0.0f;
-    for (int c0 = lane; c0 < nvec; c0 += 32 * kHeadUnroll) {
-      uint4 u[kHeadUnroll];
+    constexpr int U = kHeadMaxRows > 1 ? kHeadUnroll / 2 : kHeadUnroll;  // registers for 8 rows
+    for (int c0 = lane; c0 < nvec; c0 += 32 * U) {
+      uint4 u[U];
 #pragma unroll
-      for (int j = 0; j < kHeadUnroll; j++)
+      for (int j = 0; j < U; j++)
         if (c0 + 32 * j < nvec) u[j] = __ldcs(wr + c0 + 32 * j);  // read once: stream past L2
 #pragma unroll
-      for (int j = 0; j < kHeadUnroll; j++) {
+      for (int j = 0; j < U; j++) {
         const int c = c0 + 32 * j;
         if (c >= nvec) break;
         const __half2 *hp = reinterpret_cast<const __half2 *>(&u[j]);
@@ -563,11 +578,11 @@ __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
       }
     }
   }
-  if (!amax) return;
+  if (!amax && !keys) return;
   if (lane == 0) {
 #pragma unroll
     for (int r = 0; r < kHeadMaxRows; r++)
-      if (r < rows) s_key[warp][r] = argmax_key(bv[r], bi[r]);
+      if (r < rows) s_key[warp][r] = argmax_key(bv[r], vocab_offset + bi[r]);
   }
   __syncthreads();
   if (threadIdx.x < rows) {
@@ -592,7 +607,8 @@ __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
     if (threadIdx.x == 0) {
       unsigned long long kk = 0;
       for (int w = 0; w < warps; w++) kk = max(kk, s_key[w][0]);
-      amax[r] = (int32_t)(0xffffffffu - (unsigned)(kk & 0xffffffffu));
+      if (amax) amax[r] = (int32_t)(0xffffffffu - (unsigned)(kk & 0xffffffffu));
+      if (keys) keys[r] = kk ^ 0x8000000000000000ull;  // signed-orderable: an int64 MAX picks it
     }
     __syncthreads();
   }
@@ -640,10 +656,19 @@ __global__ void argmax_kernel(const float *logits, int V, int32_t *out) {
   }
 }
 
-__global__ void add_i32_kernel(int32_t *p, int delta) {
+// Token ids from packed (logit, index) keys (after a max-reduction of the
+// keys across vocabulary shards).
+__global__ void pick_keys_kernel(const unsigned long long *keys, int rows, int32_t *ids) {
+  pdl_trigger();
+  pdl_wait();
+  for (int i = threadIdx.x; i < rows; i += blockDim.x)
+    ids[i] = (int32_t)(0xffffffffu - (unsigned)((unsigned long long)keys[i] & 0xffffffffu));
+}
+
+__global__ void add_i32_kernel(int32_t *p, int n, int delta) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
   pdl_wait();     // inputs come from the previous kernel
-  *p += delta;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] += delta;
 }
 
 // Launch with programmatic dependent launch when `pdl`: the kernel may start
@@ -681,17 +706,19 @@ cudaError_t launch_rmsnorm(float *x, const float *add, const float *w, float eps
   return launch_k(rmsnorm_kernel, dim3(rows), dim3(threads), 0, s, pdl, x, add, w, eps, D, out, out_dtype);
 }
 
-cudaError_t launch_rope_kv(const float *qkv, int rows, int H, int Hkv, int Dh, const int *pos0, float theta,
-                           const float *q_norm, const float *k_norm, float eps, void *q_out, void *k_cache,
-                           void *v_cache, int cache_len, unsigned *flags, cudaStream_t s, bool pdl) {
-  return launch_k(rope_kv_kernel, dim3(rows, H + Hkv), dim3(Dh / 2), 0, s, pdl, qkv, H, Hkv, Dh, pos0, theta, q_norm,
+cudaError_t launch_rope_kv(const float *qkv, int rows, int batch, int H, int Hkv, int Dh, const int *pos0,
+                           float theta, const float *q_norm, const float *k_norm, float eps, void *q_out,
+                           void *k_cache, void *v_cache, int cache_len, unsigned *flags, cudaStream_t s, bool pdl) {
+  return launch_k(rope_kv_kernel, dim3(rows, H + Hkv), dim3(Dh / 2), 0, s, pdl, qkv, rows / batch, H, Hkv, Dh, pos0,
+                  theta, q_norm,
                   k_norm, eps, reinterpret_cast<__half *>(q_out), reinterpret_cast<__half *>(k_cache),
                   reinterpret_cast<__half *>(v_cache), cache_len, flags);
 }
 
 template <int DPL>
-cudaError_t launch_attention_t(const void *q, int rows, int H, int Hkv, const void *k_cache, const void *v_cache,
-                               int cache_len, const int *pos0, void *out, cudaStream_t s, bool pdl) {
+cudaError_t launch_attention_t(const void *q, int rows, int rps, int H, int Hkv, const void *k_cache,
+                               const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s,
+                               bool pdl) {
   const AttnSmem lay(32 * DPL, H / Hkv);
   const size_t smem = lay.total;
   auto kern = attention_kernel<DPL>;
@@ -700,19 +727,20 @@ cudaError_t launch_attention_t(const void *q, int rows, int H, int Hkv, const vo
     if (e != cudaSuccess) return e;
   }
   return launch_k(kern, dim3(kAttnCluster, Hkv, rows), dim3(kAttnThreads), smem, s, pdl,
-                  reinterpret_cast<const __half *>(q), H, Hkv, reinterpret_cast<const __half *>(k_cache),
+                  reinterpret_cast<const __half *>(q), rps, H, Hkv, reinterpret_cast<const __half *>(k_cache),
                   reinterpret_cast<const __half *>(v_cache), cache_len, pos0, reinterpret_cast<__half *>(out));
 }
 
-cudaError_t launch_attention(const void *q, int rows, int H, int Hkv, int Dh, const void *k_cache,
+cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                              const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s,
                              bool pdl) {
   if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
+  const int rps = rows / batch;
   switch (Dh) {
-    case 32: return launch_attention_t<1>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
-    case 64: return launch_attention_t<2>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
-    case 128: return launch_attention_t<4>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
-    case 256: return launch_attention_t<8>(q, rows, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 32: return launch_attention_t<1>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 64: return launch_attention_t<2>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 128: return launch_attention_t<4>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 256: return launch_attention_t<8>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -724,17 +752,19 @@ cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_d
                   out_dtype);
 }
 
-cudaError_t launch_short_conv(const float *bcx, int rows, int D, int W, const float *w, void *state, void *out,
-                              int out_dtype, cudaStream_t s, bool pdl) {
+cudaError_t launch_short_conv(const float *bcx, int rows, int batch, int D, int W, const float *w, void *state,
+                              void *out, int out_dtype, cudaStream_t s, bool pdl) {
   if (W < 1 || W > kMaxConvWidth) return cudaErrorInvalidValue;
-  const dim3 grid((D + 127) / 128, (rows + kConvRows - 1) / kConvRows);
-  return launch_k(short_conv_kernel, grid, dim3(128), 0, s, pdl, bcx, rows, D, W, w,
+  const int rps = rows / batch, cps = (rps + kConvRows - 1) / kConvRows;
+  const dim3 grid((D + 127) / 128, batch * cps);
+  return launch_k(short_conv_kernel, grid, dim3(128), 0, s, pdl, bcx, rps, cps, D, W, w,
                   reinterpret_cast<__half *>(state), out, out_dtype);
 }
 
-cudaError_t launch_head(const void *x, const float *na, const float *nb, const float *nw, float eps, int rows, int D,
-                        const void *W, int V, float *logits, int32_t *amax, unsigned long long *part,
-                        size_t part_bytes, unsigned *count, int num_sms, cudaStream_t s, bool pdl) {
+cudaError_t launch_head(const void *x, const float *na, const float *nb, const float *nw, float eps, int rows,
+                        int row_stride, int D, const void *W, int V, int vocab_offset, float *logits, int32_t *amax,
+                        unsigned long long *keys, unsigned long long *part, size_t part_bytes, unsigned *count,
+                        int num_sms, cudaStream_t s, bool pdl) {
   if (rows > kHeadMaxRows || D % 8) return cudaErrorInvalidValue;
   const size_t smem = (size_t)rows * D * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
@@ -750,15 +780,21 @@ cudaError_t launch_head(const void *x, const float *na, const float *nb, const f
   if (grid > max_grid) grid = max_grid;
   const HeadNorm hn{na, nb, nw, eps};
   return launch_k(kern, dim3(grid), dim3(kHeadThreads), smem, s, pdl, reinterpret_cast<const __half *>(x), hn, rows,
-                  D, reinterpret_cast<const __half *>(W), V, logits, amax, part, count);
+                  row_stride, D, reinterpret_cast<const __half *>(W), V, vocab_offset, logits, amax, keys, part,
+                  count);
 }
 
 cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *out, cudaStream_t s, bool pdl) {
   return launch_k(argmax_kernel, dim3(rows), dim3(1024), 0, s, pdl, logits, V, out);
 }
 
-cudaError_t launch_add_i32(int32_t *p, int delta, cudaStream_t s, bool pdl) {
-  return launch_k(add_i32_kernel, dim3(1), dim3(1), 0, s, pdl, p, delta);
+cudaError_t launch_pick_keys(const unsigned long long *keys, int rows, int32_t *ids, cudaStream_t s, bool pdl) {
+  return launch_k(pick_keys_kernel, dim3(1), dim3(rows < 1024 ? ((rows + 31) / 32) * 32 : 1024), 0, s, pdl, keys,
+                  rows, ids);
+}
+
+cudaError_t launch_add_i32(int32_t *p, int n, int delta, cudaStream_t s, bool pdl) {
+  return launch_k(add_i32_kernel, dim3(1), dim3(n < 1024 ? ((n + 31) / 32) * 32 : 1024), 0, s, pdl, p, n, delta);
 }
 
 }  // namespace wg

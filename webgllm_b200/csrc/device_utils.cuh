@@ -1,5 +1,5 @@
 // Device helpers shared by the Q4 kernels: mbarriers with bounded waits,
-// bulk async copies (the TMA engine, no multicast), fp16 bit tricks.
+// bulk async copies (the TMA engine, one destination CTA), fp16 bit tricks.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -65,7 +65,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   return true;
 }
 
-// ---- bulk async copy global -> shared (the TMA engine, no multicast) -----
+// ---- bulk async copy global -> shared (the TMA engine, one destination CTA)
 
 // `bytes` a multiple of 16, both addresses 16-byte aligned.
 __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src, uint32_t bytes, uint64_t *bar) {

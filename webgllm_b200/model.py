@@ -8,9 +8,12 @@ matrix through wg_q4_matmul (decode GEMV or tcgen05 GEMM), the rest through
 include/webgllm_decoder.h. Weights are random (BASELINE: "random init"),
 quantised to Q4_0 by the llama.cpp rule on the device.
 
-A decode step is captured once as a CUDA graph and replayed: the token id
-(argmax) and the position live on the device, so no host round trip is
-needed between tokens.
+A decode step is captured once as a CUDA graph and replayed: the token ids
+(argmax) and the positions live on the device, so no host round trip is
+needed between tokens. `batch` independent sequences decode together (one
+row each), and with `tp` the model is split across the GPUs of a node
+(webgllm_b200.tp): two NCCL all-reduces per layer and one for the greedy
+pick.
 """
 from __future__ import annotations
 
@@ -20,6 +23,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib
+from . import tp as TP
 from .q4 import QuantMatrix, context, newQuantMatrix, packQ4_0
 from ._lib import WG_F16, WG_F32, WG_PRO_RMSNORM, WG_PRO_SWIGLU
 
@@ -90,10 +94,7 @@ def dequantize_q4_0(blocks: torch.Tensor, N: int, K: int) -> torch.Tensor:
 class Linear:
     """A Q4_0 matrix on the device (and its GGUF bytes, for references)."""
 
-    def __init__(self, ctx, N: int, K: int, gen: torch.Generator, std: float = 0.02, keep_blocks=False):
-        w = torch.randn((N, K), generator=gen, device="cuda") * std
-        blocks = quantize_q4_0(w)
-        del w
+    def __init__(self, ctx, blocks: torch.Tensor, N: int, K: int, keep_blocks=False):
         self.N, self.K = N, K
         self.m: QuantMatrix = newQuantMatrix(N, K, ctx=ctx)
         ctx.use_torch_stream()
@@ -102,64 +103,99 @@ class Linear:
         self.blocks = blocks if keep_blocks else None
 
 
+def random_q4(N: int, K: int, gen: torch.Generator, std: float = 0.02) -> torch.Tensor:
+    """GGUF Q4_0 bytes of an N x K matrix drawn from N(0, std^2) (device)."""
+    w = torch.randn((N, K), generator=gen, device="cuda") * std
+    return quantize_q4_0(w)
 
 
 class DecoderModel:
-    """Weights, caches and the forward pass of one decoder on one GPU."""
+    """Weights, caches and the forward pass of one decoder on one GPU (or on
+    this rank's GPU of a tensor-parallel group).
+
+    tp: None, or (rank, world, process_group) of an NCCL group; every rank
+    draws the same full random weights and keeps its shard (webgllm_b200.tp),
+    so the model is the same for every world size."""
 
     def __init__(self, cfg: DecoderConfig, seed: int = 0, max_ctx: int = 1024, max_rows: int = 512,
-                 keep_blocks: bool = False, device: int | None = None, fused: bool = True):
+                 keep_blocks: bool = False, device: int | None = None, fused: bool = True, batch: int = 1,
+                 tp=None):
         self.cfg = cfg
         self.fused = fused
+        self.batch = batch
         self.ctx = context(device)
         self.max_ctx, self.max_rows = max_ctx, max_rows
+        rank, world, self.group = tp if tp else (0, 1, None)
+        self.world = world
+        sh = self.shard = TP.plan(cfg, rank, world) if world > 1 else None
         g = torch.Generator(device="cuda")
         g.manual_seed(seed)
         D, H, Hkv, Dh, I, V = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab
+        self.H = sh.heads if sh else H
+        self.Hkv = sh.kv_heads if sh else Hkv
+        self.I = sh.ffn if sh else I
+        self.V = sh.vocab if sh else V
+        self.vocab_offset = sh.vocab_offset if sh else 0
         self.embed = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
-        self.head = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
+        head = (torch.randn((V, D), generator=g, device="cuda") * 0.02).half()
+        self.head = head[self.vocab_offset:self.vocab_offset + self.V].contiguous()
+        del head
         self.final_norm = torch.ones(D, device="cuda")
         self.layers = []
         n_attn = n_conv = 0
+        kb = keep_blocks
+
+        def lin(N, K, rows=None, cols=None):
+            blocks = random_q4(N, K, g)
+            if rows is not None:
+                blocks, N = TP.q4_rows(blocks, N, K, rows), rows.numel()
+            if cols is not None:
+                blocks, K = TP.q4_cols(blocks, N, K, *cols), cols[1] - cols[0]
+            return Linear(self.ctx, blocks, N, K, kb)
+
         for t in cfg.layer_types:
             L = {"type": t, "norm1": torch.ones(D, device="cuda"), "norm2": torch.ones(D, device="cuda")}
             if t == "attn":
-                L["qkv"] = Linear(self.ctx, (H + 2 * Hkv) * Dh, D, g, keep_blocks=keep_blocks)
-                L["o"] = Linear(self.ctx, D, H * Dh, g, keep_blocks=keep_blocks)
+                L["qkv"] = lin((H + 2 * Hkv) * Dh, D, rows=TP.qkv_rows(cfg, sh) if sh else None)
+                L["o"] = lin(D, H * Dh, cols=TP.o_cols(cfg, sh) if sh else None)
                 if cfg.qk_norm:
                     L["q_norm"] = torch.ones(Dh, device="cuda")
                     L["k_norm"] = torch.ones(Dh, device="cuda")
                 L["slot"] = n_attn
                 n_attn += 1
             else:
-                L["in"] = Linear(self.ctx, 3 * D, D, g, keep_blocks=keep_blocks)
+                L["in"] = lin(3 * D, D)
                 L["conv_w"] = torch.randn((D, cfg.conv_width), generator=g, device="cuda") * 0.1
-                L["out"] = Linear(self.ctx, D, D, g, keep_blocks=keep_blocks)
+                L["out"] = lin(D, D)
                 L["slot"] = n_conv
                 n_conv += 1
-            L["gu"] = Linear(self.ctx, 2 * I, D, g, keep_blocks=keep_blocks)
-            L["down"] = Linear(self.ctx, D, I, g, keep_blocks=keep_blocks)
+            L["gu"] = lin(2 * I, D, rows=TP.gate_up_rows(cfg, sh) if sh else None)
+            L["down"] = lin(D, I, cols=TP.down_cols(cfg, sh) if sh else None)
             self.layers.append(L)
-        self.k_cache = torch.zeros((max(n_attn, 1), Hkv, max_ctx, Dh), dtype=torch.float16, device="cuda")
+        B = batch
+        self.k_cache = torch.zeros((max(n_attn, 1), B, self.Hkv, max_ctx, Dh), dtype=torch.float16, device="cuda")
         self.v_cache = torch.zeros_like(self.k_cache)
-        self.conv_state = torch.zeros((max(n_conv, 1), cfg.conv_width - 1, D), dtype=torch.float16, device="cuda")
+        self.conv_state = torch.zeros((max(n_conv, 1), B, cfg.conv_width - 1, D), dtype=torch.float16,
+                                      device="cuda")
         # activations for up to max_rows rows
         R = max_rows
+        Hl, Hkvl, Il = self.H, self.Hkv, self.I
         self.x = torch.zeros((R, D), device="cuda")                      # residual stream
         self.x2 = torch.zeros((R, D), device="cuda")                     # its other copy (fused path)
         self.h = torch.zeros((R, D), dtype=torch.float16, device="cuda")  # normed input of a matmul
-        self.qkv = torch.zeros((R, (H + 2 * Hkv) * Dh), device="cuda")
-        self.q = torch.zeros((R, H * Dh), dtype=torch.float16, device="cuda")
-        self.att = torch.zeros((R, H * Dh), dtype=torch.float16, device="cuda")
+        self.qkv = torch.zeros((R, (Hl + 2 * Hkvl) * Dh), device="cuda")
+        self.q = torch.zeros((R, Hl * Dh), dtype=torch.float16, device="cuda")
+        self.att = torch.zeros((R, Hl * Dh), dtype=torch.float16, device="cuda")
         self.bcx = torch.zeros((R, 3 * D), device="cuda")
         self.cv = torch.zeros((R, D), dtype=torch.float16, device="cuda")
         self.o = torch.zeros((R, D), device="cuda")
-        self.gu = torch.zeros((R, 2 * I), device="cuda")
-        self.act = torch.zeros((R, I), dtype=torch.float16, device="cuda")
-        self.logits = torch.zeros((1, V), device="cuda")
-        self.pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.gu = torch.zeros((R, 2 * Il), device="cuda")
+        self.act = torch.zeros((R, Il), dtype=torch.float16, device="cuda")
+        self.logits = torch.zeros((B, self.V), device="cuda")
+        self.keys = torch.zeros(B, dtype=torch.int64, device="cuda")
+        self.pos = torch.zeros(B, dtype=torch.int32, device="cuda")
         self.ids = torch.zeros(R, dtype=torch.int32, device="cuda")
-        self.next_id = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.next_id = torch.zeros(B, dtype=torch.int32, device="cuda")
         self.graph = None
 
     # -- low level ---------------------------------------------------------
@@ -172,6 +208,12 @@ class DecoderModel:
         xd = WG_F16 if x.dtype == torch.float16 else WG_F32
         yd = WG_F16 if y.dtype == torch.float16 else WG_F32
         self._c(L.wg_q4_matmul(P(self.ctx.handle), P(lin.m.handle), P(x.data_ptr()), xd, rows, P(y.data_ptr()), yd))
+
+    def _all_reduce(self, t: torch.Tensor, op=None):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(t, op=op or dist.ReduceOp.SUM, group=self.group)
 
     def reset(self):
         self.pos.zero_()
@@ -192,41 +234,65 @@ class DecoderModel:
                                               P(y.data_ptr()), WG_F32))
 
     def forward(self, ids: torch.Tensor, rows: int):
-        """Runs `rows` tokens (device int32 ids) at the current position; leaves
-        the last row's logits in self.logits and its greedy next token in
-        self.next_id, and advances the position."""
+        """Runs `rows` tokens (device int32 ids; batch sequences of rows /
+        batch tokens each) at the current positions; leaves each sequence's
+        last-row logits in self.logits and greedy next token in self.next_id,
+        and advances the positions."""
+        if rows % self.batch or rows > self.max_rows:
+            raise ValueError(f"rows {rows} for batch {self.batch} (max rows {self.max_rows})")
         if self.fused:
             return self._forward_fused(ids, rows)
         return self._forward_passes(ids, rows)
 
     def _attend(self, lay, rows):
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
-        H, Hkv, Dh = cfg.heads, cfg.kv_heads, cfg.head_dim
+        H, Hkv, Dh = self.H, self.Hkv, cfg.head_dim
         s = lay["slot"]
         kc, vc = self.k_cache[s], self.v_cache[s]
         qn, kn = lay.get("q_norm"), lay.get("k_norm")
-        self._c(L.wg_rope_kv(c, P(self.qkv.data_ptr()), rows, H, Hkv, Dh, P(self.pos.data_ptr()), cfg.theta,
-                             P(qn.data_ptr() if qn is not None else None), P(kn.data_ptr() if kn is not None else None),
-                             cfg.eps, P(self.q.data_ptr()), P(kc.data_ptr()), P(vc.data_ptr()), self.max_ctx))
-        self._c(L.wg_attention(c, P(self.q.data_ptr()), rows, H, Hkv, Dh, P(kc.data_ptr()), P(vc.data_ptr()),
-                               self.max_ctx, P(self.pos.data_ptr()), P(self.att.data_ptr())))
+        self._c(L.wg_rope_kv(c, P(self.qkv.data_ptr()), rows, self.batch, H, Hkv, Dh, P(self.pos.data_ptr()),
+                             cfg.theta, P(qn.data_ptr() if qn is not None else None),
+                             P(kn.data_ptr() if kn is not None else None), cfg.eps, P(self.q.data_ptr()),
+                             P(kc.data_ptr()), P(vc.data_ptr()), self.max_ctx))
+        self._c(L.wg_attention(c, P(self.q.data_ptr()), rows, self.batch, H, Hkv, Dh, P(kc.data_ptr()),
+                               P(vc.data_ptr()), self.max_ctx, P(self.pos.data_ptr()), P(self.att.data_ptr())))
         self._mm(lay["o"], self.att, self.o, rows)
+        self._all_reduce(self.o[:rows])
 
     def _convolve(self, lay, rows):
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
-        self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, cfg.hidden, cfg.conv_width,
+        self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, self.batch, cfg.hidden, cfg.conv_width,
                                 P(lay["conv_w"].data_ptr()), P(self.conv_state[lay["slot"]].data_ptr()),
                                 P(self.cv.data_ptr()), WG_F16))
         self._mm(lay["out"], self.cv, self.o, rows)
+
+    def _head(self, cur, add, rows):
+        """Final norm + head on each sequence's last row, greedy pick, and the
+        position advance."""
+        cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
+        B, rps = self.batch, rows // self.batch
+        last = rps - 1
+        sharded = self.world > 1
+        self._c(L.wg_head_rmsnorm(c, P(cur[last].data_ptr()), P(add[last].data_ptr() if add is not None else None),
+                                  P(self.final_norm.data_ptr()), cfg.eps, B, rps, cfg.hidden,
+                                  P(self.head.data_ptr()), self.V, self.vocab_offset, P(self.logits.data_ptr()),
+                                  P(None if sharded else self.next_id.data_ptr()),
+                                  P(self.keys.data_ptr() if sharded else None)))
+        if sharded:
+            import torch.distributed as dist
+
+            self._all_reduce(self.keys, dist.ReduceOp.MAX)
+            self._c(L.wg_pick_keys(c, P(self.keys.data_ptr()), B, P(self.next_id.data_ptr())))
+        self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), B, rps))
 
     def _forward_fused(self, ids: torch.Tensor, rows: int):
         """Each norm runs inside the matmul that consumes it, SwiGLU inside the
         down projection and the final norm inside the head: per layer the
         residual stream alternates between self.x and self.x2."""
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
-        D, V = cfg.hidden, cfg.vocab
+        D = cfg.hidden
         self.ctx.use_torch_stream()
-        self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), V, D, P(self.x.data_ptr())))
+        self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), cfg.vocab, D, P(self.x.data_ptr())))
         cur, other = self.x, self.x2
         add = None
         for lay in self.layers:
@@ -244,20 +310,17 @@ class DecoderModel:
             self._mm_norm(lay["gu"], cur, self.o, lay["norm2"], other, self.gu, rows)
             cur, other = other, cur
             self._mm_swiglu(lay["down"], self.gu, self.o, rows)
+            self._all_reduce(self.o[:rows])
             add = self.o
-        last = rows - 1
-        self._c(L.wg_head_rmsnorm(c, P(cur[last].data_ptr()), P(add[last].data_ptr()),
-                                  P(self.final_norm.data_ptr()), cfg.eps, 1, D, P(self.head.data_ptr()), V,
-                                  P(self.logits.data_ptr()), P(self.next_id.data_ptr())))
-        self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), rows))
+        self._head(cur, add, rows)
 
     def _forward_passes(self, ids: torch.Tensor, rows: int):
         """One launch per engine pass (norm, matmul, SwiGLU, ... each on its
         own)."""
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
-        D, I, V = cfg.hidden, cfg.ffn, cfg.vocab
+        D = cfg.hidden
         self.ctx.use_torch_stream()
-        self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), V, D, P(self.x.data_ptr())))
+        self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), cfg.vocab, D, P(self.x.data_ptr())))
         add = None
         for lay in self.layers:
             self._c(L.wg_rmsnorm(c, P(self.x.data_ptr()), P(add), P(lay["norm1"].data_ptr()), cfg.eps, rows, D,
@@ -271,28 +334,25 @@ class DecoderModel:
             self._c(L.wg_rmsnorm(c, P(self.x.data_ptr()), P(self.o.data_ptr()), P(lay["norm2"].data_ptr()), cfg.eps,
                                  rows, D, P(self.h.data_ptr()), WG_F16))
             self._mm(lay["gu"], self.h, self.gu, rows)
-            self._c(L.wg_swiglu(c, P(self.gu.data_ptr()), rows, I, P(self.act.data_ptr()), WG_F16))
+            self._c(L.wg_swiglu(c, P(self.gu.data_ptr()), rows, self.I, P(self.act.data_ptr()), WG_F16))
             self._mm(lay["down"], self.act, self.o, rows)
+            self._all_reduce(self.o[:rows])
             add = self.o.data_ptr()
-        # final norm and head for the last row only
-        last = rows - 1
-        xl = self.x[last:last + 1]
-        ol = self.o[last:last + 1]
-        self._c(L.wg_rmsnorm(c, P(xl.data_ptr()), P(ol.data_ptr()), P(self.final_norm.data_ptr()), cfg.eps, 1, D,
-                             P(self.h.data_ptr()), WG_F16))
-        self._c(L.wg_head(c, P(self.h.data_ptr()), 1, D, P(self.head.data_ptr()), V, P(self.logits.data_ptr()),
-                          P(self.next_id.data_ptr())))
-        self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), rows))
+        self._head(self.x, self.o, rows)
 
-    def prefill(self, prompt: torch.Tensor):
-        rows = prompt.numel()
-        assert rows <= self.max_rows
-        self.ids[:rows].copy_(prompt.to(torch.int32))
+    def prefill(self, prompts: torch.Tensor):
+        """prompts: device ids [batch][T] (or [T] for batch 1)."""
+        prompts = prompts.reshape(self.batch, -1)
+        rows = prompts.numel()
+        if rows > self.max_rows:
+            raise ValueError(f"prompt rows {rows} > max_rows {self.max_rows}")
+        self.ids[:rows].copy_(prompts.reshape(-1).to(torch.int32))
         self.forward(self.ids, rows)
 
     def decode_step(self):
-        """One greedy token: input = the last argmax (on the device)."""
-        self.forward(self.next_id, 1)
+        """One greedy token per sequence: input = the last picks (on the
+        device)."""
+        self.forward(self.next_id, self.batch)
 
     def capture_decode(self):
         """Records decode_step as a CUDA graph (after one eager step, so that
@@ -301,17 +361,18 @@ class DecoderModel:
         with torch.cuda.graph(self.graph):  # captures on a side stream of torch's
             self.decode_step()
 
-    def generate(self, prompt: torch.Tensor, n_new: int, use_graph: bool = True) -> torch.Tensor:
-        """Greedy continuation of `prompt` (device ids): returns n_new ids."""
-        out = torch.zeros(n_new, dtype=torch.int32, device="cuda")
-        self.prefill(prompt)
+    def generate(self, prompts: torch.Tensor, n_new: int, use_graph: bool = True) -> torch.Tensor:
+        """Greedy continuation of `prompts` (device ids [batch][T]): returns
+        [batch][n_new] ids."""
+        out = torch.zeros((self.batch, n_new), dtype=torch.int32, device="cuda")
+        self.prefill(prompts)
         if n_new == 0:
             return out
-        out[0:1].copy_(self.next_id)
+        out[:, 0].copy_(self.next_id)
         for i in range(1, n_new):
             if use_graph and self.graph is not None:
                 self.graph.replay()
             else:
                 self.decode_step()
-            out[i:i + 1].copy_(self.next_id)
+            out[:, i].copy_(self.next_id)
         return out
