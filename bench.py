@@ -14,8 +14,11 @@ is the max over ranks and `value` sums all ranks' bytes.
 Extra keys: `roofline` (the GEMV kernel against the measured HBM copy
 bandwidth), `e2e` (the same GB/s through the C ABI with pinned host buffers,
 copies inside the timed region), `cpu_baseline` (the CPU oracle's restatement
-of the reference's shader arithmetic on the host cores), `clocks`, and
-`sweep` (config 1's other row counts, informational).
+of the reference's shader arithmetic on the host cores), `clocks`, `sweep`
+(config 1's other row counts, informational) and `decode` (BASELINE's
+"decode tokens/s": greedy generation of the random-init decoders of configs
+2, 3 and 4 on one GPU; with --gpus N, config 4 tensor-parallel over the N
+GPUs).
 
 `--impl reference` times the reference's algorithm on the CPU instead (the
 reference's own path is WebGL2 shaders, unavailable on this host; the oracle
@@ -213,6 +216,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decoder generation runs")
     ap.add_argument("--matrices", type=int, default=MATRICES,
                     help="distinct matrices per step (default 64 = 604 MB; >= 14 exceeds L2)")
     args = ap.parse_args()
@@ -316,12 +320,46 @@ def main() -> None:
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
 
+    decode = None if args.no_decode else run_decode(world, rank, barrier, max_over_ranks, hbm)
+
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
     line = make_line(args, world, value, ms_step, per_launch, achieved, hbm, src, traffic, e2e, clock, cpu, sweep)
+    line["decode"] = decode
     print(json.dumps(line), flush=True)
+
+
+def run_decode(world, rank, barrier, max_over_ranks, hbm):
+    """Greedy generation (webgllm_b200.runner): configs 2 and 3 on one GPU
+    and config 4 (batch 8) on all ranks, tensor-parallel when world > 1.
+    Times are the max over ranks; `frac_hbm` is the bytes one decode step
+    must read per GPU over the step time, against the measured copy
+    bandwidth."""
+    from webgllm_b200 import runner
+
+    names = ["2", "3", "4"] if world == 1 else ["4"]
+    out = []
+    for k in names:
+        cfg, batch, prompt, gen = runner.WORKLOADS[k]
+        tp = (rank, world, None) if world > 1 else None
+        r = runner.measure(cfg, batch, prompt, gen, tp=tp, barrier=barrier)
+        step_ms = max_over_ranks(r["decode_ms_per_step"])
+        prefill_ms = max_over_ranks(r["prefill_ms"])
+        steps = gen - 1
+        total_s = (prefill_ms + step_ms * steps) / 1e3
+        out.append({
+            "config": int(k), "model": r["model"], "batch": batch, "prompt_tokens": prompt,
+            "generated_tokens": gen, "tensor_parallel": world if k == "4" else 1,
+            "decode_tok_s": round(batch / (step_ms / 1e3), 1), "decode_ms_per_step": round(step_ms, 4),
+            "prefill_ms": round(prefill_ms, 3), "prefill_tok_s": round(batch * prompt / (prefill_ms / 1e3), 1),
+            "e2e_tok_s": round(batch * gen / total_s, 1),
+            "step_bytes_per_gpu": int(r["step_bytes"]),
+            "frac_hbm": round(r["step_bytes"] / (step_ms / 1e3) / 1e9 / hbm, 4),
+            "first_tokens": r["tokens_head"][0],
+        })
+    return out
 
 
 def run_e2e(args, ctx, mats, x, ys, per_launch, world, barrier, max_over_ranks):

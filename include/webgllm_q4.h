@@ -177,8 +177,10 @@ typedef struct wg_prologue {
  * from `pro` inside the matmul's own launch for M <= 8 rows (the decode
  * GEMV stages x in shared memory; each CTA computes the row statistics of
  * the norm itself): the engine's norm / SwiGLU pass and the matmul that
- * consumes it become one kernel. More rows run the prologue as its own
- * kernel into the context's scratch (it may allocate, as wg_q4_matmul).
+ * consumes it become one kernel. More rows, or a norm whose statistics
+ * would make every CTA read over 64 KB (M * K * 4 bytes, twice with b), run
+ * the prologue as its own kernel into the context's scratch (it may
+ * allocate, as wg_q4_matmul).
  * Tensors are device pointers, 16-byte aligned. No reference counterpart as
  * one call: the engine runs the two passes back to back
  * (src/engine.ts:8875-9304). */

@@ -182,6 +182,8 @@ int wg_init(int device, wg_ctx **out) {
   ctx->stream = ctx->own_stream;
   const char *pdl = getenv("WG_PDL");
   if (pdl && pdl[0] == '0') ctx->pdl = false;
+  const char *wide = getenv("WG_GEMV_WIDE");
+  if (wide && (wide[0] == '0' || wide[0] == '1')) ctx->gemv_wide = wide[0] - '0';
   const char *trig = getenv("WG_GEMV_TRIGGER");
   if (trig && trig[0] >= '0' && trig[0] <= '2') ctx->trigger_at = trig[0] - '0';
   *out = ctx;
@@ -438,6 +440,24 @@ int wg_q4_matrix_row(wg_ctx *ctx, const wg_q4mat *m, int n, float *out) {
 
 namespace {
 
+// Which GEMV serves a launch of up to 8 rows: the wide one (x resident per
+// CTA, columns streamed) when the tile-column GEMV would need several waves
+// of CTAs or re-stage several rows of x in each of them. WG_GEMV_WIDE=0 / 1
+// forces one or the other (measurement).
+bool use_wide(const wg_ctx *ctx, const wg::GemvArgs &a) {
+  if (a.M > wg::kProMaxTokens) return false;
+  if (ctx->gemv_wide >= 0) return ctx->gemv_wide == 1;
+  wg::GemvArgs t = a;
+  if (!wg::plan_gemv(t, ctx->num_sms)) return true;
+  // Measured on B200 (M x N x K): the wide kernel wins from 4 rows on, and
+  // for long K (>= 8192: the tile-column kernel's x re-staging) or, at 2-3
+  // rows, many columns; one row of a short-K matrix stays on the
+  // tile-column kernel, whose smaller CTAs overlap a chain's launches.
+  if (a.M >= 4) return true;
+  if (a.K >= 8192) return true;
+  return a.M >= 2 && a.N >= 16384;
+}
+
 // The matmul behind wg_q4_matmul and wg_q4_matmul_fused: y = x . W^T, with
 // x given (pro == null) or made by a prologue. Arguments are checked.
 int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y, int y_dtype,
@@ -476,8 +496,12 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     WG_CUDA(ctx, wg::launch_gemm(g, xh, ctx->stream));
     return WG_OK;
   }
-  // A prologue over more rows than one fused GEMV takes runs on its own.
-  if (pro && M > wg::kProMaxTokens) {
+  // A prologue over more rows than one fused GEMV takes runs on its own; so
+  // does a norm whose row statistics would cost every CTA more than 64 KB of
+  // reads (each CTA of the fused form reads all of a and b for them).
+  const bool heavy_norm =
+      pro && pro->kind == wg::kProRmsNorm && (size_t)M * K * 4 * (pro->b ? 2 : 1) > ((size_t)64 << 10);
+  if (pro && (M > wg::kProMaxTokens || heavy_norm)) {
     st = ensure_work(ctx, (size_t)M * K * 2);
     if (st) return st;
     WG_CUDA(ctx, wg::launch_prologue(*pro, M, (int)K, ctx->work, ctx->stream));
@@ -510,6 +534,11 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     a.launch_index = ctx->launch_index++;
     a.trigger_at = ctx->trigger_at;
     if (pro) a.pro = *pro;  // M <= kProMaxTokens: one launch
+    wg::GemvArgs w = a;
+    if (use_wide(ctx, a) && wg::plan_gemv_wide(w, ctx->num_sms)) {
+      WG_CUDA(ctx, wg::launch_gemv_wide(w, ctx->stream, ctx->pdl));
+      continue;
+    }
     if (!wg::plan_gemv(a, ctx->num_sms))
       return fail(ctx, WG_UNSUPPORTED, "K = %d is beyond the GEMV's largest cluster split", m->d.K);
     WG_CUDA(ctx, wg::launch_gemv(a, ctx->stream, ctx->pdl));

@@ -29,6 +29,9 @@
 #include <cooperative_groups.h>
 
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "device_utils.cuh"
@@ -106,11 +109,15 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
       lo_g8 = zp_lo((zz >> 8) & 15u);
       hi_g8 = zp_hi((zz >> 8) & 15u);
     }
-    float blk[NG][4];
+    // the block's two 16-wide K steps accumulate separately (independent
+    // MMAs), then add
+    float blk[2][NG][4];
 #pragma unroll
-    for (int ng = 0; ng < NG; ng++)
+    for (int js = 0; js < 2; js++)
 #pragma unroll
-      for (int e = 0; e < 4; e++) blk[ng][e] = 0.0f;
+      for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) blk[js][ng][e] = 0.0f;
 #pragma unroll
     for (int js = 0; js < 2; js++) {
       const int j = 2 * bsel + js;
@@ -122,17 +129,17 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
         uint2 b = make_uint2(0, 0);
         if (tok < M) b = *reinterpret_cast<const uint2 *>(xt + (size_t)tok * stride + 16 * j);
         // fragment k {2t,2t+1 | 2t+8,2t+9} <-> K offset {4t,4t+1 | 4t+2,4t+3}
-        mma_16816(blk[ng], P[0], P[2], P[1], P[3], b.x, b.y);
+        mma_16816(blk[js][ng], P[0], P[2], P[1], P[3], b.x, b.y);
       }
     }
     const uint32_t sp = bsel ? sv.y : sv.x;
     const float2 sc = __half22float2(*reinterpret_cast<const __half2 *>(&sp));
 #pragma unroll
     for (int ng = 0; ng < NG; ng++) {
-      acc[ng][0] = fmaf(sc.x, blk[ng][0], acc[ng][0]);
-      acc[ng][1] = fmaf(sc.x, blk[ng][1], acc[ng][1]);
-      acc[ng][2] = fmaf(sc.y, blk[ng][2], acc[ng][2]);
-      acc[ng][3] = fmaf(sc.y, blk[ng][3], acc[ng][3]);
+      acc[ng][0] = fmaf(sc.x, blk[0][ng][0] + blk[1][ng][0], acc[ng][0]);
+      acc[ng][1] = fmaf(sc.x, blk[0][ng][1] + blk[1][ng][1], acc[ng][1]);
+      acc[ng][2] = fmaf(sc.y, blk[0][ng][2] + blk[1][ng][2], acc[ng][2]);
+      acc[ng][3] = fmaf(sc.y, blk[0][ng][3] + blk[1][ng][3], acc[ng][3]);
     }
   }
 }
@@ -178,7 +185,9 @@ __device__ __forceinline__ uint4 prologue_x8(const Prologue &p, int K, int m, in
 // The norm prologue's row statistics: inv[m] = 1 / sqrt(mean((residual +
 // b)^2) + eps) over all of K, for every row (all threads of the CTA), and
 // the residual sum written out by a grid-strided share of every CTA.
+template <int NW = kWarps>
 __device__ void rmsnorm_rows(const Prologue &p, int M, int K, float *s_part, float *s_inv) {
+  constexpr int kThreads = NW * 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K4 = K / 4;
   for (int m = 0; m < M; m++) {
@@ -204,7 +213,7 @@ __device__ void rmsnorm_rows(const Prologue &p, int M, int K, float *s_part, flo
   __syncthreads();
   if (threadIdx.x < M) {
     float t = 0.0f;
-    for (int w = 0; w < kWarps; w++) t += s_part[w * kProMaxTokens + threadIdx.x];
+    for (int w = 0; w < NW; w++) t += s_part[w * kProMaxTokens + threadIdx.x];
     s_inv[threadIdx.x] = rsqrtf(t / (float)K + p.eps);
   }
   __syncthreads();
@@ -451,6 +460,284 @@ __global__ void __launch_bounds__(kThreads) prologue_kernel(const Prologue p, in
   }
 }
 
+// ---- the wide GEMV: x staged once per CTA, tile columns streamed ---------
+//
+// For matrices with many 16-row tile columns (or several activation rows),
+// the kernel above re-stages x in every CTA of a multi-wave grid: at M = 8
+// and N = 28672 that is 8x the weight bytes in L2 reads. Here a grid of about
+// one CTA per SM (or cluster of C CTAs when x does not fit: C splits K) keeps
+// its x slice resident in shared memory for the whole launch and walks tile
+// columns g, g + G, g + 2G, ...; a column's K range is contiguous in each
+// plane, so one thread streams whole columns (two or three bulk async
+// copies each) through a ring of S stages with one mbarrier per stage, and
+// the copies of the next columns are in flight while the 16 warps multiply
+// this one (each warp a slice of its K tiles). Per column the warps'
+// fragments are summed in shared memory; with a K split, the per-column sums
+// stay in shared memory and the cluster reduces them once at the end.
+
+constexpr int kWideXBudget = 96 * 1024;   // x slice per CTA
+constexpr int kWideSmemMax = 200 * 1024;
+constexpr int kWWarps = 16;                // warps of a wide CTA (one CTA per SM)
+constexpr int kWThreads = kWWarps * 32;
+
+struct WideSmem {
+  int x, stage, bars, red, part, total;
+  int xstride, stage_bytes;
+};
+
+__host__ __device__ inline WideSmem wide_smem(int M, int ktc, int S, int J, int C, bool zeros) {
+  WideSmem w;
+  w.xstride = ktc * kTileK + 16;
+  w.stage_bytes = align_to(ktc * (kTileNibBytes + kTileSclBytes + (zeros ? kTileZroBytes : 0)), 128);
+  w.x = 0;
+  w.stage = align_to(w.x + M * w.xstride * 2, 128);
+  w.bars = align_to(w.stage + S * w.stage_bytes, 8);
+  w.red = align_to(w.bars + (S + 1) * 8, 16);  // + the x barrier
+  w.part = w.red + kWWarps * 128 * 4;
+  w.total = w.part + (C > 1 ? J * 128 * 4 : 0);
+  return w;
+}
+
+template <bool ZEROS, int PRO>
+__global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = lane & 3;
+  const int C = a.cluster, crank = blockIdx.x;
+  const int G = gridDim.y, g = blockIdx.y;
+  const int S = a.stages;
+  const int kt0 = crank * a.kt_per_cta;
+  const int kt1 = min(a.KT, kt0 + a.kt_per_cta);
+  const int ktc = kt1 - kt0;
+  const int J = (a.NT - g + G - 1) / G;  // columns of this CTA: g, g + G, ...
+  const int Jmax = (a.NT + G - 1) / G;
+  const WideSmem L = wide_smem(a.M, a.kt_per_cta, S, Jmax, C, ZEROS);
+  const int tpw = (a.kt_per_cta + kWWarps - 1) / kWWarps;
+  const int wt0 = min(ktc, warp * tpw), wt1 = min(ktc, wt0 + tpw);  // this warp's K tiles
+  __half *xs = reinterpret_cast<__half *>(smem + L.x);
+  uint8_t *stages = smem + L.stage;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+  uint64_t *xbar = bars + S;
+  // fp16 x without a prologue arrives by bulk copy, one per row
+  const bool x_bulk = PRO == kProNone && a.x_dtype == WG_F16;
+  float *red = reinterpret_cast<float *>(smem + L.red);
+  float *part = reinterpret_cast<float *>(smem + L.part);
+  const int nib_b = ktc * kTileNibBytes, scl_b = ktc * kTileSclBytes;
+  __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
+  if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
+
+  auto issue = [&](int j) {  // thread 0: column g + j*G (this CTA's K range) into stage j % S
+    const int st = j % S;
+    uint8_t *dst = stages + st * L.stage_bytes;
+    const size_t tile = (size_t)(g + j * G) * a.KT + kt0;
+    mbar_expect_tx(&bars[st], nib_b + scl_b + (ZEROS ? ktc * kTileZroBytes : 0));
+    bulk_g2s(dst, reinterpret_cast<const uint8_t *>(a.nib) + tile * kTileNibBytes, nib_b, &bars[st]);
+    bulk_g2s(dst + nib_b, reinterpret_cast<const uint8_t *>(a.scl) + tile * kTileSclBytes, scl_b, &bars[st]);
+    if (ZEROS) bulk_g2s(dst + nib_b + scl_b, a.zro + tile * kTileZroBytes, ktc * kTileZroBytes, &bars[st]);
+  };
+
+  // 1. Weight copies of the first S columns: they depend on nothing the
+  //    previous kernel writes.
+  if (threadIdx.x == 0) {
+    for (int st = 0; st <= S; st++) mbar_init(&bars[st], 1);  // stages and x
+    fence_mbar_init();
+    for (int j = 0; j < min(S, J); j++) issue(j);
+  }
+  __syncthreads();
+  if (a.trace && threadIdx.x == 0) ts[1] = globaltimer();
+
+  // 2. x (or its prologue) for this CTA's K range, once.
+  pdl_wait();
+  if (a.trace && threadIdx.x == 0) ts[2] = globaltimer();
+  const int M = a.M;
+  __shared__ float s_inv[kProMaxTokens];
+  if constexpr (PRO == kProRmsNorm) {
+    __shared__ float s_part[kWWarps * kProMaxTokens];
+    rmsnorm_rows<kWWarps>(a.pro, M, a.K, s_part, s_inv);
+  }
+  if (x_bulk) {
+    const int kbase = kt0 * kTileK;
+    const int kcols = min(a.K - kbase, ktc * kTileK);  // a multiple of 32
+    if (threadIdx.x == 0) {
+      mbar_expect_tx(xbar, (uint32_t)(M * kcols * 2));
+      for (int m = 0; m < M; m++)
+        bulk_g2s(xs + (size_t)m * L.xstride, reinterpret_cast<const __half *>(a.x) + (size_t)m * a.K + kbase,
+                 kcols * 2, xbar);
+    }
+    // the partial last tile reads zeros past K
+    const int tail = ktc * kTileK - kcols;
+    for (int i = threadIdx.x; i < M * tail; i += kWThreads) {
+      const int m = i / tail;
+      xs[(size_t)m * L.xstride + kcols + (i - m * tail)] = __float2half_rn(0.0f);
+    }
+    mbar_wait_bounded(xbar, 0, a.flags);
+  } else {
+    const int chunks = ktc * (kTileK / 8);
+    const int kbase = kt0 * kTileK;
+    for (int base = 0; base < M * chunks; base += 4 * kWThreads) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int idx = base + u * kWThreads + threadIdx.x;
+        v[u] = make_uint4(0, 0, 0, 0);
+        if (idx < M * chunks) {
+          const int m = idx / chunks, c = idx - m * chunks;
+          const int k = kbase + c * 8;
+          if (k < a.K) {
+            if constexpr (PRO == kProNone)
+              v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
+            else
+              v[u] = prologue_x8<PRO>(a.pro, a.K, m, k, PRO == kProRmsNorm ? s_inv[m] : 0.0f);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int idx = base + u * kWThreads + threadIdx.x;
+        if (idx < M * chunks) {
+          const int m = idx / chunks, c = idx - m * chunks;
+          *reinterpret_cast<uint4 *>(xs + (size_t)m * L.xstride + c * 8) = v[u];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (a.trigger_at <= 1) pdl_trigger();
+  if (a.trace && threadIdx.x == 0) ts[3] = globaltimer();
+
+  // 3. Columns.
+  constexpr int kOut = 16 * 8;
+  for (int j = 0; j < J; j++) {
+    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+    const int st = j % S;
+    mbar_wait_bounded(&bars[st], (j / S) & 1, a.flags);
+    const uint8_t *sb = stages + st * L.stage_bytes;
+#pragma unroll 2
+    for (int i = wt0; i < wt1; i++)
+      tile_mma<1, ZEROS>(sb + i * kTileNibBytes, sb + nib_b + i * kTileSclBytes,
+                         sb + nib_b + scl_b + i * kTileZroBytes, xs + i * kTileK + 4 * t, L.xstride, M, lane, acc);
+#pragma unroll
+    for (int e = 0; e < 4; e++) red[(warp * 4 + e) * 32 + lane] = acc[0][e];
+    __syncthreads();
+    if (threadIdx.x == 0 && j + S < J) issue(j + S);  // every warp is done with the stage
+    const int nt = g + j * G;
+    for (int o = threadIdx.x; o < kOut; o += kWThreads) {
+      const int r = o / 8, tok = o - r * 8;
+      const int ln = 4 * (r & 7) + (tok >> 1);
+      const int e = ((r >> 3) << 1) | (tok & 1);
+      float sum = 0.0f;
+#pragma unroll
+      for (int w2 = 0; w2 < kWWarps; w2++) sum += red[(w2 * 4 + e) * 32 + ln];
+      if (C > 1) {
+        part[j * kOut + o] = sum;
+      } else {
+        const int n = nt * kTileRows + r;
+        if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
+      }
+    }
+    __syncthreads();  // red is reused by the next column
+  }
+  if (a.trigger_at == 2) pdl_trigger();
+  if (a.trace && threadIdx.x == 0) ts[4] = globaltimer();
+
+  // 4. K split: sum the per-column partials over the cluster (rank c takes
+  //    entries c, c + C, ... of every column).
+  if (C > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    for (int idx = crank + C * (int)threadIdx.x; idx < J * kOut; idx += C * kWThreads) {
+      float sum = 0.0f;
+      for (int c = 0; c < C; c++) sum += cluster.map_shared_rank(part, c)[idx];
+      const int j = idx / kOut, o = idx - j * kOut;
+      const int r = o / 8, tok = o - r * 8;
+      const int n = (g + j * G) * kTileRows + r;
+      if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
+    }
+    cluster.sync();
+  }
+  // No copy may still be writing shared memory at exit (only possible after
+  // a timed-out wait).
+  if (threadIdx.x == 0) {
+    if (x_bulk) mbar_wait_bounded(xbar, 0, a.flags);
+    for (int j = max(0, J - S); j < J; j++) mbar_wait_bounded(&bars[j % S], (j / S) & 1, a.flags);
+  }
+  if (a.trace && threadIdx.x == 0) {
+    ts[5] = globaltimer();
+    trace_record(a.trace, a.trace_next, a.trace_cap, ts, a.launch_index, blockIdx.y * gridDim.x + blockIdx.x);
+  }
+}
+
+// Clusters of C CTAs with `smem` bytes each that fit on the GPU at once
+// (clusters must sit within one GPC, so this can be below num_sms / C).
+int wide_max_clusters(int C, int smem, int num_sms) {
+  static std::mutex lock;
+  static std::map<std::pair<int, int>, int> cache;
+  std::lock_guard<std::mutex> guard(lock);
+  const auto key = std::make_pair(C, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto kern = gemv_wide_kernel<false, kProNone>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMax) == cudaSuccess &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)C, (unsigned)(num_sms / C > 0 ? num_sms / C : 1), 1);
+    cfg.blockDim = dim3(kWThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = (unsigned)C;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();  // a failed query leaves no sticky error
+  if (n <= 0) n = num_sms / C > 0 ? num_sms / C : 1;
+  cache[key] = n;
+  return n;
+}
+
+template <bool ZEROS, int PRO>
+cudaError_t launch_wide_t(const GemvArgs &a, cudaStream_t stream, bool pdl) {
+  const int G = a.groups;
+  const int Jmax = (a.NT + G - 1) / G;
+  const WideSmem L = wide_smem(a.M, a.kt_per_cta, a.stages, Jmax, a.cluster, ZEROS);
+  auto kern = gemv_wide_kernel<ZEROS, PRO>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMax);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  if (L.total > kWideSmemMax) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.cluster, (unsigned)G, 1);
+  cfg.blockDim = dim3(kWThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)L.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  if (a.cluster > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = (unsigned)a.cluster;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
+    n++;
+  }
+  if (pdl) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
 }  // namespace
 
 cudaError_t launch_prologue(const Prologue &p, int M, int K, void *x_f16, cudaStream_t stream) {
@@ -484,6 +771,44 @@ bool plan_gemv(GemvArgs &a, int num_sms) {
   a.kt_per_cta = ktc;
   a.cluster = C;
   return true;
+}
+
+bool plan_gemv_wide(GemvArgs &a, int num_sms) {
+  if (a.M < 1 || a.M > kProMaxTokens) return false;
+  const bool zeros = a.zro != nullptr;
+  int C = 1;
+  while (a.M * ((a.KT + C - 1) / C) * kTileK * 2 > kWideXBudget) C++;
+  if (C > 8) return false;
+  const int ktc = (a.KT + C - 1) / C;
+  C = (a.KT + ktc - 1) / ktc;
+  // stages: as many as fit (with the largest column count a CTA can get)
+  int G = num_sms / C;
+  if (G < 1) G = 1;
+  if (G > a.NT) G = a.NT;
+  int S = 4;
+  while (S > 1 && wide_smem(a.M, ktc, S, (a.NT + G - 1) / G * 2, C, zeros).total > kWideSmemMax) S--;
+  // one wave: no more clusters than fit at once
+  const int fit = wide_max_clusters(C, wide_smem(a.M, ktc, S, (a.NT + G - 1) / G * 2, C, zeros).total, num_sms);
+  if (G > fit) G = fit;
+  const int J = (a.NT + G - 1) / G;
+  if (wide_smem(a.M, ktc, S, J, C, zeros).total > kWideSmemMax) return false;
+  a.kt_per_cta = ktc;
+  a.cluster = C;
+  a.groups = G;
+  a.stages = S;
+  return true;
+}
+
+cudaError_t launch_gemv_wide(const GemvArgs &a, cudaStream_t stream, bool pdl) {
+  const bool z = a.zro != nullptr;
+  switch (a.pro.kind) {
+    case kProNone: return z ? launch_wide_t<true, kProNone>(a, stream, pdl) : launch_wide_t<false, kProNone>(a, stream, pdl);
+    case kProRmsNorm:
+      return z ? launch_wide_t<true, kProRmsNorm>(a, stream, pdl) : launch_wide_t<false, kProRmsNorm>(a, stream, pdl);
+    case kProSwiglu:
+      return z ? launch_wide_t<true, kProSwiglu>(a, stream, pdl) : launch_wide_t<false, kProSwiglu>(a, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl) {

@@ -66,12 +66,18 @@ struct GemvArgs {
   unsigned launch_index;
   int trigger_at;  // when dependents may launch: 0 entry, 1 x staged, 2 multiplies done
   Prologue pro;    // kProNone: x as given; else x is made from pro (M <= kProMaxTokens)
+  int groups;      // wide GEMV: column groups (grid.y)
+  int stages;      // wide GEMV: weight ring stages per warp
 };
 
 constexpr int kGemvMaxTokens = 32;
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl);
 // Plans kt_per_cta / cluster for a shape; false if the shape is too large.
 bool plan_gemv(GemvArgs &a, int num_sms);
+// The wide GEMV (M <= kProMaxTokens): x resident per CTA, tile columns
+// streamed through a ring; plans kt_per_cta / cluster / groups / stages.
+bool plan_gemv_wide(GemvArgs &a, int num_sms);
+cudaError_t launch_gemv_wide(const GemvArgs &a, cudaStream_t stream, bool pdl);
 
 // The prefill GEMM (tcgen05): y[M][N] = x[M][K] . W^T for M > 32, x fp16.
 struct GemmArgs {

@@ -1,0 +1,84 @@
+"""Greedy generation throughput of the random-init decoders (BASELINE
+configs 2-4): prompt prefill, then decode steps replayed from a CUDA graph.
+
+Used by bench.py; a run is `measure(cfg, batch, prompt_len, gen_len, tp)`:
+every rank of a tensor-parallel group calls it with the same arguments.
+"""
+from __future__ import annotations
+
+import torch
+
+from .model import CONFIGS, DecoderModel
+
+# BASELINE workloads: (config, batch, prompt tokens, generated tokens)
+WORKLOADS = {
+    "2": (CONFIGS["2"], 1, 128, 128),
+    "3": (CONFIGS["3"], 1, 512, 256),
+    "4": (CONFIGS["4"], 8, 512, 256),
+}
+
+
+def step_bytes(m: DecoderModel, ctx_len: float) -> float:
+    """HBM bytes one decode step must read on this rank: every Q4 matrix
+    (18 bytes per 32 weights), the head shard (fp16), the embedding rows, and
+    the K / V cache of `ctx_len` positions per sequence."""
+    cfg = m.cfg
+    q4 = 0
+    for lay in m.layers:
+        for k in ("qkv", "o", "in", "out", "gu", "down"):
+            if k in lay:
+                q4 += lay[k].N * lay[k].K * 18 // 32
+    head = m.V * cfg.hidden * 2
+    n_attn = sum(t == "attn" for t in cfg.layer_types)
+    kv = n_attn * m.batch * m.Hkv * ctx_len * cfg.head_dim * 2 * 2
+    return q4 + head + m.batch * cfg.hidden * 2 + kv
+
+
+def measure(cfg, batch: int, prompt_len: int, gen_len: int, tp=None, seed: int = 0, barrier=None) -> dict:
+    """Prefill `batch` random prompts of `prompt_len` tokens and generate
+    `gen_len` tokens each (the first from the prefill, the rest from graph
+    replays). Device-timed with CUDA events; `barrier` (if given) runs before
+    and after the timed region."""
+    m = DecoderModel(cfg, seed=seed, max_ctx=prompt_len + gen_len + 8, max_rows=batch * prompt_len, batch=batch,
+                     tp=tp)
+    g = torch.Generator().manual_seed(seed + 1)
+    prompts = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=g).to("cuda", torch.int32)
+    out = torch.zeros((batch, gen_len), dtype=torch.int32, device="cuda")
+    # warm-up: every kernel configured, graph captured
+    m.prefill(prompts)
+    m.decode_step()
+    m.capture_decode()
+    m.graph.replay()
+    torch.cuda.synchronize()
+    m.reset()
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record(s)
+    m.prefill(prompts)
+    out[:, 0].copy_(m.next_id)
+    ev[1].record(s)
+    for i in range(1, gen_len):
+        m.graph.replay()
+        out[:, i].copy_(m.next_id)
+    ev[2].record(s)
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    decode_ms = ev[1].elapsed_time(ev[2])
+    steps = gen_len - 1
+    res = {
+        "model": cfg.name, "batch": batch, "prompt": prompt_len, "generated": gen_len,
+        "tp": m.world, "prefill_ms": prefill_ms, "decode_ms_per_step": decode_ms / max(steps, 1),
+        "decode_tok_s": batch * steps / (decode_ms / 1e3) if steps else None,
+        "prefill_tok_s": batch * prompt_len / (prefill_ms / 1e3),
+        "e2e_tok_s": batch * gen_len / ((prefill_ms + decode_ms) / 1e3),
+        "step_bytes": step_bytes(m, prompt_len + gen_len / 2),
+        "tokens_head": out[:, :8].tolist(),
+    }
+    del m
+    torch.cuda.empty_cache()
+    return res
