@@ -615,6 +615,157 @@ __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
   if (threadIdx.x == 0) *count = 0;  // ready for the next launch (stream order)
 }
 
+// The head on tensor cores (D % 32 == 0): a warp computes 16 vocabulary
+// rows against all (up to 8) input rows with mma.m16n8k16, fp32 accumulate.
+// Per 32 dims a lane loads 16 contiguous bytes of each of its two W rows
+// (rows g and g + 8 of the tile, dims 8t .. 8t+7) and uses them as the A
+// fragments of two MMAs; the same K order is read from x (dims 8t + 4j ..
+// 8t + 4j + 3 for MMA j), so W streams with full 64-byte row segments per
+// instruction and no data shuffling. x lives in shared memory (fp16, 8
+// rows, zero past `rows`). Grid: one 16-warp CTA per SM, tiles strided
+// over all warps; the greedy pick as in head_kernel.
+
+constexpr int kHmWarps = 16;
+constexpr int kHmThreads = kHmWarps * 32;
+constexpr int kHmChunks = 4;  // 32-dim chunks per batch of loads (8 x 16 B in flight per lane)
+
+__device__ __forceinline__ void mma_f16_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <bool NORM>
+__global__ void __launch_bounds__(kHmThreads, 1)
+    head_mma_kernel(const __half *x, HeadNorm nrm, int rows, int row_stride, int D, const __half *W, int V,
+                    int vocab_offset, float *logits, int32_t *amax, unsigned long long *keys,
+                    unsigned long long *part, unsigned *count) {
+  pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  pdl_wait();     // inputs come from the previous kernel
+  extern __shared__ __align__(16) __half xh[];  // [8][D + 16]
+  __shared__ unsigned long long s_key[kHmWarps][8];
+  __shared__ bool s_last;
+  __shared__ float red[32];
+  const int xstride = D + 16;
+  for (int r = 0; r < 8; r++) {
+    if (r >= rows) {
+      for (int i = threadIdx.x; i < D; i += blockDim.x) xh[r * xstride + i] = __float2half_rn(0.0f);
+      continue;
+    }
+    const size_t src = (size_t)r * row_stride * D;
+    if (NORM) {
+      float ss = 0.0f;
+      for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        float v = nrm.a[src + i];
+        if (nrm.b) v += nrm.b[src + i];
+        ss += v * v;
+      }
+      const float inv = rsqrtf(block_sum(ss, red) / (float)D + nrm.eps);
+      for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        float v = nrm.a[src + i];
+        if (nrm.b) v += nrm.b[src + i];
+        xh[r * xstride + i] = __float2half_rn(clamp_half(v * inv * nrm.w[i]));
+      }
+    } else {
+      for (int i = threadIdx.x; i < D; i += blockDim.x) xh[r * xstride + i] = x[src + i];
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int ntiles = (V + 15) / 16;
+  const int nchunks = D / 32;
+  float bv[2] = {-INFINITY, -INFINITY};
+  int bi[2] = {0x7fffffff, 0x7fffffff};
+  const __half *xg = xh + g * xstride + 8 * t;  // this lane's B rows: token g
+  for (int tile = blockIdx.x * kHmWarps + warp; tile < ntiles; tile += gridDim.x * kHmWarps) {
+    const int v0 = tile * 16;
+    const int ra = min(v0 + g, V - 1), rb = min(v0 + g + 8, V - 1);  // past V: read a valid row, drop it
+    const uint4 *wa = reinterpret_cast<const uint4 *>(W + (size_t)ra * D) + t;
+    const uint4 *wb = reinterpret_cast<const uint4 *>(W + (size_t)rb * D) + t;
+    float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int k0 = 0; k0 < nchunks; k0 += kHmChunks) {
+      uint4 ua[kHmChunks], ub[kHmChunks];
+#pragma unroll
+      for (int u = 0; u < kHmChunks; u++) {
+        if (k0 + u < nchunks) {
+          ua[u] = __ldcs(wa + (k0 + u) * 4);  // read once: stream past L2
+          ub[u] = __ldcs(wb + (k0 + u) * 4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kHmChunks; u++) {
+        if (k0 + u >= nchunks) break;
+        const uint2 b0 = *reinterpret_cast<const uint2 *>(xg + (k0 + u) * 32);
+        const uint2 b1 = *reinterpret_cast<const uint2 *>(xg + (k0 + u) * 32 + 4);
+        mma_f16_16816(c, ua[u].x, ub[u].x, ua[u].y, ub[u].y, b0.x, b0.y);
+        mma_f16_16816(c, ua[u].z, ub[u].z, ua[u].w, ub[u].w, b1.x, b1.y);
+      }
+    }
+    // c0, c1: row v0 + g, tokens 2t, 2t + 1; c2, c3: row v0 + g + 8
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int v = v0 + g + 8 * h;
+      if (v >= V) continue;
+#pragma unroll
+      for (int q = 0; q < 2; q++) {
+        const int tok = 2 * t + q;
+        if (tok >= rows) continue;
+        const float val = c[2 * h + q];
+        logits[(size_t)tok * V + v] = val;
+        if (val > bv[q]) {  // v grows along a lane's walk: ties keep the lower index
+          bv[q] = val;
+          bi[q] = v;
+        }
+      }
+    }
+  }
+  if (!amax && !keys) return;
+  // best per token: lanes with the same t (g = 0..7) hold tokens 2t, 2t + 1
+  unsigned long long k0 = argmax_key(bv[0], vocab_offset + bi[0]);
+  unsigned long long k1 = argmax_key(bv[1], vocab_offset + bi[1]);
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    k0 = max(k0, __shfl_xor_sync(0xffffffffu, k0, o));
+    k1 = max(k1, __shfl_xor_sync(0xffffffffu, k1, o));
+  }
+  if (g == 0) {
+    s_key[warp][2 * t] = k0;
+    s_key[warp][2 * t + 1] = k1;
+  }
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    unsigned long long k = 0;
+    for (int w = 0; w < kHmWarps; w++) k = max(k, s_key[w][threadIdx.x]);
+    part[(size_t)blockIdx.x * rows + threadIdx.x] = k;
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(count, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int r = 0; r < rows; r++) {
+    unsigned long long k = 0;
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) k = max(k, __ldcg(part + (size_t)b * rows + r));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) k = max(k, __shfl_xor_sync(0xffffffffu, k, o));
+    if (lane == 0) s_key[warp][0] = k;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long kk = 0;
+      for (int w = 0; w < kHmWarps; w++) kk = max(kk, s_key[w][0]);
+      if (amax) amax[r] = (int32_t)(0xffffffffu - (unsigned)(kk & 0xffffffffu));
+      if (keys) keys[r] = kk ^ 0x8000000000000000ull;  // signed-orderable: an int64 MAX picks it
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = 0;  // ready for the next launch (stream order)
+}
+
 // Per row: the index of the largest logit, the lowest index on ties.
 __global__ void argmax_kernel(const float *logits, int V, int32_t *out) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
@@ -766,9 +917,24 @@ cudaError_t launch_head(const void *x, const float *na, const float *nb, const f
                         unsigned long long *keys, unsigned long long *part, size_t part_bytes, unsigned *count,
                         int num_sms, cudaStream_t s, bool pdl) {
   if (rows > kHeadMaxRows || D % 8) return cudaErrorInvalidValue;
+  const bool norm = na != nullptr;
+  const HeadNorm hn{na, nb, nw, eps};
+  const size_t smem_mma = (size_t)8 * (D + 16) * sizeof(__half);
+  if (D % 32 == 0 && smem_mma <= 200 * 1024) {
+    auto kern = norm ? head_mma_kernel<true> : head_mma_kernel<false>;
+    if (smem_mma > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mma);
+      if (e != cudaSuccess) return e;
+    }
+    int grid = num_sms;
+    const int max_grid = (int)(part_bytes / (sizeof(unsigned long long) * (rows ? rows : 1)));
+    if (grid > max_grid) grid = max_grid;
+    return launch_k(kern, dim3(grid), dim3(kHmThreads), smem_mma, s, pdl, reinterpret_cast<const __half *>(x), hn,
+                    rows, row_stride, D, reinterpret_cast<const __half *>(W), V, vocab_offset, logits, amax, keys,
+                    part, count);
+  }
   const size_t smem = (size_t)rows * D * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  const bool norm = na != nullptr;
   auto kern = norm ? (rows == 1 ? head_kernel<true, 1> : head_kernel<true, kHeadMaxRows>)
                    : (rows == 1 ? head_kernel<false, 1> : head_kernel<false, kHeadMaxRows>);
   if (smem > 48 * 1024) {
@@ -778,7 +944,6 @@ cudaError_t launch_head(const void *x, const float *na, const float *nb, const f
   int grid = num_sms * kHeadCtasPerSm;
   const int max_grid = (int)(part_bytes / (sizeof(unsigned long long) * (rows ? rows : 1)));
   if (grid > max_grid) grid = max_grid;
-  const HeadNorm hn{na, nb, nw, eps};
   return launch_k(kern, dim3(grid), dim3(kHeadThreads), smem, s, pdl, reinterpret_cast<const __half *>(x), hn, rows,
                   row_stride, D, reinterpret_cast<const __half *>(W), V, vocab_offset, logits, amax, keys, part,
                   count);
