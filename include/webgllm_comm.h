@@ -1,0 +1,67 @@
+/*
+ * webgllm_comm.h: tensor-parallel exchange for libwebgllm_b200.so — a
+ * one-shot push all-reduce over NVLink peer memory, fused into the
+ * row-parallel matmul that produces the partial sums.
+ *
+ * No reference counterpart: webgllm runs a model on one device. This is the
+ * exchange of the 8B-shape config split across the GPUs of one node
+ * (o and down projections are row parallel: each rank holds a K slice and
+ * produces a partial [M][N] that must be summed across ranks). NCCL's
+ * all-reduce does the same in a separate launch; here the matmul's own
+ * epilogue stores its partial into every rank's exchange buffer (P2P
+ * stores) and its last CTA raises a per-rank flag (system-scope release);
+ * wg_comm_reduce waits for the flags (at most ~2 s, then WG_TIMEOUT from
+ * wg_sync) and sums the partials from local memory.
+ *
+ * Setup, per rank (one process per GPU): wg_ipc_alloc a buffer, exchange
+ * the 64-byte handles (e.g. an all-gather over torch.distributed),
+ * wg_ipc_open every peer's handle, then wg_comm_init with the world's
+ * buffers in rank order (this rank's own at index rank). Every rank must
+ * issue the same sequence of wg_q4_matmul_push / wg_comm_reduce pairs.
+ */
+#ifndef WEBGLLM_COMM_H
+#define WEBGLLM_COMM_H
+
+#include <stddef.h>
+
+#include "webgllm_q4.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WG_IPC_HANDLE_BYTES 64
+
+typedef struct wg_comm wg_comm;
+
+/* A zeroed device buffer of `bytes` that peers can map; handle receives its
+ * WG_IPC_HANDLE_BYTES-byte CUDA IPC handle. */
+int wg_ipc_alloc(wg_ctx *ctx, size_t bytes, void **dptr, void *handle);
+int wg_ipc_free(wg_ctx *ctx, void *dptr);
+/* Maps a peer's buffer into this context's device. */
+int wg_ipc_open(wg_ctx *ctx, const void *handle, void **dptr);
+int wg_ipc_close(wg_ctx *ctx, void *dptr);
+
+/* An exchange over `world` (<= 8) ranks' buffers of `bytes` each
+ * (buffers[rank] is this rank's own). The caller keeps owning the buffers
+ * and mappings. */
+int wg_comm_init(wg_ctx *ctx, int world, int rank, void *const *buffers, size_t bytes, wg_comm **out);
+int wg_comm_destroy(wg_ctx *ctx, wg_comm *comm);
+/* Floats one rank's partial may hold (M * N of a pushing matmul). */
+int wg_comm_slot(const wg_comm *comm, size_t *floats);
+
+/* y_partial = x . W^T (x as wg_q4_matmul, or made by `pro` as
+ * wg_q4_matmul_fused when pro is not NULL), pushed into every rank's
+ * exchange buffer instead of being stored. M <= 32 (the decode GEMV). */
+int wg_q4_matmul_push(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, const void *x, int x_dtype, int M,
+                      wg_comm *comm);
+
+/* out fp32 [M][N] = the sum over ranks of the next exchange's partials
+ * (waits for every rank's push). */
+int wg_comm_reduce(wg_ctx *ctx, wg_comm *comm, int M, int N, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

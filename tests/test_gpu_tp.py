@@ -44,7 +44,7 @@ def _run(model, prompts, steps):
     return toks, logits
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, push):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
@@ -53,9 +53,10 @@ def _worker(rank, world, port, q):
         from webgllm_b200.model import DecoderModel
 
         cfg = _cfg()
-        m = DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=2, tp=(rank, world, None))
+        m = DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=2, tp=(rank, world, None), push=push)
         prompts = torch.randint(0, cfg.vocab, (2, 24), generator=torch.Generator().manual_seed(3)).cuda()
         toks, logits = _run(m, prompts, 4)
+        m.ctx.sync()  # surfaces a timed-out exchange
         # both vocabulary shards, side by side
         full = []
         for lg in logits:
@@ -63,6 +64,7 @@ def _worker(rank, world, port, q):
             dist.all_gather(parts, lg)
             full.append(torch.cat(parts, dim=1))
         m.graph = None
+        m.close()
         if rank == 0:
             single = DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=2)
             stoks, slog = _run(single, prompts, 4)
@@ -73,16 +75,67 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_tp2_decodes_like_one_gpu():
+def _push_worker(rank, world, port, q):
+    """Three exchanges of a pushing matmul against NCCL's sum of the same
+    local products."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import webgllm_b200 as wg
+        from webgllm_b200.comm import PushComm
+        from webgllm_b200.model import quantize_q4_0
+
+        ctx = wg.context(rank)
+        ctx.use_torch_stream()
+        comm = PushComm(ctx, rank, world)
+        errs = []
+        for it, (M, N, K) in enumerate([(1, 512, 256), (8, 4096, 1024), (3, 1024, 14336 // 2)]):
+            g = torch.Generator(device="cuda")
+            g.manual_seed(100 * it + rank)
+            m = wg.newQuantMatrix(N, K)
+            wg.packQ4_0(m, 0, quantize_q4_0(torch.randn((N, K), generator=g, device="cuda") * 0.02), N)
+            x = torch.randn((M, K), generator=g, device="cuda").half()
+            ref = wg.matmul(x, m, out_dtype=torch.float32)
+            dist.all_reduce(ref)
+            out = torch.full((M, N), float("nan"), device="cuda")
+            ctx.use_torch_stream()
+            comm.push(m, M, x=x)
+            comm.reduce(out, M, N)
+            ctx.sync()  # a missing push would surface here as WG_TIMEOUT
+            errs.append(((out - ref).abs().max() / ref.abs().max()).item())
+        comm.close()
+        q.put((rank, max(errs)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, extra=()):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29500 + random.Random().randrange(0, 2000)
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, 2, port, q, *extra)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return q
+
+
+def test_push_all_reduce_matches_nccl():
+    q = _spawn(_push_worker)
+    for _ in range(2):
+        rank, err = q.get(timeout=10)
+        assert err < 1e-6, (rank, err)
+
+
+@pytest.mark.parametrize("push", [True, False])
+def test_tp2_decodes_like_one_gpu(push):
+    """push: the row-parallel sums go through the fused push all-reduce
+    (decode) and NCCL (prefill); otherwise NCCL everywhere."""
+    q = _spawn(_worker, (push,))
     err, same = q.get(timeout=10)
     assert err < 2e-2, err
     assert all(same), same

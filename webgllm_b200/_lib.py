@@ -73,6 +73,16 @@ SIGNATURES = {
     "wg_pick_keys": (_I, [_P, _P, _I, _P]),
     "wg_argmax": (_I, [_P, _P, _I, _I, _P]),
     "wg_add_i32": (_I, [_P, _P, _I, _I]),
+    # include/webgllm_comm.h
+    "wg_ipc_alloc": (_I, [_P, _SZ, _PP, _P]),
+    "wg_ipc_free": (_I, [_P, _P]),
+    "wg_ipc_open": (_I, [_P, _P, _PP]),
+    "wg_ipc_close": (_I, [_P, _P]),
+    "wg_comm_init": (_I, [_P, _I, _I, _P, _SZ, _PP]),
+    "wg_comm_destroy": (_I, [_P, _P]),
+    "wg_comm_slot": (_I, [_P, ctypes.POINTER(_SZ)]),
+    "wg_q4_matmul_push": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "wg_comm_reduce": (_I, [_P, _P, _I, _I, _P]),
     "wg_error_string": (ctypes.c_char_p, [_I]),
     "wg_last_error": (ctypes.c_char_p, [_P]),
 }

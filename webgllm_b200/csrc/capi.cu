@@ -461,10 +461,12 @@ bool use_wide(const wg_ctx *ctx, const wg::GemvArgs &a) {
 // The matmul behind wg_q4_matmul and wg_q4_matmul_fused: y = x . W^T, with
 // x given (pro == null) or made by a prologue. Arguments are checked.
 int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y, int y_dtype,
-               const wg::Prologue *pro) {
+               const wg::Prologue *pro, const wg_comm *push = nullptr) {
   int st = use_device(ctx);
   if (st) return st;
   const size_t K = m->d.K;
+  if (push && M > wg::kGemvMaxTokens)
+    return fail(ctx, WG_UNSUPPORTED, "a pushing matmul takes at most %d rows (got %d)", wg::kGemvMaxTokens, M);
   // Many rows: the tcgen05 GEMM (src/engine.ts:4684: more rows than the
   // split path takes go to the prompt matmul).
   if (M > wg::kGemvMaxTokens && wg::gemm_supported()) {
@@ -534,6 +536,10 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     a.launch_index = ctx->launch_index++;
     a.trigger_at = ctx->trigger_at;
     if (pro) a.pro = *pro;  // M <= kProMaxTokens: one launch
+    if (push) {
+      a.push_on = 1;
+      a.push = push->dev;
+    }
     wg::GemvArgs w = a;
     if (use_wide(ctx, a) && wg::plan_gemv_wide(w, ctx->num_sms)) {
       WG_CUDA(ctx, wg::launch_gemv_wide(w, ctx->stream, ctx->pdl));
@@ -573,6 +579,38 @@ int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int
   int st = check_matmul(ctx, m, M, y, y_dtype);
   if (st) return st;
   return run_matmul(ctx, m, x, x_dtype, M, y, y_dtype, nullptr);
+}
+
+int wg_q4_matmul_push(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, const void *x, int x_dtype, int M,
+                      wg_comm *comm) {
+  if (!ctx || !m || !comm) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_push: null argument");
+  if (M < 0) return fail(ctx, WG_INVALID_ARGUMENT, "negative row count %d", M);
+  if (M == 0) return WG_OK;
+  if (m->device != ctx->device || comm->device != ctx->device)
+    return fail(ctx, WG_INVALID_ARGUMENT, "matrix, exchange and context must share a device");
+  if ((size_t)M * m->d.N > (size_t)comm->dev.slot)
+    return fail(ctx, WG_UNSUPPORTED, "%d x %d outputs exceed the exchange slot (%lld floats)", M, m->d.N,
+                (long long)comm->dev.slot);
+  if (pro) {
+    wg::Prologue p{};
+    p.kind = pro->kind;
+    p.a = pro->a;
+    p.b = pro->b;
+    p.w = pro->weight;
+    p.eps = pro->eps;
+    p.out = pro->resid_out;
+    if (p.kind != WG_PRO_RMSNORM && p.kind != WG_PRO_SWIGLU)
+      return fail(ctx, WG_INVALID_ARGUMENT, "unknown prologue kind %d", p.kind);
+    if (!p.a || (p.kind == WG_PRO_RMSNORM && !p.w))
+      return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_push: null prologue input");
+    if (!aligned16(p.a) || !aligned16(p.b) || !aligned16(p.w) || !aligned16(p.out))
+      return fail(ctx, WG_INVALID_ARGUMENT, "prologue tensors must be 16-byte aligned");
+    if (p.kind == WG_PRO_SWIGLU) p.b = nullptr, p.w = nullptr, p.out = nullptr;
+    return run_matmul(ctx, m, nullptr, WG_F16, M, nullptr, WG_F32, &p, comm);
+  }
+  if (!x || !aligned16(x)) return fail(ctx, WG_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer");
+  if (x_dtype < WG_F32 || x_dtype > WG_BF16) return fail(ctx, WG_INVALID_ARGUMENT, "unknown x dtype %d", x_dtype);
+  return run_matmul(ctx, m, x, x_dtype, M, nullptr, WG_F32, nullptr, comm);
 }
 
 int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, int M, void *y, int y_dtype) {

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <string>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "q4_layout.cuh"
 
@@ -33,6 +34,15 @@ struct wg_ctx {
   unsigned long long *d_trace_next = nullptr;  // device record counter
   unsigned launch_index = 0;
   std::string last_error;
+};
+
+// A tensor-parallel exchange (comm.cuh): this rank's view of every rank's
+// buffer (the caller owns the buffers and their mappings).
+struct wg_comm {
+  int device;
+  int world, rank;
+  size_t bytes;
+  wg::CommDev dev;
 };
 
 struct wg_q4mat {

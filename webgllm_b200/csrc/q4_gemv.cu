@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L.bar) + warp;
   __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
+  const int parity = a.push_on ? push_parity(a.push) : 0;
 
   // 1. Each warp starts the copies of its own tiles (the TMA engine, one
   //    mbarrier a warp): weights depend on nothing the previous kernel
@@ -356,7 +357,12 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
       part[o] = s;
     } else {
       const int n = nt * kTileRows + r;
-      if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
+      if (n < a.N && tok < M) {
+        if (a.push_on)
+          push_store(a.push, parity, n, tok, M, s);
+        else
+          store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
+      }
     }
   }
 
@@ -370,7 +376,12 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
       for (int c = 0; c < C; c++) s += cluster.map_shared_rank(part, c)[o];
       const int r = o / (8 * NG), tok = o - r * (8 * NG);
       const int n = nt * kTileRows + r;
-      if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
+      if (n < a.N && tok < M) {
+        if (a.push_on)
+          push_store(a.push, parity, n, tok, M, s);
+        else
+          store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
+      }
     }
     cluster.sync();
   }
@@ -378,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
   // 7. No copy may still be writing this CTA's shared memory when it exits
   //    (only possible after a timed-out wait).
   if (lane == 0 && nw > 0) mbar_wait_bounded(bar, 0, a.flags);
+  if (a.push_on) push_signal(a.push);
   if (a.trace && threadIdx.x == 0) {
     ts[5] = globaltimer();
     trace_record(a.trace, a.trace_next, a.trace_cap, ts, a.launch_index, blockIdx.y * gridDim.x + blockIdx.x);
@@ -525,6 +537,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   const int nib_b = ktc * kTileNibBytes, scl_b = ktc * kTileSclBytes;
   __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
+  const int parity = a.push_on ? push_parity(a.push) : 0;
 
   auto issue = [&](int j) {  // thread 0: column g + j*G (this CTA's K range) into stage j % S
     const int st = j % S;
@@ -632,7 +645,12 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
         part[j * kOut + o] = sum;
       } else {
         const int n = nt * kTileRows + r;
-        if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
+        if (n < a.N && tok < M) {
+          if (a.push_on)
+            push_store(a.push, parity, n, tok, M, sum);
+          else
+            store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
+        }
       }
     }
     __syncthreads();  // red is reused by the next column
@@ -651,7 +669,12 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
       const int j = idx / kOut, o = idx - j * kOut;
       const int r = o / 8, tok = o - r * 8;
       const int n = (g + j * G) * kTileRows + r;
-      if (n < a.N && tok < M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
+      if (n < a.N && tok < M) {
+        if (a.push_on)
+          push_store(a.push, parity, n, tok, M, sum);
+        else
+          store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
+      }
     }
     cluster.sync();
   }
@@ -661,6 +684,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
     if (x_bulk) mbar_wait_bounded(xbar, 0, a.flags);
     for (int j = max(0, J - S); j < J; j++) mbar_wait_bounded(&bars[j % S], (j / S) & 1, a.flags);
   }
+  if (a.push_on) push_signal(a.push);
   if (a.trace && threadIdx.x == 0) {
     ts[5] = globaltimer();
     trace_record(a.trace, a.trace_next, a.trace_cap, ts, a.launch_index, blockIdx.y * gridDim.x + blockIdx.x);

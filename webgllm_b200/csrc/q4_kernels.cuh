@@ -4,6 +4,7 @@
 
 #include <cstdint>
 
+#include "comm.cuh"
 #include "q4_layout.cuh"
 
 namespace wg {
@@ -68,6 +69,8 @@ struct GemvArgs {
   Prologue pro;    // kProNone: x as given; else x is made from pro (M <= kProMaxTokens)
   int groups;      // wide GEMV: column groups (grid.y)
   int stages;      // wide GEMV: weight ring stages per warp
+  int push_on;     // outputs go to every rank's exchange buffer (comm.cuh), not y
+  CommDev push;
 };
 
 constexpr int kGemvMaxTokens = 32;

@@ -119,7 +119,7 @@ class DecoderModel:
 
     def __init__(self, cfg: DecoderConfig, seed: int = 0, max_ctx: int = 1024, max_rows: int = 512,
                  keep_blocks: bool = False, device: int | None = None, fused: bool = True, batch: int = 1,
-                 tp=None):
+                 tp=None, push: bool = True):
         self.cfg = cfg
         self.fused = fused
         self.batch = batch
@@ -197,6 +197,13 @@ class DecoderModel:
         self.ids = torch.zeros(R, dtype=torch.int32, device="cuda")
         self.next_id = torch.zeros(B, dtype=torch.int32, device="cuda")
         self.graph = None
+        # row-parallel exchange: the push all-reduce for decode rows, NCCL
+        # for the rest (and for everything when push is False)
+        self.comm = None
+        if world > 1 and push:
+            from .comm import PushComm
+
+            self.comm = PushComm(self.ctx, rank, world, self.group)
 
     # -- low level ---------------------------------------------------------
 
@@ -256,8 +263,27 @@ class DecoderModel:
                              P(kc.data_ptr()), P(vc.data_ptr()), self.max_ctx))
         self._c(L.wg_attention(c, P(self.q.data_ptr()), rows, self.batch, H, Hkv, Dh, P(kc.data_ptr()),
                                P(vc.data_ptr()), self.max_ctx, P(self.pos.data_ptr()), P(self.att.data_ptr())))
-        self._mm(lay["o"], self.att, self.o, rows)
+        self._mm_rowpar(lay["o"], rows, x=self.att)
+
+    def _mm_rowpar(self, lin: Linear, rows: int, x=None, pro=None):
+        """self.o[:rows] = the sum over ranks of this rank's partial x . W^T
+        (x given, or made by the prologue `pro`)."""
+        D = self.cfg.hidden
+        if self.comm is not None and rows <= 8 and rows * D <= self.comm.slot:
+            self.comm.push(lin.m, rows, x=x, pro=pro)
+            self.comm.reduce(self.o, rows, D)
+            return
+        if pro is not None:
+            self._c(_lib.lib().wg_q4_matmul_fused(P(self.ctx.handle), P(lin.m.handle), ctypes.byref(pro), rows,
+                                                  P(self.o.data_ptr()), WG_F32))
+        else:
+            self._mm(lin, x, self.o, rows)
         self._all_reduce(self.o[:rows])
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     def _convolve(self, lay, rows):
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
@@ -309,8 +335,8 @@ class DecoderModel:
                 self._convolve(lay, rows)
             self._mm_norm(lay["gu"], cur, self.o, lay["norm2"], other, self.gu, rows)
             cur, other = other, cur
-            self._mm_swiglu(lay["down"], self.gu, self.o, rows)
-            self._all_reduce(self.o[:rows])
+            self._mm_rowpar(lay["down"], rows, pro=_lib.wg_prologue(WG_PRO_SWIGLU, self.gu.data_ptr(), None, None,
+                                                                    0.0, None))
             add = self.o
         self._head(cur, add, rows)
 

@@ -34,13 +34,14 @@ def step_bytes(m: DecoderModel, ctx_len: float) -> float:
     return q4 + head + m.batch * cfg.hidden * 2 + kv
 
 
-def measure(cfg, batch: int, prompt_len: int, gen_len: int, tp=None, seed: int = 0, barrier=None) -> dict:
+def measure(cfg, batch: int, prompt_len: int, gen_len: int, tp=None, seed: int = 0, barrier=None,
+            push: bool = True) -> dict:
     """Prefill `batch` random prompts of `prompt_len` tokens and generate
     `gen_len` tokens each (the first from the prefill, the rest from graph
     replays). Device-timed with CUDA events; `barrier` (if given) runs before
     and after the timed region."""
     m = DecoderModel(cfg, seed=seed, max_ctx=prompt_len + gen_len + 8, max_rows=batch * prompt_len, batch=batch,
-                     tp=tp)
+                     tp=tp, push=push)
     g = torch.Generator().manual_seed(seed + 1)
     prompts = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=g).to("cuda", torch.int32)
     out = torch.zeros((batch, gen_len), dtype=torch.int32, device="cuda")
@@ -79,6 +80,8 @@ def measure(cfg, batch: int, prompt_len: int, gen_len: int, tp=None, seed: int =
         "step_bytes": step_bytes(m, prompt_len + gen_len / 2),
         "tokens_head": out[:, :8].tolist(),
     }
+    m.graph = None
+    m.close()
     del m
     torch.cuda.empty_cache()
     return res
