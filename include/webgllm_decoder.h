@@ -61,6 +61,11 @@ int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv
  * [rows][2I] (gate | up) -> out[r][i] = silu(gate) * up, in out_dtype. */
 int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int out_dtype);
 
+/* The same for a gate|up matrix packed interleaved by 8 (see
+ * WG_EPI_SWIGLU_PAIRS): gate_up [rows][2I] with columns 16t .. 16t+7 = gate
+ * features 8t .. 8t+7 and 16t+8 .. 16t+15 = their up values. I % 8 == 0. */
+int wg_swiglu_pairs(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int out_dtype);
+
 /* LFM2 gated short convolution (shortConv / convState,
  * src/gpu/kernels.ts:1380-1437): bcx fp32 [rows][3D] = B | C | x,
  * y = B * x, out[t] = C[t] * sum_k weight[c][k] * y[t - (W-1-k)] (weight fp32

@@ -187,6 +187,20 @@ typedef struct wg_prologue {
 int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro,
                        int M, void *y, int y_dtype);
 
+/* Epilogues of wg_q4_matmul_ex. */
+#define WG_EPI_SWIGLU_PAIRS 1 /* REDUCE_SWIGLU (src/gpu/kernels.ts:1066) in the matmul's epilogue */
+
+/* The matmul with an optional prologue (as wg_q4_matmul_fused; x unused
+ * then) and epilogue. WG_EPI_SWIGLU_PAIRS: the matrix is a gate|up pair
+ * whose rows were packed interleaved by 8 (rows 16t .. 16t+7 = gate rows
+ * 8t .. 8t+7, rows 16t+8 .. 16t+15 = the same up rows; packQ4_0's srcRows
+ * does this at load time), and y [M][N/2] receives silu(gate) * up, so the
+ * gate|up product is never stored. Epilogues run in the decode GEMV
+ * (M <= 32, N % 16 == 0). */
+int wg_q4_matmul_ex(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro,
+                    const void *x, int x_dtype, int M, void *y, int y_dtype,
+                    int epilogue);
+
 /* ---- tracing ------------------------------------------------------------- */
 
 /* Gpu.trace / drawTrace (src/gpu/gl.ts:553-598), per CTA instead of per

@@ -497,3 +497,43 @@ def test_matmul_fused_rejects_aliasing_and_bad_kind():
     pro = _lib.wg_prologue(7, a.data_ptr(), None, w.data_ptr(), 1e-5, None)
     assert lib().wg_q4_matmul_fused(P(c.handle), P(m.handle), ctypes.byref(pro), 1, ptr(y), WG_F32) == \
         _lib.WG_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("rows,I,K", [(1, 2816, 2048), (3, 1024, 8192), (8, 14336 // 8, 4096), (20, 512, 1024)])
+def test_matmul_swiglu_pairs_epilogue(rows, I, K):
+    """gate|up packed interleaved by 8 (model.swiglu_pairs_perm): the
+    epilogue's silu(gate) * up equals SwiGLU of the plain product, with and
+    without the norm prologue; wg_swiglu_pairs does the same from a stored
+    interleaved product."""
+    from webgllm_b200.model import dequantize_q4_0, quantize_q4_0, swiglu_pairs_perm
+
+    g = gen(rows + I + K)
+    w = torch.randn((2 * I, K), generator=g, device="cuda") * 0.02
+    blocks = quantize_q4_0(w)
+    Wd = dequantize_q4_0(blocks, 2 * I, K)
+    m = wg.newQuantMatrix(2 * I, K)
+    perm = swiglu_pairs_perm(I)
+    wg.packQ4_0(m, 0, blocks, 2 * I, perm)
+    x = torch.randn((rows, K), generator=g, device="cuda").half()
+    act = torch.empty((rows, I), dtype=torch.float16, device="cuda")
+    c = ctx()
+    _lib.check(lib().wg_q4_matmul_ex(P(c.handle), P(m.handle), None, ptr(x), WG_F16, rows, ptr(act), WG_F16,
+                                     _lib.WG_EPI_SWIGLU_PAIRS), c.handle)
+    torch.cuda.synchronize()
+    want = R.swiglu(x.float() @ Wd.t(), I)
+    assert rel(act, want) < 2e-3
+    # with the norm prologue
+    a = torch.randn((rows, K), generator=g, device="cuda")
+    nw = torch.rand(K, generator=g, device="cuda") + 0.5
+    pro = _lib.wg_prologue(_lib.WG_PRO_RMSNORM, a.data_ptr(), None, nw.data_ptr(), 1e-5, None)
+    _lib.check(lib().wg_q4_matmul_ex(P(c.handle), P(m.handle), ctypes.byref(pro), None, WG_F16, rows, ptr(act),
+                                     WG_F16, _lib.WG_EPI_SWIGLU_PAIRS), c.handle)
+    torch.cuda.synchronize()
+    _, h = R.rmsnorm(a, None, nw, 1e-5)
+    assert rel(act, R.swiglu(h.half().float() @ Wd.t(), I)) < 2e-3
+    # stored interleaved product, then the pairs pass
+    gu = torch.empty((rows, 2 * I), device="cuda")
+    _lib.check(lib().wg_q4_matmul(P(c.handle), P(m.handle), ptr(x), WG_F16, rows, ptr(gu), WG_F32), c.handle)
+    act2 = torch.empty((rows, I), dtype=torch.float16, device="cuda")
+    call(lib().wg_swiglu_pairs, ptr(gu), rows, I, ptr(act2), WG_F16)
+    assert rel(act2, want) < 2e-3

@@ -25,6 +25,7 @@ WG_NO_DEVICE = 10
 
 WG_F32, WG_F16, WG_BF16 = 0, 1, 2
 WG_PRO_RMSNORM, WG_PRO_SWIGLU = 1, 2
+WG_EPI_SWIGLU_PAIRS = 1
 
 
 class wg_prologue(ctypes.Structure):
@@ -59,6 +60,7 @@ SIGNATURES = {
     "wg_q4_matmul": (_I, [_P, _P, _P, _I, _I, _P, _I]),
     "wg_q4_matmul_static": (_I, [_P, _P, _P, _I, _I, _P, _I]),
     "wg_q4_matmul_fused": (_I, [_P, _P, _P, _I, _P, _I]),
+    "wg_q4_matmul_ex": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, _I]),
     "wg_trace": (_I, [_P, _P, _SZ]),
     "wg_trace_count": (_I, [_P, ctypes.POINTER(_SZ)]),
     # include/webgllm_decoder.h
@@ -67,6 +69,7 @@ SIGNATURES = {
     "wg_rope_kv": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, ctypes.c_float, _P, _P, _P, _I]),
     "wg_attention": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P]),
     "wg_swiglu": (_I, [_P, _P, _I, _I, _P, _I]),
+    "wg_swiglu_pairs": (_I, [_P, _P, _I, _I, _P, _I]),
     "wg_short_conv": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
     "wg_head": (_I, [_P, _P, _I, _I, _P, _I, _P, _P]),
     "wg_head_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _I, _P, _I, _I, _P, _P, _P]),

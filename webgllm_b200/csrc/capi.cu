@@ -461,10 +461,13 @@ bool use_wide(const wg_ctx *ctx, const wg::GemvArgs &a) {
 // The matmul behind wg_q4_matmul and wg_q4_matmul_fused: y = x . W^T, with
 // x given (pro == null) or made by a prologue. Arguments are checked.
 int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y, int y_dtype,
-               const wg::Prologue *pro, const wg_comm *push = nullptr) {
+               const wg::Prologue *pro, const wg_comm *push = nullptr, int epi = wg::kEpiNone) {
   int st = use_device(ctx);
   if (st) return st;
   const size_t K = m->d.K;
+  if (epi != wg::kEpiNone && (M > wg::kGemvMaxTokens || push || m->d.N % 16))
+    return fail(ctx, WG_UNSUPPORTED, "the SwiGLU-pairs epilogue takes at most %d rows, N %% 16 == 0 (M %d, N %d)",
+                wg::kGemvMaxTokens, M, m->d.N);
   if (push && M > wg::kGemvMaxTokens)
     return fail(ctx, WG_UNSUPPORTED, "a pushing matmul takes at most %d rows (got %d)", wg::kGemvMaxTokens, M);
   // Many rows: the tcgen05 GEMM (src/engine.ts:4684: more rows than the
@@ -540,6 +543,7 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
       a.push_on = 1;
       a.push = push->dev;
     }
+    a.epi = epi;
     wg::GemvArgs w = a;
     if (use_wide(ctx, a) && wg::plan_gemv_wide(w, ctx->num_sms)) {
       WG_CUDA(ctx, wg::launch_gemv_wide(w, ctx->stream, ctx->pdl));
@@ -611,6 +615,39 @@ int wg_q4_matmul_push(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, co
   if (!x || !aligned16(x)) return fail(ctx, WG_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer");
   if (x_dtype < WG_F32 || x_dtype > WG_BF16) return fail(ctx, WG_INVALID_ARGUMENT, "unknown x dtype %d", x_dtype);
   return run_matmul(ctx, m, x, x_dtype, M, nullptr, WG_F32, nullptr, comm);
+}
+
+int wg_q4_matmul_ex(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, const void *x, int x_dtype, int M,
+                    void *y, int y_dtype, int epilogue) {
+  if (!ctx || !m) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_ex: null argument");
+  int st = check_matmul(ctx, m, M, y, y_dtype);
+  if (st) return st;
+  if (M == 0) return WG_OK;
+  if (epilogue != 0 && epilogue != WG_EPI_SWIGLU_PAIRS)
+    return fail(ctx, WG_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
+  const int epi = epilogue == WG_EPI_SWIGLU_PAIRS ? wg::kEpiSwigluPairs : wg::kEpiNone;
+  if (pro) {
+    wg::Prologue p{};
+    p.kind = pro->kind;
+    p.a = pro->a;
+    p.b = pro->b;
+    p.w = pro->weight;
+    p.eps = pro->eps;
+    p.out = pro->resid_out;
+    if (p.kind != WG_PRO_RMSNORM && p.kind != WG_PRO_SWIGLU)
+      return fail(ctx, WG_INVALID_ARGUMENT, "unknown prologue kind %d", p.kind);
+    if (!p.a || (p.kind == WG_PRO_RMSNORM && !p.w))
+      return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_ex: null prologue input");
+    if (!aligned16(p.a) || !aligned16(p.b) || !aligned16(p.w) || !aligned16(p.out))
+      return fail(ctx, WG_INVALID_ARGUMENT, "prologue tensors must be 16-byte aligned");
+    if (p.out && (p.out == p.a || (p.b && p.out == p.b)))
+      return fail(ctx, WG_INVALID_ARGUMENT, "resid_out must not alias the residual or the addend");
+    if (p.kind == WG_PRO_SWIGLU) p.b = nullptr, p.w = nullptr, p.out = nullptr;
+    return run_matmul(ctx, m, nullptr, WG_F16, M, y, y_dtype, &p, nullptr, epi);
+  }
+  if (!x || !aligned16(x)) return fail(ctx, WG_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer");
+  if (x_dtype < WG_F32 || x_dtype > WG_BF16) return fail(ctx, WG_INVALID_ARGUMENT, "unknown x dtype %d", x_dtype);
+  return run_matmul(ctx, m, x, x_dtype, M, y, y_dtype, nullptr, nullptr, epi);
 }
 
 int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, int M, void *y, int y_dtype) {

@@ -107,6 +107,15 @@ int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int
   return finish(ctx, wg::launch_swiglu(gate_up, rows, I, out, out_dtype, ctx->stream, ctx->pdl), "wg_swiglu");
 }
 
+int wg_swiglu_pairs(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int out_dtype) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || I <= 0 || I % 8) return dfail(ctx, WG_INVALID_SHAPE, "wg_swiglu_pairs: bad shape (I %d)", I);
+  if (!rows) return WG_OK;
+  if (!gate_up || !out || !dtype_ok(out_dtype)) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_swiglu_pairs: argument");
+  return finish(ctx, wg::launch_swiglu_pairs(gate_up, rows, I, out, out_dtype, ctx->stream, ctx->pdl),
+                "wg_swiglu_pairs");
+}
+
 int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int batch, int D, int W, const float *weight,
                   void *state, void *out, int out_dtype) {
   WG_BEGIN(ctx);

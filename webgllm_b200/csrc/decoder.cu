@@ -389,6 +389,20 @@ __global__ void swiglu_kernel(const float *gu, int rows, int I, void *out, int o
   }
 }
 
+// gate|up rows interleaved by 8 per 16-row tile (the SwiGLU-pairs packing):
+// out[r][8t + i] = silu(gu[r][16t + i]) * gu[r][16t + 8 + i].
+__global__ void swiglu_pairs_kernel(const float *gu, int rows, int I, void *out, int out_dtype) {
+  pdl_trigger();
+  pdl_wait();
+  const size_t n = (size_t)rows * I;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / I, f = i - r * I;
+    const size_t col = (f / 8) * 16 + (f % 8);
+    const float g = gu[r * 2 * I + col], u = gu[r * 2 * I + col + 8];
+    store_out(out, out_dtype, i, g / (1.0f + expf(-g)) * u);
+  }
+}
+
 // ---- gated short conv (shortConv / convState kernels.ts:1380-1437) --------
 // bcx [rows][3D] = B | C | x; y_t = B_t x_t; out_t = C_t * sum_k w[c][k]
 // y_{t - (W-1-k)}; y before the batch comes from the fp16 state [W-1][D]
@@ -900,6 +914,14 @@ cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_d
   const size_t n = (size_t)rows * I;
   const size_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
   return launch_k(swiglu_kernel, dim3((unsigned)(blocks ? blocks : 1)), dim3(256), 0, s, pdl, gu, rows, I, out,
+                  out_dtype);
+}
+
+cudaError_t launch_swiglu_pairs(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s,
+                                bool pdl) {
+  const size_t n = (size_t)rows * I;
+  const size_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+  return launch_k(swiglu_pairs_kernel, dim3((unsigned)(blocks ? blocks : 1)), dim3(256), 0, s, pdl, gu, rows, I, out,
                   out_dtype);
 }
 

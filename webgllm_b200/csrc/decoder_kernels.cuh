@@ -22,6 +22,8 @@ cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv,
                              const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s,
                              bool pdl);
 cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s, bool pdl);
+cudaError_t launch_swiglu_pairs(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s,
+                                bool pdl);
 cudaError_t launch_short_conv(const float *bcx, int rows, int batch, int D, int W, const float *w, void *state,
                               void *out, int out_dtype, cudaStream_t s, bool pdl);
 // x fp16 [rows][D], or with na != null the norm rmsnorm(na + nb) * nw; input

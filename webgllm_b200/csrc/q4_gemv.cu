@@ -156,6 +156,23 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
+// The final value of output row n (tile nt, row r) for token tok: stored,
+// pushed to the exchange, or (SwiGLU pairs, only rows r < 8 of a tile,
+// given the paired up value) activated into y [M][N/2].
+__device__ __forceinline__ void emit(const GemvArgs &a, int parity, int nt, int r, int tok, float v) {
+  const int n = nt * kTileRows + r;
+  if (n >= a.N || tok >= a.M) return;
+  if (a.push_on)
+    push_store(a.push, parity, n, tok, a.M, v);
+  else
+    store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, v);
+}
+__device__ __forceinline__ void emit_pair(const GemvArgs &a, int nt, int r, int tok, float gate, float up) {
+  const int f = nt * (kTileRows / 2) + r;  // feature: tile nt holds gate / up rows of features 8nt .. 8nt+7
+  if (nt * kTileRows + r >= a.N || tok >= a.M) return;
+  store_out(a.y, a.y_dtype, (size_t)tok * (a.N / 2) + f, silu_mul(gate, up));
+}
+
 // Eight consecutive x values (row m, columns k..k+7) as fp16, made by the
 // prologue: (residual + b) * inv * w for the norm, silu(gate) * up for SwiGLU.
 template <int PRO>
@@ -220,7 +237,7 @@ __device__ void rmsnorm_rows(const Prologue &p, int M, int K, float *s_part, flo
 }
 
 template <int NG, bool ZEROS, int PRO>
-__global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = lane & 3;
@@ -345,24 +362,28 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
   if (a.trace && threadIdx.x == 0) ts[4] = globaltimer();
   constexpr int kOut = 16 * 8 * NG;
   const int C = a.cluster;
-  for (int o = threadIdx.x; o < kOut; o += kThreads) {
-    const int r = o / (8 * NG), tok = o - r * (8 * NG);
+  auto warp_sum_at = [&](int r, int tok) {  // sum over the 8 warps of output (r, tok)
     const int ng = tok >> 3, tk = tok & 7;
     const int ln = 4 * (r & 7) + (tk >> 1);
     const int e = ((r >> 3) << 1) | (tk & 1);
     float s = 0.0f;
 #pragma unroll
     for (int w2 = 0; w2 < kWarps; w2++) s += red[((w2 * NG + ng) * 4 + e) * 32 + ln];
-    if (C > 1) {
-      part[o] = s;
-    } else {
-      const int n = nt * kTileRows + r;
-      if (n < a.N && tok < M) {
-        if (a.push_on)
-          push_store(a.push, parity, n, tok, M, s);
-        else
-          store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
-      }
+    return s;
+  };
+  if (C > 1 || a.epi == kEpiNone) {
+    for (int o = threadIdx.x; o < kOut; o += kThreads) {
+      const int r = o / (8 * NG), tok = o - r * (8 * NG);
+      const float s = warp_sum_at(r, tok);
+      if (C > 1)
+        part[o] = s;
+      else
+        emit(a, parity, nt, r, tok, s);
+    }
+  } else {
+    for (int o = threadIdx.x; o < kOut / 2; o += kThreads) {
+      const int r = o / (8 * NG), tok = o - r * (8 * NG);
+      emit_pair(a, nt, r, tok, warp_sum_at(r, tok), warp_sum_at(r + 8, tok));
     }
   }
 
@@ -371,17 +392,19 @@ __global__ void __launch_bounds__(kThreads, NG <= 2 ? 4 : 2) gemv_kernel(const G
   if (C > 1) {
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    for (int o = crank + C * (int)threadIdx.x; o < kOut; o += C * kThreads) {
-      float s = 0.0f;
-      for (int c = 0; c < C; c++) s += cluster.map_shared_rank(part, c)[o];
+    const int nout = a.epi == kEpiNone ? kOut : kOut / 2;
+    for (int o = crank + C * (int)threadIdx.x; o < nout; o += C * kThreads) {
       const int r = o / (8 * NG), tok = o - r * (8 * NG);
-      const int n = nt * kTileRows + r;
-      if (n < a.N && tok < M) {
-        if (a.push_on)
-          push_store(a.push, parity, n, tok, M, s);
-        else
-          store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, s);
+      float s = 0.0f, u = 0.0f;
+      for (int c = 0; c < C; c++) {
+        const float *pc = cluster.map_shared_rank(part, c);
+        s += pc[o];
+        if (a.epi != kEpiNone) u += pc[o + kOut / 2];  // row r + 8: index + 8 * 8NG
       }
+      if (a.epi == kEpiNone)
+        emit(a, parity, nt, r, tok, s);
+      else
+        emit_pair(a, nt, r, tok, s, u);
     }
     cluster.sync();
   }
@@ -634,23 +657,27 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
     __syncthreads();
     if (threadIdx.x == 0 && j + S < J) issue(j + S);  // every warp is done with the stage
     const int nt = g + j * G;
-    for (int o = threadIdx.x; o < kOut; o += kWThreads) {
-      const int r = o / 8, tok = o - r * 8;
+    auto warp_sum_at = [&](int r, int tok) {
       const int ln = 4 * (r & 7) + (tok >> 1);
       const int e = ((r >> 3) << 1) | (tok & 1);
       float sum = 0.0f;
 #pragma unroll
       for (int w2 = 0; w2 < kWWarps; w2++) sum += red[(w2 * 4 + e) * 32 + ln];
-      if (C > 1) {
-        part[j * kOut + o] = sum;
-      } else {
-        const int n = nt * kTileRows + r;
-        if (n < a.N && tok < M) {
-          if (a.push_on)
-            push_store(a.push, parity, n, tok, M, sum);
-          else
-            store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
-        }
+      return sum;
+    };
+    if (C > 1 || a.epi == kEpiNone) {
+      for (int o = threadIdx.x; o < kOut; o += kWThreads) {
+        const int r = o / 8, tok = o - r * 8;
+        const float sum = warp_sum_at(r, tok);
+        if (C > 1)
+          part[j * kOut + o] = sum;
+        else
+          emit(a, parity, nt, r, tok, sum);
+      }
+    } else {
+      for (int o = threadIdx.x; o < kOut / 2; o += kWThreads) {
+        const int r = o / 8, tok = o - r * 8;
+        emit_pair(a, nt, r, tok, warp_sum_at(r, tok), warp_sum_at(r + 8, tok));
       }
     }
     __syncthreads();  // red is reused by the next column
@@ -663,18 +690,20 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   if (C > 1) {
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    for (int idx = crank + C * (int)threadIdx.x; idx < J * kOut; idx += C * kWThreads) {
-      float sum = 0.0f;
-      for (int c = 0; c < C; c++) sum += cluster.map_shared_rank(part, c)[idx];
-      const int j = idx / kOut, o = idx - j * kOut;
+    const int per = a.epi == kEpiNone ? kOut : kOut / 2;  // outputs per column
+    for (int idx = crank + C * (int)threadIdx.x; idx < J * per; idx += C * kWThreads) {
+      const int j = idx / per, o = idx - j * per;
       const int r = o / 8, tok = o - r * 8;
-      const int n = (g + j * G) * kTileRows + r;
-      if (n < a.N && tok < M) {
-        if (a.push_on)
-          push_store(a.push, parity, n, tok, M, sum);
-        else
-          store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, sum);
+      float sum = 0.0f, up = 0.0f;
+      for (int c = 0; c < C; c++) {
+        const float *pc = cluster.map_shared_rank(part, c) + j * kOut;
+        sum += pc[o];
+        if (a.epi != kEpiNone) up += pc[o + kOut / 2];  // row r + 8
       }
+      if (a.epi == kEpiNone)
+        emit(a, parity, g + j * G, r, tok, sum);
+      else
+        emit_pair(a, g + j * G, r, tok, sum, up);
     }
     cluster.sync();
   }

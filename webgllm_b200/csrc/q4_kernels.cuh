@@ -71,7 +71,9 @@ struct GemvArgs {
   int stages;      // wide GEMV: weight ring stages per warp
   int push_on;     // outputs go to every rank's exchange buffer (comm.cuh), not y
   CommDev push;
+  int epi;         // kEpiNone, or kEpiSwigluPairs: y [M][N/2] = silu(rows 16t..16t+7) * rows 16t+8..16t+15
 };
+enum EpiKind { kEpiNone = 0, kEpiSwigluPairs = 1 };
 
 constexpr int kGemvMaxTokens = 32;
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl);

@@ -94,13 +94,24 @@ def dequantize_q4_0(blocks: torch.Tensor, N: int, K: int) -> torch.Tensor:
 class Linear:
     """A Q4_0 matrix on the device (and its GGUF bytes, for references)."""
 
-    def __init__(self, ctx, blocks: torch.Tensor, N: int, K: int, keep_blocks=False):
+    def __init__(self, ctx, blocks: torch.Tensor, N: int, K: int, keep_blocks=False, perm=None):
         self.N, self.K = N, K
         self.m: QuantMatrix = newQuantMatrix(N, K, ctx=ctx)
         ctx.use_torch_stream()
-        packQ4_0(self.m, 0, blocks, N)
+        packQ4_0(self.m, 0, blocks, N, perm)
         torch.cuda.synchronize()
         self.blocks = blocks if keep_blocks else None
+
+
+def swiglu_pairs_perm(I: int):
+    """Row order of a gate|up matrix [2I] for the SwiGLU-pairs epilogue
+    (WG_EPI_SWIGLU_PAIRS): destination row 16t + i is gate row 8t + i for
+    i < 8 and up row I + 8t + i - 8 otherwise."""
+    import numpy as np
+
+    d = np.arange(2 * I)
+    t, r = d // 16, d % 16
+    return np.where(r < 8, 8 * t + r, I + 8 * t + r - 8).astype(np.int32)
 
 
 def random_q4(N: int, K: int, gen: torch.Generator, std: float = 0.02) -> torch.Tensor:
@@ -145,13 +156,13 @@ class DecoderModel:
         n_attn = n_conv = 0
         kb = keep_blocks
 
-        def lin(N, K, rows=None, cols=None):
+        def lin(N, K, rows=None, cols=None, perm=None):
             blocks = random_q4(N, K, g)
             if rows is not None:
                 blocks, N = TP.q4_rows(blocks, N, K, rows), rows.numel()
             if cols is not None:
                 blocks, K = TP.q4_cols(blocks, N, K, *cols), cols[1] - cols[0]
-            return Linear(self.ctx, blocks, N, K, kb)
+            return Linear(self.ctx, blocks, N, K, kb, perm)
 
         for t in cfg.layer_types:
             L = {"type": t, "norm1": torch.ones(D, device="cuda"), "norm2": torch.ones(D, device="cuda")}
@@ -169,7 +180,9 @@ class DecoderModel:
                 L["out"] = lin(D, D)
                 L["slot"] = n_conv
                 n_conv += 1
-            L["gu"] = lin(2 * I, D, rows=TP.gate_up_rows(cfg, sh) if sh else None)
+            # gate|up packed interleaved by 8: SwiGLU runs in the matmul's epilogue
+            L["gu"] = lin(2 * I, D, rows=TP.gate_up_rows(cfg, sh) if sh else None,
+                          perm=swiglu_pairs_perm(sh.ffn if sh else I))
             L["down"] = lin(D, I, cols=TP.down_cols(cfg, sh) if sh else None)
             self.layers.append(L)
         B = batch
@@ -234,6 +247,20 @@ class DecoderModel:
                                w.data_ptr(), self.cfg.eps, resid_out.data_ptr() if resid_out is not None else None)
         self._c(_lib.lib().wg_q4_matmul_fused(P(self.ctx.handle), P(lin.m.handle), ctypes.byref(pro), rows,
                                               P(y.data_ptr()), WG_F32))
+
+    def _gate_up(self, lin: Linear, resid, add, w, resid_out, rows: int):
+        """self.act = silu(gate) * up of rmsnorm(resid + add) * w: the norm in
+        the matmul's prologue and SwiGLU in its epilogue (decode rows); more
+        rows go through the gate|up product and a separate SwiGLU pass."""
+        pro = _lib.wg_prologue(WG_PRO_RMSNORM, resid.data_ptr(), add.data_ptr() if add is not None else None,
+                               w.data_ptr(), self.cfg.eps, resid_out.data_ptr() if resid_out is not None else None)
+        L, c = _lib.lib(), P(self.ctx.handle)
+        if rows <= 32:
+            self._c(L.wg_q4_matmul_ex(c, P(lin.m.handle), ctypes.byref(pro), None, WG_F16, rows,
+                                      P(self.act.data_ptr()), WG_F16, _lib.WG_EPI_SWIGLU_PAIRS))
+            return
+        self._c(L.wg_q4_matmul_fused(c, P(lin.m.handle), ctypes.byref(pro), rows, P(self.gu.data_ptr()), WG_F32))
+        self._c(L.wg_swiglu_pairs(c, P(self.gu.data_ptr()), rows, self.I, P(self.act.data_ptr()), WG_F16))
 
     def _mm_swiglu(self, lin: Linear, gu, y: torch.Tensor, rows: int):
         pro = _lib.wg_prologue(WG_PRO_SWIGLU, gu.data_ptr(), None, None, 0.0, None)
@@ -333,10 +360,9 @@ class DecoderModel:
                 self._attend(lay, rows)
             else:
                 self._convolve(lay, rows)
-            self._mm_norm(lay["gu"], cur, self.o, lay["norm2"], other, self.gu, rows)
+            self._gate_up(lay["gu"], cur, self.o, lay["norm2"], other, rows)
             cur, other = other, cur
-            self._mm_rowpar(lay["down"], rows, pro=_lib.wg_prologue(WG_PRO_SWIGLU, self.gu.data_ptr(), None, None,
-                                                                    0.0, None))
+            self._mm_rowpar(lay["down"], rows, x=self.act)
             add = self.o
         self._head(cur, add, rows)
 
@@ -360,7 +386,7 @@ class DecoderModel:
             self._c(L.wg_rmsnorm(c, P(self.x.data_ptr()), P(self.o.data_ptr()), P(lay["norm2"].data_ptr()), cfg.eps,
                                  rows, D, P(self.h.data_ptr()), WG_F16))
             self._mm(lay["gu"], self.h, self.gu, rows)
-            self._c(L.wg_swiglu(c, P(self.gu.data_ptr()), rows, self.I, P(self.act.data_ptr()), WG_F16))
+            self._c(L.wg_swiglu_pairs(c, P(self.gu.data_ptr()), rows, self.I, P(self.act.data_ptr()), WG_F16))
             self._mm(lay["down"], self.act, self.o, rows)
             self._all_reduce(self.o[:rows])
             add = self.o.data_ptr()
