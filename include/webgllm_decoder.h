@@ -52,8 +52,8 @@ int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int batch, int H, int Hk
  * (scores / attend, src/gpu/kernels.ts:2386-2579): a query row at position p
  * of head h attends keys 0..p of its sequence's KV head h / (H / Hkv). q fp16 [rows][H][Dh]
  * (already scaled), out fp16 [rows][H][Dh]. Dh in {32, 64, 128, 256},
- * H / Hkv <= 16. Each (row, KV head) is served by a cluster of 8 CTAs that
- * split the keys and merge through distributed shared memory. */
+ * H / Hkv <= 16. Each (row, KV head) is served by a cluster of up to 8
+ * CTAs that split the keys and merge through distributed shared memory. */
 int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                  const void *v_cache, int cache_len, const int32_t *pos, void *out);
 

@@ -94,8 +94,8 @@ int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv
   if (int st = check_batch(ctx, "wg_attention", rows, batch)) return st;
   if (!q || !k_cache || !v_cache || !pos || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_attention: null");
   return finish(ctx,
-                wg::launch_attention(q, rows, batch, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->stream,
-                                     ctx->pdl),
+                wg::launch_attention(q, rows, batch, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->num_sms,
+                                     ctx->stream, ctx->pdl),
                 "wg_attention");
 }
 

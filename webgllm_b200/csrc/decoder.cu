@@ -127,9 +127,11 @@ __global__ void rope_kv_kernel(const float *qkv, int rps, int H, int Hkv, int Dh
 }
 
 // ---- causal GQA attention (scores / attend kernels.ts:2386-2579) -----------
-// Split-K ("flash decoding") over a thread-block cluster: the cluster of
-// kAttnCluster CTAs serves one (query row, KV head) pair and every query
-// head of its group; CTA c takes the c-th slice of the row's keys 0..pos.
+// Split-K ("flash decoding") over a thread-block cluster: a cluster of CL
+// CTAs (CL = 8 when few (row, KV head) pairs share the GPU, down to 1 for
+// large batches or prompts, so the grid stays about one wave) serves one
+// (query row, KV head) pair and every query head of its group; CTA c takes
+// the c-th slice of the row's keys 0..pos.
 // Per slice, tiles of 128 keys (64 for Dh = 256) of K and V are staged in shared memory with
 // cp.async (all copies in flight at once; K rows padded by 16 bytes so that
 // row-strided reads hit distinct banks). Scores: one thread per (head, key).
@@ -140,7 +142,7 @@ __global__ void rope_kv_kernel(const float *qkv, int rps, int H, int Hkv, int Dh
 // memory: CTA c finishes outputs c*128 + i (mod 8*128) of the group's
 // G * Dh. No global scratch: one launch per step and nothing to allocate.
 
-constexpr int kAttnCluster = 8;
+constexpr int kAttnCluster = 8;  // largest cluster
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxGroup = 16;
@@ -215,7 +217,7 @@ __device__ __forceinline__ void load_halves(const __half *p, float v[DPL]) {
 }
 
 template <int DPL>  // head dims per lane: Dh = 32 * DPL
-__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThreads)
+__global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const __half *q, int rps, int H, int Hkv, const __half *k_cache, const __half *v_cache,
                      int cache_len, const int *pos0, __half *out) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
@@ -240,11 +242,12 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
   float *sred = reinterpret_cast<float *>(smem + lay.red);
 
   const int c = (int)cluster.block_rank();
+  const int CL = (int)cluster.num_blocks();
   const int hk = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bseq = r / rps;  // sequence of this query row (rps rows per sequence)
   const int L = max(0, min(pos0[bseq] + (r - bseq * rps) + 1, cache_len));
-  const int per = (L + kAttnCluster - 1) / kAttnCluster;
+  const int per = (L + CL - 1) / CL;
   const int t0 = min(L, c * per), t1 = min(L, t0 + per);
 
   // queries of the group (already scaled by 1/sqrt(Dh))
@@ -352,13 +355,14 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
     }
   }
   cluster.sync();
-  // merge the slices: this CTA finishes outputs c * 128 + tid, + 8 * 128, ...
-  for (int i = c * kAttnThreads + tid; i < G * Dh; i += kAttnCluster * kAttnThreads) {
+  // merge the slices: this CTA finishes outputs c * 128 + tid, + CL * 128, ...
+  for (int i = c * kAttnThreads + tid; i < G * Dh; i += CL * kAttnThreads) {
     const int g = i / Dh;
     float mj[kAttnCluster];
     float M = -INFINITY;
 #pragma unroll
     for (int j = 0; j < kAttnCluster; j++) {
+      if (j >= CL) break;
       mj[j] = cluster.map_shared_rank(sm, j)[g];
       M = fmaxf(M, mj[j]);
     }
@@ -366,6 +370,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
     if (M != -INFINITY) {
 #pragma unroll
       for (int j = 0; j < kAttnCluster; j++) {
+        if (j >= CL) break;
         const float w = mj[j] == -INFINITY ? 0.0f : expf(mj[j] - M);
         lsum += cluster.map_shared_rank(sl, j)[g] * w;
         a += cluster.map_shared_rank(sacc, j)[i] * w;
@@ -882,8 +887,8 @@ cudaError_t launch_rope_kv(const float *qkv, int rows, int batch, int H, int Hkv
 
 template <int DPL>
 cudaError_t launch_attention_t(const void *q, int rows, int rps, int H, int Hkv, const void *k_cache,
-                               const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s,
-                               bool pdl) {
+                               const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
+                               cudaStream_t s, bool pdl) {
   const AttnSmem lay(32 * DPL, H / Hkv);
   const size_t smem = lay.total;
   auto kern = attention_kernel<DPL>;
@@ -891,21 +896,50 @@ cudaError_t launch_attention_t(const void *q, int rows, int rps, int H, int Hkv,
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  return launch_k(kern, dim3(kAttnCluster, Hkv, rows), dim3(kAttnThreads), smem, s, pdl,
-                  reinterpret_cast<const __half *>(q), rps, H, Hkv, reinterpret_cast<const __half *>(k_cache),
-                  reinterpret_cast<const __half *>(v_cache), cache_len, pos0, reinterpret_cast<__half *>(out));
+  // cluster size: split each pair's keys over up to 8 CTAs while the grid
+  // stays within about one wave (CTAs per SM by shared memory)
+  const int per_sm = smem <= 100 * 1024 ? 2 : 1;
+  const long long pairs = (long long)rows * Hkv;
+  int CL = kAttnCluster;
+  while (CL > 1 && pairs * CL > (long long)num_sms * per_sm) CL /= 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)CL, (unsigned)Hkv, (unsigned)rows);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  at[n].id = cudaLaunchAttributeClusterDimension;
+  at[n].val.clusterDim.x = (unsigned)CL;
+  at[n].val.clusterDim.y = 1;
+  at[n].val.clusterDim.z = 1;
+  n++;
+  if (pdl) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const __half *>(q), rps, H, Hkv,
+                            reinterpret_cast<const __half *>(k_cache), reinterpret_cast<const __half *>(v_cache),
+                            cache_len, pos0, reinterpret_cast<__half *>(out));
 }
 
 cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
-                             const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s,
-                             bool pdl) {
+                             const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
+                             cudaStream_t s, bool pdl) {
   if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
   const int rps = rows / batch;
   switch (Dh) {
-    case 32: return launch_attention_t<1>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
-    case 64: return launch_attention_t<2>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
-    case 128: return launch_attention_t<4>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
-    case 256: return launch_attention_t<8>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, s, pdl);
+    case 32:
+      return launch_attention_t<1>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
+    case 64:
+      return launch_attention_t<2>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
+    case 128:
+      return launch_attention_t<4>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
+    case 256:
+      return launch_attention_t<8>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
