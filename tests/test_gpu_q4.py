@@ -258,3 +258,38 @@ def test_gemm_repeated_calls_are_deterministic():
     b = wg.matmul(x, m, out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+def test_gemm_pair_kernel_parity():
+    """The 2-SM (cta_group::2) GEMM, opt-in through WG_GEMM_PAIR=1 (read once
+    per process, hence a child process): the same products as the fp32
+    product of the dequantised weights, rel 1e-3."""
+    import subprocess
+    import sys
+
+    code = r'''
+import sys, torch
+sys.path.insert(0, ".")
+import webgllm_b200 as wg
+from webgllm_b200.model import quantize_q4_0, dequantize_q4_0
+c = wg.context(); c.use_torch_stream()
+worst = 0.0
+for (M, N, K) in [(256, 256, 256), (300, 512, 1024), (1024, 4096, 4096), (77, 768, 2048)]:
+    g = torch.Generator(device="cuda"); g.manual_seed(M + N + K)
+    w = torch.randn((N, K), generator=g, device="cuda") * 0.02
+    bl = quantize_q4_0(w)
+    m = wg.newQuantMatrix(N, K); wg.packQ4_0(m, 0, bl, N)
+    x = torch.randn((M, K), generator=g, device="cuda").half()
+    y = wg.matmul(x, m, out_dtype=torch.float32)
+    c.sync()
+    ref = x.float() @ dequantize_q4_0(bl, N, K).t()
+    worst = max(worst, ((y - ref).norm() / ref.norm()).item())
+print(worst)
+'''
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, WG_GEMM_PAIR="1")
+    out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert float(out.stdout.strip().splitlines()[-1]) < 1e-3

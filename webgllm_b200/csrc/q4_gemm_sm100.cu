@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < kStages; i++) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
-      mbar_init(&afull[i], kDequantWarps * 32);
+      mbar_init(&afull[i], kDequantWarps);
     }
     mbar_init(accfull, 1);
     fence_mbar_init();
@@ -282,7 +282,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tmem_st_16x256b_x4(tmem_a + ((uint32_t)(32 * q + 16 * sub) << 16) + s * 32, v);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&afull[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[s]);
     }
 
     // Epilogue: this warp's 32 TMEM lanes (weight rows 32q..32q+31) and half
@@ -318,6 +319,321 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0 && aborted) {
     for (int it = nk > kStages ? nk - kStages : 0; it < nk; it++)
       mbar_wait_bounded(&full[it % kStages], (it / kStages) & 1, a.flags);
+  }
+}
+
+// ---- the 2-SM GEMM (cta_group::2) -----------------------------------------
+//
+// A cluster of two CTAs computes a 256-row (weights) x BM2-row (tokens) tile
+// with tcgen05.mma.cta_group::2 (MMA M = 256): each CTA dequantises its own
+// 128 weight rows into its own tensor memory (the A operand's two halves)
+// and loads half of the token tile (the B operand's two halves) into its own
+// shared memory; the leader CTA (rank 0) issues the MMAs, which read A and B
+// from both SMs and accumulate each CTA's 128 rows of D in that CTA's tensor
+// memory. Per SM, the activation tile in shared memory is half of the 1-SM
+// kernel's for the same tensor work — the operand whose TMA writes and MMA
+// reads bound that kernel.
+//
+// Rings: shared-memory stages (x half + code tiles), kStages2 deep, and a
+// TMEM A ring of kTmemStages2 stages, decoupled so that loads run further
+// ahead than the dequantised weights. Barriers: wfull (each CTA: its code
+// tiles), xfull (leader: both x halves, two arrive.expect_tx), afull
+// (leader: both CTAs' dequantisers), sempty / tempty / accfull (each CTA,
+// arrived by the leader's commits multicast to the pair). Loads that signal
+// the leader's barrier from the peer use the .cta_group::2 form (no
+// multicast). Every wait is bounded; TMEM (256 columns, one CTA per SM) is
+// freed on every path.
+
+constexpr int kStages2 = 8;
+constexpr int kTmemStages2 = 12;
+constexpr int kBM2 = 128;                        // tokens per CTA pair (MMA N)
+constexpr int kX2StageBytes = (kBM2 / 2) * 128;  // this CTA's half: 64 tokens x 64 K fp16
+constexpr int kTmemCols2 = 512;                  // D [0, 128), A ring [128, 512)
+constexpr int kMinSmem2 = 130 * 1024;            // one CTA per SM
+
+struct Gemm2Smem {
+  int x, nib, scl, zro, bar, tmem_slot, total;
+};
+
+__host__ __device__ inline Gemm2Smem gemm2_smem() {
+  Gemm2Smem s;
+  s.x = 0;
+  s.nib = s.x + kStages2 * kX2StageBytes;
+  s.scl = s.nib + kStages2 * kNibStageBytes;
+  s.zro = s.scl + kStages2 * kSclStageBytes;
+  s.bar = s.zro + kStages2 * kZroStageBytes;
+  // wfull[S], xfull[S], sempty[S], afull[T], tempty[T], pfull[T], accfull
+  s.tmem_slot = s.bar + (3 * kStages2 + 3 * kTmemStages2 + 1) * 8;
+  s.total = s.tmem_slot + 16;
+  return s;
+}
+
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// arrive on an mbarrier given by its shared::cluster address
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// Relaxed: no memory ordering of its own (the caller orders what it must).
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// Waits (bounded) with cluster-scope acquire: the phase may have been
+// completed by the peer CTA's arrivals.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *flags) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > 2000000000LL) {
+      raise_flag(flags, kFlagTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int c0, int c1,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc2(uint32_t *slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrives on `bar` (same shared-memory offset) in both CTAs of the pair once
+// the leader's MMAs issued so far are complete.
+__device__ __forceinline__ void tc_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((unsigned short)3)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <bool ZEROS>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_nib,
+                 const __grid_constant__ CUtensorMap tm_scl, const __grid_constant__ CUtensorMap tm_zro,
+                 const GemmArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const Gemm2Smem L = gemm2_smem();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t *wfull = reinterpret_cast<uint64_t *>(smem + L.bar);
+  uint64_t *xfull = wfull + kStages2;
+  uint64_t *sempty = xfull + kStages2;
+  uint64_t *afull = sempty + kStages2;
+  uint64_t *tempty = afull + kTmemStages2;
+  uint64_t *pfull = tempty + kTmemStages2;  // peer only: its dequantisers, before forwarding
+  uint64_t *accfull = pfull + kTmemStages2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
+  __shared__ int aborted;
+
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int pair = blockIdx.x >> 1;
+  const int nt0 = pair * 16 + (int)rank * 8;  // this CTA's eight 16-row tiles
+  const int m0 = blockIdx.y * kBM2;            // the pair's tokens; this CTA loads half
+  const int kpc = a.kt_per_split;
+  const int kt_begin = blockIdx.z * kpc;
+  const int kt_end = min(a.KT, kt_begin + kpc);
+  const int nk = kt_end - kt_begin;
+
+  if (threadIdx.x == 0) {
+    aborted = 0;
+    for (int i = 0; i < kStages2; i++) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&xfull[i], 1);   // the leader expects both CTAs' x halves
+      mbar_init(&sempty[i], 1);
+    }
+    for (int i = 0; i < kTmemStages2; i++) {
+      mbar_init(&afull[i], kDequantWarps + 1);  // the leader's dequant warps + the peer's forward
+      mbar_init(&tempty[i], 1);
+      mbar_init(&pfull[i], kDequantWarps);
+    }
+    mbar_init(accfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc2(tmem_slot, kTmemCols2);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_d = tmem;
+  const uint32_t tmem_a = tmem + 128;
+
+  auto wait = [&](uint64_t *bar, uint32_t parity) {
+    if (aborted) return;
+    if (!mbar_wait_cluster(bar, parity, a.flags)) aborted = 1;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t wbytes = kNibStageBytes + kSclStageBytes + (ZEROS ? kZroStageBytes : 0);
+      const uint32_t xfull_leader = map_rank(smem_u32(xfull), 0);
+      for (int it = 0; it < nk; it++) {
+        const int s = it % kStages2;
+        const uint32_t ph = (it / kStages2) & 1;
+        wait(&sempty[s], ph ^ 1);
+        const int kt = kt_begin + it;
+        mbar_expect_tx(&wfull[s], wbytes);
+        tma_load_3d(smem + L.nib + s * kNibStageBytes, &tm_nib, 0, kt, nt0, &wfull[s]);
+        tma_load_3d(smem + L.scl + s * kSclStageBytes, &tm_scl, 0, kt, nt0, &wfull[s]);
+        if (ZEROS) tma_load_3d(smem + L.zro + s * kZroStageBytes, &tm_zro, 0, kt, nt0, &wfull[s]);
+        const uint32_t xbar = xfull_leader + (uint32_t)(s * 8);
+        // the leader expects both halves (the peer's load may complete first:
+        // the transaction count dips below zero, the phase cannot complete
+        // before the leader's arrive)
+        if (rank == 0) mbar_expect_tx(&xfull[s], 2 * kX2StageBytes);
+        tma_load_2d_pair(smem + L.x + s * kX2StageBytes, &tm_x, kt * kTileK, m0 + (int)rank * (kBM2 / 2), xbar);
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(kBM2 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+      for (int it = 0; it < nk; it++) {
+        const int s = it % kStages2, t = it % kTmemStages2;
+        wait(&xfull[s], (it / kStages2) & 1);
+        wait(&afull[t], (it / kTmemStages2) & 1);
+        tc_fence_after();
+        const uint64_t bdesc = sw128_desc(smem_u32(smem + L.x + s * kX2StageBytes));
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          mma_f16_pair(tmem_d, tmem_a + t * 32 + kk * 8, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit_pair(&sempty[s]);
+        tc_commit_pair(&tempty[t]);
+      }
+      tc_commit_pair(accfull);
+    } else if (rank == 1 && lane == 0) {
+      // Forward each A stage of this CTA to the leader: one cluster-scope
+      // release per stage, off the dequantisers' path.
+      const uint32_t afull_leader = map_rank(smem_u32(afull), 0);
+      for (int it = 0; it < nk; it++) {
+        const int t = it % kTmemStages2;
+        wait(&pfull[t], (it / kTmemStages2) & 1);
+        if (a.fwd_relaxed)
+          mbar_arrive_remote_relaxed(afull_leader + (uint32_t)(t * 8));
+        else
+          mbar_arrive_remote(afull_leader + (uint32_t)(t * 8));
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int sub = (warp - 2) >> 2;
+    const int tile = 2 * q + sub;
+    const int g = lane >> 2;
+    for (int it = 0; it < nk; it++) {
+      const int s = it % kStages2, t = it % kTmemStages2;
+      wait(&wfull[s], (it / kStages2) & 1);
+      wait(&tempty[t], ((it / kTmemStages2) & 1) ^ 1);  // the MMA that last read A stage t is done
+      tc_fence_after();
+      const uint4 wv = *reinterpret_cast<const uint4 *>(smem + L.nib + s * kNibStageBytes + tile * kTileNibBytes +
+                                                        lane * 16);
+      const uint2 sv =
+          *reinterpret_cast<const uint2 *>(smem + L.scl + s * kSclStageBytes + tile * kTileSclBytes + g * 8);
+      uint32_t zv = 0x08080808u;
+      if (ZEROS)
+        zv = *reinterpret_cast<const uint32_t *>(smem + L.zro + s * kZroStageBytes + tile * kTileZroBytes + g * 4);
+      const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t v[16];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int bsel = j >> 1;
+        const uint32_t zz = zv >> (16 * bsel);
+        const uint32_t z_g = zz & 15u, z_g8 = (zz >> 8) & 15u;
+        uint32_t P[4];
+        unpack_codes(w[j], zp_lo(z_g), zp_hi(z_g), zp_lo(z_g8), zp_hi(z_g8), P);
+        const uint32_t sp = bsel ? sv.y : sv.x;
+        const uint32_t d_g = (sp & 0xFFFFu) * 0x00010001u;
+        const uint32_t d_g8 = (sp >> 16) * 0x00010001u;
+        v[4 * j + 0] = hmul2_u(P[0], d_g);
+        v[4 * j + 1] = hmul2_u(P[1], d_g);
+        v[4 * j + 2] = hmul2_u(P[2], d_g8);
+        v[4 * j + 3] = hmul2_u(P[3], d_g8);
+      }
+      tmem_st_16x256b_x4(tmem_a + ((uint32_t)(32 * q + 16 * sub) << 16) + t * 32, v);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rank == 0 ? &afull[t] : &pfull[t]);
+    }
+
+    // Epilogue: this CTA's 128 rows of D (its weight rows) x the pair's tokens.
+    // (Waited for even after a timeout: TMEM must not be freed under MMAs.)
+    mbar_wait_cluster(accfull, 0, a.flags);
+    tc_fence_after();
+    const int n = nt0 * kTileRows + 32 * q + lane;
+    const int c_begin = sub * (kBM2 / 2), c_end = c_begin + kBM2 / 2;
+    for (int c = c_begin; c < c_end; c += 16) {
+      float v[16];
+      tmem_ld_32x32b_x16(tmem_d + ((uint32_t)(32 * q) << 16) + c, v);
+      if (n < a.N) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int tok = m0 + c + i;
+          if (tok < a.M) {
+            if (a.ws) a.ws[((size_t)blockIdx.z * a.M + tok) * a.N + n] = v[i];
+            else store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, v[i]);
+          }
+        }
+      }
+    }
+  }
+
+  // No TMA may still be writing when the pair exits (only possible after a
+  // timed-out wait): each CTA waits for its own code tiles, the leader for
+  // both x halves (they complete on its barrier).
+  if (threadIdx.x == 0 && aborted) {
+    for (int it = nk > kStages2 ? nk - kStages2 : 0; it < nk; it++) {
+      mbar_wait_cluster(&wfull[it % kStages2], (it / kStages2) & 1, a.flags);
+      if (rank == 0) mbar_wait_cluster(&xfull[it % kStages2], (it / kStages2) & 1, a.flags);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs (which use both SMs) are done; neither CTA exits early
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem, kTmemCols2);
   }
 }
 
@@ -392,9 +708,54 @@ cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+template <bool ZEROS>
+cudaError_t launch_pair(const GemmArgs &a, const void *x, cudaStream_t stream) {
+  const Gemm2Smem L = gemm2_smem();
+  auto kern = gemm2_kernel<ZEROS>;
+  const int smem_bytes = L.total + 1024 > kMinSmem2 ? L.total + 1024 : kMinSmem2;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  CUtensorMap tx, tn, ts, tz;
+  if (!encode_x(&tx, x, a.M, a.K, kBM2 / 2) || !encode_plane(&tn, a.nib, kTileNibBytes / 4, a.KT, a.NT) ||
+      !encode_plane(&ts, a.scl, kTileSclBytes / 4, a.KT, a.NT))
+    return cudaErrorInvalidValue;
+  tz = ts;
+  if (ZEROS && !encode_plane(&tz, a.zro, kTileZroBytes / 4, a.KT, a.NT)) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * ((a.NT + 15) / 16)), (unsigned)((a.M + kBM2 - 1) / kBM2), (unsigned)a.splits);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = (size_t)smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tx, tn, ts, tz, a);
+}
+
 }  // namespace
 
 bool gemm_supported() { return encode_fn() != nullptr; }
+
+// The 2-SM kernel runs only when asked (WG_GEMM_PAIR=1, N % 256 == 0): on
+// B200 it measured 300 TFLOP/s (490 with relaxed forwarding) against the
+// 1-SM kernel's 900-1000 at M = 4096 — the per-stage hand-offs between the
+// two SMs (a cluster-scope release per 64-K stage) serialise the pipeline.
+static bool gemm_use_pair(const GemmArgs &a) {
+  static int forced = -2;
+  if (forced == -2) {
+    const char *e = getenv("WG_GEMM_PAIR");
+    forced = e ? atoi(e) : 0;
+  }
+  return forced == 1 && a.N % 256 == 0 && a.M >= 2;
+}
 
 // Token rows per CTA; WG_GEMM_BM (64 / 128 / 256) overrides (tuning).
 static int gemm_tile_m(int M) {
@@ -409,8 +770,11 @@ static int gemm_tile_m(int M) {
 }
 
 size_t plan_gemm(GemmArgs &a, int num_sms) {
-  const int BM = gemm_tile_m(a.M);
-  const int tiles = ((a.NT + 7) / 8) * ((a.M + BM - 1) / BM);
+  const bool pair = gemm_use_pair(a);
+  const int BM = pair ? kBM2 : gemm_tile_m(a.M);
+  // CTAs of one K range (the pair kernel runs one per SM, the 1-SM kernel two)
+  const int tiles = pair ? 2 * ((a.NT + 15) / 16) * ((a.M + BM - 1) / BM)
+                         : ((a.NT + 7) / 8) * ((a.M + BM - 1) / BM);
   // Split K until the grid covers the SMs, keeping >= 4 stages per split.
   int splits = 1;
   while (tiles * splits < num_sms && a.KT / (splits + 1) >= 4) splits++;
@@ -422,6 +786,12 @@ size_t plan_gemm(GemmArgs &a, int num_sms) {
 cudaError_t launch_gemm(const GemmArgs &args, const void *x_f16, cudaStream_t stream) {
   if (!encode_fn()) return cudaErrorNotSupported;
   GemmArgs a = args;
+  static int relaxed = -1;
+  if (relaxed < 0) {
+    const char *e = getenv("WG_GEMM_FWD_RELAXED");
+    relaxed = e && e[0] == '1' ? 1 : 0;
+  }
+  a.fwd_relaxed = relaxed;
   const int BM = gemm_tile_m(a.M);
   cudaError_t e;
   if (a.splits > 1) {
@@ -430,7 +800,8 @@ cudaError_t launch_gemm(const GemmArgs &args, const void *x_f16, cudaStream_t st
     a.ws = nullptr;
   }
   const bool z = a.zro != nullptr;
-  if (BM == 64) e = z ? launch_bm<64, true>(a, x_f16, stream) : launch_bm<64, false>(a, x_f16, stream);
+  if (gemm_use_pair(a)) e = z ? launch_pair<true>(a, x_f16, stream) : launch_pair<false>(a, x_f16, stream);
+  else if (BM == 64) e = z ? launch_bm<64, true>(a, x_f16, stream) : launch_bm<64, false>(a, x_f16, stream);
   else if (BM == 128) e = z ? launch_bm<128, true>(a, x_f16, stream) : launch_bm<128, false>(a, x_f16, stream);
   else e = z ? launch_bm<256, true>(a, x_f16, stream) : launch_bm<256, false>(a, x_f16, stream);
   if (e != cudaSuccess || a.splits == 1) return e;

@@ -95,6 +95,7 @@ struct GemmArgs {
   int y_dtype;
   int splits, kt_per_split;
   unsigned *flags;
+  int fwd_relaxed;  // pair kernel: forward A stages with relaxed arrives (measurement knob)
 };
 
 bool gemm_supported();
