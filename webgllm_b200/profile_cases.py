@@ -1,0 +1,159 @@
+"""Small, self-contained runs of single kernels for profiling (ncu) and
+timing: `python -m webgllm_b200.profile_cases <case> [reps]`.
+
+Each case builds its inputs, runs the kernel `reps` times (default 5) on
+torch's current stream and prints the mean device time per launch (CUDA
+events), so that the same command serves a plain timing run and an ncu
+capture (`-k regex:<kernel> -s <warm-up launches> -c <n>`). Inputs are
+larger than L2 where the kernel streams weights.
+"""
+from __future__ import annotations
+
+import ctypes
+import sys
+
+import torch
+
+from . import _lib
+from .model import CONFIGS, DecoderModel, quantize_q4_0
+from .q4 import context, newQuantMatrix, packQ4_0
+
+P = ctypes.c_void_p
+
+
+def _q4(N: int, K: int, seed: int = 0):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    m = newQuantMatrix(N, K)
+    packQ4_0(m, 0, quantize_q4_0(torch.randn((N, K), generator=g, device="cuda") * 0.02), N)
+    return m
+
+
+def _time(fn, reps: int) -> float:
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+def gemv(M: int, N: int, K: int, reps: int):
+    """The decode GEMV (tile-column or wide, by the library's choice) over
+    `copies` distinct matrices (rotating, > L2)."""
+    c = context()
+    copies = max(2, (256 << 20) // (N * K * 18 // 32) + 1)
+    mats = [_q4(N, K, i) for i in range(copies)]
+    x = torch.randn((M, K), device="cuda").half()
+    y = torch.empty((M, N), device="cuda")
+    L = _lib.lib()
+    c.use_torch_stream()
+    i = [0]
+
+    def run():
+        m = mats[i[0] % copies]
+        i[0] += 1
+        _lib.check(L.wg_q4_matmul(P(c.handle), P(m.handle), P(x.data_ptr()), _lib.WG_F16, M, P(y.data_ptr()),
+                                  _lib.WG_F32), c.handle)
+
+    run()
+    us = _time(run, reps)
+    print(f"gemv M={M} N={N} K={K}: {us:.2f} us/launch, {N * K * 18 / 32 / us / 1e3:.1f} GB/s (weights)")
+
+
+def gemm(M: int, N: int, K: int, reps: int):
+    c = context()
+    m = _q4(N, K)
+    x = torch.randn((M, K), device="cuda").half()
+    y = torch.empty((M, N), device="cuda", dtype=torch.float16)
+    L = _lib.lib()
+    c.use_torch_stream()
+
+    def run():
+        _lib.check(L.wg_q4_matmul(P(c.handle), P(m.handle), P(x.data_ptr()), _lib.WG_F16, M, P(y.data_ptr()),
+                                  _lib.WG_F16), c.handle)
+
+    run()
+    us = _time(run, reps)
+    print(f"gemm M={M} N={N} K={K}: {us:.2f} us/launch, {2 * M * N * K / us / 1e6:.1f} TFLOP/s")
+
+
+def attention(batch: int, H: int, Hkv: int, Dh: int, ctx_len: int, reps: int):
+    c = context()
+    cache = 2048
+    kc = torch.randn((batch, Hkv, cache, Dh), device="cuda").half()
+    vc = torch.randn_like(kc)
+    q = (torch.randn((batch, H, Dh), device="cuda") / Dh ** 0.5).half()
+    o = torch.empty_like(q)
+    pos = torch.full((batch,), ctx_len - 1, dtype=torch.int32, device="cuda")
+    L = _lib.lib()
+    c.use_torch_stream()
+
+    def run():
+        _lib.check(L.wg_attention(P(c.handle), P(q.data_ptr()), batch, batch, H, Hkv, Dh, P(kc.data_ptr()),
+                                  P(vc.data_ptr()), cache, P(pos.data_ptr()), P(o.data_ptr())), c.handle)
+
+    run()
+    us = _time(run, reps)
+    kv = batch * Hkv * ctx_len * Dh * 2 * 2
+    print(f"attention batch={batch} H={H} Hkv={Hkv} Dh={Dh} ctx={ctx_len}: {us:.2f} us, {kv / us / 1e3:.1f} GB/s KV")
+
+
+def head(rows: int, D: int, V: int, reps: int):
+    c = context()
+    W = (torch.randn((V, D), device="cuda") * 0.02).half()
+    x = torch.randn((rows, D), device="cuda")
+    w = torch.ones(D, device="cuda")
+    logits = torch.empty((rows, V), device="cuda")
+    ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+    L = _lib.lib()
+    c.use_torch_stream()
+
+    def run():
+        _lib.check(L.wg_head_rmsnorm(P(c.handle), P(x.data_ptr()), None, P(w.data_ptr()), ctypes.c_float(1e-5), rows,
+                                     1, D, P(W.data_ptr()), V, 0, P(logits.data_ptr()), P(ids.data_ptr()), None),
+                   c.handle)
+
+    run()
+    us = _time(run, reps)
+    print(f"head rows={rows} D={D} V={V}: {us:.2f} us, {V * D * 2 / us / 1e3:.1f} GB/s")
+
+
+def decode(config: str, batch: int, reps: int):
+    """Eager decode steps (every launch visible to a profiler)."""
+    cfg = CONFIGS[config]
+    m = DecoderModel(cfg, seed=0, max_ctx=1024, max_rows=batch * 512, batch=batch)
+    m.prefill(torch.randint(0, cfg.vocab, (batch, 512), device="cuda", dtype=torch.int32))
+    m.decode_step()
+    us = _time(m.decode_step, reps)
+    print(f"decode config {config} batch {batch}: {us:.1f} us/step (eager)")
+
+
+CASES = {
+    "gemv_config1_m1": lambda r: gemv(1, 4096, 4096, r),
+    "gemv_wide_m8": lambda r: gemv(8, 28672, 4096, r),
+    "gemm_m1024": lambda r: gemm(1024, 4096, 4096, r),
+    "gemm_m4096_down": lambda r: gemm(4096, 4096, 14336, r),
+    "attention_config4_b8": lambda r: attention(8, 32, 8, 128, 640, r),
+    "attention_config2": lambda r: attention(1, 32, 4, 64, 256, r),
+    "head_config2": lambda r: head(1, 2048, 32000, r),
+    "head_config4_b8": lambda r: head(8, 4096, 128256, r),
+    "decode_config4_b8": lambda r: decode("4", 8, r),
+    "decode_config2": lambda r: decode("2", 1, r),
+}
+
+
+def main(argv=None):
+    argv = sys.argv[1:] if argv is None else argv
+    if not argv or argv[0] not in CASES:
+        print("cases:", " ".join(CASES))
+        return 2
+    reps = int(argv[1]) if len(argv) > 1 else 5
+    CASES[argv[0]](reps)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
