@@ -60,6 +60,14 @@ int wg_q4_matmul_push(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, co
  * (waits for every rank's push). */
 int wg_comm_reduce(wg_ctx *ctx, wg_comm *comm, int M, int N, float *out);
 
+/* The exchange fused with what consumes it in a decoder layer: v = resid +
+ * (the sum over ranks of the next exchange's partials, M x K), resid_out =
+ * v (if not NULL; must not alias resid), x_out fp16 = rmsnorm(v) * weight —
+ * the all-reduce, the residual add and the next RMS norm in one launch
+ * (addNormed, src/engine.ts:5695), one thread-block cluster per row. */
+int wg_comm_reduce_norm(wg_ctx *ctx, wg_comm *comm, int M, int K, const float *resid, const float *weight, float eps,
+                        float *resid_out, void *x_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -105,8 +105,29 @@ def _push_worker(rank, world, port, q):
             comm.reduce(out, M, N)
             ctx.sync()  # a missing push would surface here as WG_TIMEOUT
             errs.append(((out - ref).abs().max() / ref.abs().max()).item())
+        # the exchange fused with the residual add and the next RMS norm
+        M, N, K = 8, 4096, 512
+        m = wg.newQuantMatrix(N, K)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(7 + rank)
+        wg.packQ4_0(m, 0, quantize_q4_0(torch.randn((N, K), generator=g, device="cuda") * 0.02), N)
+        x = torch.randn((M, K), generator=g, device="cuda").half()
+        resid = torch.randn((M, N), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+        w = torch.rand(N, device="cuda", generator=torch.Generator(device="cuda").manual_seed(2)) + 0.5
+        part = wg.matmul(x, m, out_dtype=torch.float32)
+        dist.all_reduce(part)
+        v = resid + part
+        want = (v * torch.rsqrt((v * v).mean(-1, keepdim=True) + 1e-5) * w).half()
+        new_resid = torch.empty_like(resid)
+        xh = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        ctx.use_torch_stream()
+        comm.push(m, M, x=x)
+        comm.reduce_norm(resid, w, 1e-5, new_resid, xh, M, N)
+        ctx.sync()
+        errs.append(((new_resid - v).abs().max() / v.abs().max()).item())
+        xerr = ((xh.float() - want.float()).abs().max() / want.float().abs().max()).item()  # fp16 rounding
         comm.close()
-        q.put((rank, max(errs)))
+        q.put((rank, max(errs), xerr))
     finally:
         dist.destroy_process_group()
 
@@ -127,8 +148,9 @@ def _spawn(target, extra=()):
 def test_push_all_reduce_matches_nccl():
     q = _spawn(_push_worker)
     for _ in range(2):
-        rank, err = q.get(timeout=10)
+        rank, err, xerr = q.get(timeout=10)
         assert err < 1e-6, (rank, err)
+        assert xerr < 2e-3, (rank, xerr)
 
 
 @pytest.mark.parametrize("push", [True, False])

@@ -86,6 +86,7 @@ SIGNATURES = {
     "wg_comm_slot": (_I, [_P, ctypes.POINTER(_SZ)]),
     "wg_q4_matmul_push": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "wg_comm_reduce": (_I, [_P, _P, _I, _I, _P]),
+    "wg_comm_reduce_norm": (_I, [_P, _P, _I, _I, _P, _P, ctypes.c_float, _P, _P]),
     "wg_error_string": (ctypes.c_char_p, [_I]),
     "wg_last_error": (ctypes.c_char_p, [_P]),
 }

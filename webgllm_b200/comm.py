@@ -63,6 +63,14 @@ class PushComm:
     def reduce(self, out, rows: int, n: int):
         check(_lib.lib().wg_comm_reduce(P(self.ctx.handle), self.handle, rows, n, P(out.data_ptr())), self.ctx.handle)
 
+    def reduce_norm(self, resid, weight, eps: float, resid_out, x_out, rows: int, k: int):
+        """x_out (fp16) = rmsnorm(resid + the exchanged sum) * weight, and
+        resid_out = resid + the sum: the all-reduce, residual add and norm in
+        one launch."""
+        check(_lib.lib().wg_comm_reduce_norm(P(self.ctx.handle), self.handle, rows, k, P(resid.data_ptr()),
+                                             P(weight.data_ptr()), ctypes.c_float(eps), P(resid_out.data_ptr()),
+                                             P(x_out.data_ptr())), self.ctx.handle)
+
     def close(self):
         import torch.distributed as dist
 

@@ -491,7 +491,7 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     if (st) return st;
     const void *xh = x;
     if (pro) {
-      WG_CUDA(ctx, wg::launch_prologue(*pro, M, (int)K, ctx->work, ctx->stream));
+      WG_CUDA(ctx, wg::launch_prologue(*pro, M, (int)K, ctx->work, ctx->stream, ctx->pdl));
       xh = ctx->work;
     } else if (x_dtype != WG_F16) {
       WG_CUDA(ctx, wg::launch_to_f16(x, x_dtype, ctx->work, (size_t)M * K, ctx->stream));
@@ -509,7 +509,7 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
   if (pro && (M > wg::kProMaxTokens || heavy_norm)) {
     st = ensure_work(ctx, (size_t)M * K * 2);
     if (st) return st;
-    WG_CUDA(ctx, wg::launch_prologue(*pro, M, (int)K, ctx->work, ctx->stream));
+    WG_CUDA(ctx, wg::launch_prologue(*pro, M, (int)K, ctx->work, ctx->stream, ctx->pdl));
     x = ctx->work;
     x_dtype = WG_F16;
     pro = nullptr;

@@ -147,4 +147,18 @@ int wg_comm_reduce(wg_ctx *ctx, wg_comm *comm, int M, int N, float *out) {
   return e == cudaSuccess ? WG_OK : cuda_fail(ctx, e, "wg_comm_reduce");
 }
 
+int wg_comm_reduce_norm(wg_ctx *ctx, wg_comm *comm, int M, int K, const float *resid, const float *weight, float eps,
+                        float *resid_out, void *x_out) {
+  if (int st = begin(ctx)) return st;
+  if (!comm || !resid || !weight || !x_out) return cfail(ctx, WG_INVALID_ARGUMENT, "wg_comm_reduce_norm: null argument");
+  if (comm->device != ctx->device) return cfail(ctx, WG_INVALID_ARGUMENT, "exchange and context devices differ");
+  if (M <= 0 || K <= 0 || K % 8 || (size_t)M * K > (size_t)comm->dev.slot)
+    return cfail(ctx, WG_INVALID_SHAPE, "wg_comm_reduce_norm: %d x %d (K %% 8 == 0, slot %lld floats)", M, K,
+                 (long long)comm->dev.slot);
+  if (resid_out == resid) return cfail(ctx, WG_INVALID_ARGUMENT, "resid_out must not alias resid");
+  cudaError_t e = wg::launch_addnorm(resid, nullptr, weight, eps, resid_out, x_out, M, K, &comm->dev, ctx->d_flags,
+                                     ctx->stream, ctx->pdl);
+  return e == cudaSuccess ? WG_OK : cuda_fail(ctx, e, "wg_comm_reduce_norm");
+}
+
 }  // extern "C"

@@ -90,5 +90,9 @@ __device__ __forceinline__ void push_signal(const CommDev &c) {
 
 cudaError_t launch_comm_reduce(const CommDev &c, int M, int N, float *out, unsigned *flags, cudaStream_t s,
                                bool pdl);
+// x fp16 [M][K] = rmsnorm(a + b) * w (and resid_out = a + b if not null);
+// with comm, b is the sum of the next exchange's partials (b unused).
+cudaError_t launch_addnorm(const float *a, const float *b, const float *w, float eps, float *resid_out, void *x,
+                           int M, int K, const CommDev *comm, unsigned *flags, cudaStream_t s, bool pdl);
 
 }  // namespace wg

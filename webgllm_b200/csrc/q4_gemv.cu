@@ -793,8 +793,10 @@ cudaError_t launch_wide_t(const GemvArgs &a, cudaStream_t stream, bool pdl) {
 
 }  // namespace
 
-cudaError_t launch_prologue(const Prologue &p, int M, int K, void *x_f16, cudaStream_t stream) {
+cudaError_t launch_prologue(const Prologue &p, int M, int K, void *x_f16, cudaStream_t stream, bool pdl) {
   if (K % 8 || (p.kind != kProRmsNorm && p.kind != kProSwiglu)) return cudaErrorInvalidValue;
+  // the norm: a cluster of CTAs per row (comm.cu)
+  if (p.kind == kProRmsNorm) return launch_addnorm(p.a, p.b, p.w, p.eps, p.out, x_f16, M, K, nullptr, nullptr, stream, pdl);
   prologue_kernel<<<M, kThreads, 0, stream>>>(p, K, reinterpret_cast<__half *>(x_f16));
   return cudaGetLastError();
 }

@@ -47,7 +47,7 @@ struct Prologue {
 // Rows of one fused GEMV launch (the prologue needs the whole row per CTA).
 constexpr int kProMaxTokens = 8;
 // The prologue alone: x fp16 [M][K] (for matmuls that do not fuse it).
-cudaError_t launch_prologue(const Prologue &p, int M, int K, void *x_f16, cudaStream_t stream);
+cudaError_t launch_prologue(const Prologue &p, int M, int K, void *x_f16, cudaStream_t stream, bool pdl);
 
 struct GemvArgs {
   const uint32_t *nib;

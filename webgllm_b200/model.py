@@ -279,6 +279,11 @@ class DecoderModel:
         return self._forward_passes(ids, rows)
 
     def _attend(self, lay, rows):
+        self._rope_attend(lay, rows)
+        self._mm_rowpar(lay["o"], rows, x=self.att)
+
+    def _rope_attend(self, lay, rows):
+        """RoPE + KV append + attention into self.att."""
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
         H, Hkv, Dh = self.H, self.Hkv, cfg.head_dim
         s = lay["slot"]
@@ -290,7 +295,6 @@ class DecoderModel:
                              P(kc.data_ptr()), P(vc.data_ptr()), self.max_ctx))
         self._c(L.wg_attention(c, P(self.q.data_ptr()), rows, self.batch, H, Hkv, Dh, P(kc.data_ptr()),
                                P(vc.data_ptr()), self.max_ctx, P(self.pos.data_ptr()), P(self.att.data_ptr())))
-        self._mm_rowpar(lay["o"], rows, x=self.att)
 
     def _mm_rowpar(self, lin: Linear, rows: int, x=None, pro=None):
         """self.o[:rows] = the sum over ranks of this rank's partial x . W^T
@@ -340,30 +344,54 @@ class DecoderModel:
 
     def _forward_fused(self, ids: torch.Tensor, rows: int):
         """Each norm runs inside the matmul that consumes it, SwiGLU inside the
-        down projection and the final norm inside the head: per layer the
-        residual stream alternates between self.x and self.x2."""
+        gate|up projection's epilogue and the final norm inside the head: per
+        layer the residual stream alternates between self.x and self.x2. Under
+        tensor parallelism with the push exchange (decode rows), each
+        row-parallel sum arrives together with the residual add and the next
+        norm (wg_comm_reduce_norm), and the next matmul takes its fp16 x."""
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
         D = cfg.hidden
         self.ctx.use_torch_stream()
         self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), cfg.vocab, D, P(self.x.data_ptr())))
         cur, other = self.x, self.x2
+        fused_ex = self.comm is not None and rows <= 8 and rows * D <= self.comm.slot
         add = None
-        for lay in self.layers:
+        normed = False  # self.h already holds the fp16 input of the next q|k|v (or in) projection
+        n = len(self.layers)
+        for li, lay in enumerate(self.layers):
             proj = self.qkv if lay["type"] == "attn" else self.bcx
             lin = lay["qkv"] if lay["type"] == "attn" else lay["in"]
-            if add is None:
+            if normed:
+                self._mm(lin, self.h, proj, rows)
+            elif add is None:
                 self._mm_norm(lin, cur, None, lay["norm1"], None, proj, rows)
             else:
                 self._mm_norm(lin, cur, add, lay["norm1"], other, proj, rows)
                 cur, other = other, cur
             if lay["type"] == "attn":
-                self._attend(lay, rows)
+                self._rope_attend(lay, rows)
+                if fused_ex:
+                    self.comm.push(lay["o"].m, rows, x=self.att)
+                    self.comm.reduce_norm(cur, lay["norm2"], cfg.eps, other, self.h, rows, D)
+                    cur, other = other, cur
+                    self._c(L.wg_q4_matmul_ex(c, P(lay["gu"].m.handle), None, P(self.h.data_ptr()), WG_F16, rows,
+                                              P(self.act.data_ptr()), WG_F16, _lib.WG_EPI_SWIGLU_PAIRS))
+                else:
+                    self._mm_rowpar(lay["o"], rows, x=self.att)
+                    self._gate_up(lay["gu"], cur, self.o, lay["norm2"], other, rows)
+                    cur, other = other, cur
             else:
                 self._convolve(lay, rows)
-            self._gate_up(lay["gu"], cur, self.o, lay["norm2"], other, rows)
-            cur, other = other, cur
-            self._mm_rowpar(lay["down"], rows, x=self.act)
-            add = self.o
+                self._gate_up(lay["gu"], cur, self.o, lay["norm2"], other, rows)
+                cur, other = other, cur
+            if fused_ex and li + 1 < n:
+                self.comm.push(lay["down"].m, rows, x=self.act)
+                self.comm.reduce_norm(cur, self.layers[li + 1]["norm1"], cfg.eps, other, self.h, rows, D)
+                cur, other = other, cur
+                normed, add = True, None
+            else:
+                self._mm_rowpar(lay["down"], rows, x=self.act)
+                normed, add = False, self.o
         self._head(cur, add, rows)
 
     def _forward_passes(self, ids: torch.Tensor, rows: int):
