@@ -103,6 +103,22 @@ int wg_pick_keys(wg_ctx *ctx, const int64_t *keys, int rows, int32_t *ids);
  * logit of row r (the lowest index on ties). */
 int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out);
 
+/* Greedy speculative decoding: acceptance of a draft's k proposals per
+ * sequence (forwardDraft / accept, src/engine.ts:8035,8063: keys and values
+ * past the kept rows are never read before they are written again, so the
+ * rollback is the position alone; conv-state prefixes are not kept here, so
+ * this serves attention-only models). drafts [batch][k] = the draft's tokens d_1..d_k;
+ * picks [k+1][batch] = the target's greedy picks after each verified row
+ * (rows: the last kept token, then d_1..d_k). Keeps the longest prefix with
+ * d_{j+1} == picks[j], appends it and the target's pick after it to
+ * out [batch][out_cap] at out_len[b] (which advances), adds the number of
+ * accepted draft tokens to accepted[b], sets both next tokens to that pick and
+ * both positions to just past the kept rows (pos_target had advanced by k + 1
+ * in the verify forward). */
+int wg_spec_accept(wg_ctx *ctx, const int32_t *drafts, const int32_t *picks, int batch, int k, int32_t *pos_target,
+                   int32_t *pos_draft, int32_t *next_target, int32_t *next_draft, int32_t *out, int out_cap,
+                   int32_t *out_len, int32_t *accepted);
+
 /* counters[0..n) += delta on the device (advances the positions of a
  * replayed decode step). */
 int wg_add_i32(wg_ctx *ctx, int32_t *counters, int n, int delta);

@@ -537,3 +537,36 @@ def test_matmul_swiglu_pairs_epilogue(rows, I, K):
     act2 = torch.empty((rows, I), dtype=torch.float16, device="cuda")
     call(lib().wg_swiglu_pairs, ptr(gu), rows, I, ptr(act2), WG_F16)
     assert rel(act2, want) < 2e-3
+
+
+@pytest.mark.parametrize("same_draft", [True, False])
+def test_speculative_decoding_emits_the_target_greedy_tokens(same_draft):
+    """Draft k = 4, verify, accept on the GPU (one CUDA graph per round): the
+    emitted tokens equal the target's plain greedy continuation; a draft
+    identical to the target has every proposal accepted."""
+    from webgllm_b200.model import DecoderConfig, DecoderModel
+    from webgllm_b200.speculative import SpeculativeDecoder
+
+    cfg = DecoderConfig("tiny-target", 3, 256, 8, 2, 64, 512, 1000, 1e-5, 1e4)
+    dcfg = cfg if same_draft else DecoderConfig("tiny-draft", 2, 128, 2, 1, 64, 256, 1000, 1e-5, 1e4)
+    B, k, n_new = 2, 4, 24
+    prompts = torch.randint(0, cfg.vocab, (B, 16), generator=gen(21), device="cuda").to(torch.int32)
+    plain = DecoderModel(cfg, seed=11, max_ctx=128, max_rows=64, batch=B)
+    want = plain.generate(prompts, n_new, use_graph=False)
+    t = DecoderModel(cfg, seed=11, max_ctx=128, max_rows=64, batch=B)
+    d = DecoderModel(dcfg, seed=11 if same_draft else 12, max_ctx=128, max_rows=64, batch=B)
+    spec = SpeculativeDecoder(t, d, k=k, max_new=64)
+    spec.prefill(prompts)
+    spec.step()  # eager round configures every kernel
+    spec.capture()
+    rounds = 1
+    while int(spec.out_len.min().item()) < n_new and rounds < 40:
+        spec.run_step()
+        rounds += 1
+    torch.cuda.synchronize()
+    got = spec.out[:, :n_new]
+    assert torch.equal(got, want), (got, want)
+    if same_draft:
+        # every round keeps all k proposals and adds the target's own token
+        assert spec.accepted.tolist() == [k * rounds] * B
+        assert spec.out_len.tolist() == [1 + (k + 1) * rounds] * B

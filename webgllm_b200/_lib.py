@@ -76,6 +76,7 @@ SIGNATURES = {
     "wg_pick_keys": (_I, [_P, _P, _I, _P]),
     "wg_argmax": (_I, [_P, _P, _I, _I, _P]),
     "wg_add_i32": (_I, [_P, _P, _I, _I]),
+    "wg_spec_accept": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P]),
     # include/webgllm_comm.h
     "wg_ipc_alloc": (_I, [_P, _SZ, _PP, _P]),
     "wg_ipc_free": (_I, [_P, _P]),

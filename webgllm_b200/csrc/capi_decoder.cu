@@ -181,6 +181,21 @@ int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out) {
   return finish(ctx, wg::launch_argmax(logits, rows, V, out, ctx->stream, ctx->pdl), "wg_argmax");
 }
 
+int wg_spec_accept(wg_ctx *ctx, const int32_t *drafts, const int32_t *picks, int batch, int k, int32_t *pos_target,
+                   int32_t *pos_draft, int32_t *next_target, int32_t *next_draft, int32_t *out, int out_cap,
+                   int32_t *out_len, int32_t *accepted) {
+  WG_BEGIN(ctx);
+  if (batch < 0 || k < 0 || out_cap < 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_spec_accept: bad shape");
+  if (!batch) return WG_OK;
+  if ((k && !drafts) || !picks || !pos_target || !pos_draft || !next_target || !next_draft || !out_len || !accepted ||
+      (out_cap && !out))
+    return dfail(ctx, WG_INVALID_ARGUMENT, "wg_spec_accept: null");
+  return finish(ctx,
+                wg::launch_spec_accept(drafts, picks, batch, k, pos_target, pos_draft, next_target, next_draft, out,
+                                       out_cap, out_len, accepted, ctx->stream, ctx->pdl),
+                "wg_spec_accept");
+}
+
 int wg_add_i32(wg_ctx *ctx, int32_t *counters, int n, int delta) {
   WG_BEGIN(ctx);
   if (n < 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_add_i32: n %d", n);

@@ -835,6 +835,36 @@ __global__ void pick_keys_kernel(const unsigned long long *keys, int rows, int32
     ids[i] = (int32_t)(0xffffffffu - (unsigned)((unsigned long long)keys[i] & 0xffffffffu));
 }
 
+// Greedy speculative decoding, acceptance (one thread per sequence): the
+// draft proposed d_1..d_k (drafts[b][j] = d_{j+1}); the target's picks at the
+// k + 1 verified rows are g_0..g_k (picks[j][b] = g_j, its token for the
+// position after row j). Accept the longest prefix with d_{j+1} == g_j, emit
+// it and g_n (the target's own token after it), and rewind both models'
+// positions to just past what was kept: the target's verify forward advanced
+// its position by k + 1; rows past the kept prefix stay in the caches but lie
+// beyond the positions, so the next rows overwrite them.
+__global__ void spec_accept_kernel(const int32_t *drafts, const int32_t *picks, int batch, int k, int32_t *pos_t,
+                                   int32_t *pos_d, int32_t *next_t, int32_t *next_d, int32_t *out, int out_cap,
+                                   int32_t *out_len, int32_t *accepted) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  int n = 0;
+  while (n < k && drafts[b * k + n] == picks[n * batch + b]) n++;
+  const int32_t last = picks[n * batch + b];
+  int len = out_len[b];
+  for (int i = 0; i < n && len < out_cap; i++) out[(size_t)b * out_cap + len++] = drafts[b * k + i];
+  if (len < out_cap) out[(size_t)b * out_cap + len++] = last;
+  out_len[b] = len;
+  accepted[b] += n;
+  const int32_t p = pos_t[b] - (k + 1) + n + 1;
+  pos_t[b] = p;
+  pos_d[b] = p;
+  next_t[b] = last;
+  next_d[b] = last;
+}
+
 __global__ void add_i32_kernel(int32_t *p, int n, int delta) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
   pdl_wait();     // inputs come from the previous kernel
@@ -1012,6 +1042,13 @@ cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *out, cu
 cudaError_t launch_pick_keys(const unsigned long long *keys, int rows, int32_t *ids, cudaStream_t s, bool pdl) {
   return launch_k(pick_keys_kernel, dim3(1), dim3(rows < 1024 ? ((rows + 31) / 32) * 32 : 1024), 0, s, pdl, keys,
                   rows, ids);
+}
+
+cudaError_t launch_spec_accept(const int32_t *drafts, const int32_t *picks, int batch, int k, int32_t *pos_t,
+                               int32_t *pos_d, int32_t *next_t, int32_t *next_d, int32_t *out, int out_cap,
+                               int32_t *out_len, int32_t *accepted, cudaStream_t s, bool pdl) {
+  return launch_k(spec_accept_kernel, dim3((batch + 127) / 128), dim3(128), 0, s, pdl, drafts, picks, batch, k, pos_t,
+                  pos_d, next_t, next_d, out, out_cap, out_len, accepted);
 }
 
 cudaError_t launch_add_i32(int32_t *p, int n, int delta, cudaStream_t s, bool pdl) {

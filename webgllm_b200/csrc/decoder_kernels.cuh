@@ -35,5 +35,8 @@ cudaError_t launch_head(const void *x, const float *na, const float *nb, const f
 cudaError_t launch_pick_keys(const unsigned long long *keys, int rows, int32_t *ids, cudaStream_t s, bool pdl);
 cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *out, cudaStream_t s, bool pdl);
 cudaError_t launch_add_i32(int32_t *p, int n, int delta, cudaStream_t s, bool pdl);
+cudaError_t launch_spec_accept(const int32_t *drafts, const int32_t *picks, int batch, int k, int32_t *pos_t,
+                               int32_t *pos_d, int32_t *next_t, int32_t *next_d, int32_t *out, int out_cap,
+                               int32_t *out_len, int32_t *accepted, cudaStream_t s, bool pdl);
 
 }  // namespace wg

@@ -210,6 +210,9 @@ class DecoderModel:
         self.ids = torch.zeros(R, dtype=torch.int32, device="cuda")
         self.next_id = torch.zeros(B, dtype=torch.int32, device="cuda")
         self.graph = None
+        # speculative verification: greedy picks after every row of each
+        # sequence, [rows per sequence][batch] (None: the last row only)
+        self.row_picks = None
         # row-parallel exchange: the push all-reduce for decode rows, NCCL
         # for the rest (and for everything when push is False)
         self.comm = None
@@ -330,6 +333,14 @@ class DecoderModel:
         B, rps = self.batch, rows // self.batch
         last = rps - 1
         sharded = self.world > 1
+        if self.row_picks is not None:
+            if sharded:
+                raise ValueError("speculative verification runs on one GPU")
+            for j in range(rps - 1):  # every row but the last: its pick only
+                self._c(L.wg_head_rmsnorm(c, P(cur[j].data_ptr()), P(add[j].data_ptr() if add is not None else None),
+                                          P(self.final_norm.data_ptr()), cfg.eps, B, rps, cfg.hidden,
+                                          P(self.head.data_ptr()), self.V, self.vocab_offset,
+                                          P(self.logits.data_ptr()), P(self.row_picks[j].data_ptr()), None))
         self._c(L.wg_head_rmsnorm(c, P(cur[last].data_ptr()), P(add[last].data_ptr() if add is not None else None),
                                   P(self.final_norm.data_ptr()), cfg.eps, B, rps, cfg.hidden,
                                   P(self.head.data_ptr()), self.V, self.vocab_offset, P(self.logits.data_ptr()),
@@ -340,6 +351,8 @@ class DecoderModel:
 
             self._all_reduce(self.keys, dist.ReduceOp.MAX)
             self._c(L.wg_pick_keys(c, P(self.keys.data_ptr()), B, P(self.next_id.data_ptr())))
+        if self.row_picks is not None:
+            self.row_picks[last].copy_(self.next_id)
         self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), B, rps))
 
     def _forward_fused(self, ids: torch.Tensor, rows: int):
