@@ -333,18 +333,19 @@ def main() -> None:
 
 def run_decode(world, rank, barrier, max_over_ranks, hbm):
     """Greedy generation (webgllm_b200.runner): configs 2 and 3 on one GPU
-    and config 4 (batch 8) on all ranks, tensor-parallel when world > 1.
+    and config 4 (batch 8) on all ranks, tensor-parallel when world > 1 (once
+    with the push all-reduce, once with NCCL's).
     Times are the max over ranks; `frac_hbm` is the bytes one decode step
     must read per GPU over the step time, against the measured copy
     bandwidth."""
     from webgllm_b200 import runner
 
-    names = ["2", "3", "4"] if world == 1 else ["4"]
+    runs = [("2", None), ("3", None), ("4", None)] if world == 1 else [("4", True), ("4", False)]
     out = []
-    for k in names:
+    for k, push in runs:
         cfg, batch, prompt, gen = runner.WORKLOADS[k]
         tp = (rank, world, None) if world > 1 else None
-        r = runner.measure(cfg, batch, prompt, gen, tp=tp, barrier=barrier)
+        r = runner.measure(cfg, batch, prompt, gen, tp=tp, barrier=barrier, push=bool(push))
         step_ms = max_over_ranks(r["decode_ms_per_step"])
         prefill_ms = max_over_ranks(r["prefill_ms"])
         steps = gen - 1
@@ -352,12 +353,24 @@ def run_decode(world, rank, barrier, max_over_ranks, hbm):
         out.append({
             "config": int(k), "model": r["model"], "batch": batch, "prompt_tokens": prompt,
             "generated_tokens": gen, "tensor_parallel": world if k == "4" else 1,
+            "exchange": None if push is None else ("push all-reduce (GEMV epilogue, NVLink P2P)" if push else "NCCL all-reduce"),
             "decode_tok_s": round(batch / (step_ms / 1e3), 1), "decode_ms_per_step": round(step_ms, 4),
             "prefill_ms": round(prefill_ms, 3), "prefill_tok_s": round(batch * prompt / (prefill_ms / 1e3), 1),
             "e2e_tok_s": round(batch * gen / total_s, 1),
             "step_bytes_per_gpu": int(r["step_bytes"]),
             "frac_hbm": round(r["step_bytes"] / (step_ms / 1e3) / 1e9 / hbm, 4),
             "first_tokens": r["tokens_head"][0],
+        })
+    if world == 1:
+        # config 4's speculative workload (draft k = 4); random-init draft and
+        # target rarely agree, so the acceptance rate comes with the rate
+        cfg, batch, prompt, gen = runner.WORKLOADS["4"]
+        r = runner.measure_speculative(cfg, batch, prompt, gen, k=4)
+        out.append({
+            "config": 4, "model": r["model"], "speculative": True, "draft": r["draft"], "k": r["k"],
+            "batch": batch, "prompt_tokens": prompt, "generated_tokens": gen,
+            "decode_tok_s": round(r["decode_tok_s"], 1), "ms_per_round": round(r["decode_ms_per_round"], 4),
+            "acceptance": round(r["acceptance"], 4), "prefill_ms": round(r["prefill_ms"], 3),
         })
     return out
 

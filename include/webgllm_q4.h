@@ -135,8 +135,8 @@ int wg_q4_matrix_row(wg_ctx *ctx, const wg_q4mat *m, int n, float *out);
 /* y = x . W^T for M rows of activations: x [M][K] (x_dtype), y [M][N]
  * (y_dtype), both device pointers, row-major and contiguous. Weight
  * (n, k) = scale * (q - zero) of its block. Few rows (the reference's
- * split path, rows <= 8) run the decode GEMV; many rows the tensor-core
- * GEMM. fp16 outputs saturate at +-65504 as packH2 does
+ * split path, rows <= 8; here up to 16) run the decode GEMV; more rows the
+ * tensor-core GEMM. fp16 outputs saturate at +-65504 as packH2 does
  * (src/gpu/kernels.ts:32-36). Enqueued on the context's stream. */
 int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype,
                  int M, void *y, int y_dtype);

@@ -445,7 +445,7 @@ namespace {
 // of CTAs or re-stage several rows of x in each of them. WG_GEMV_WIDE=0 / 1
 // forces one or the other (measurement).
 bool use_wide(const wg_ctx *ctx, const wg::GemvArgs &a) {
-  if (a.M > wg::kProMaxTokens) return false;
+  if (a.M > 32 || (a.pro.kind != wg::kProNone && a.M > wg::kProMaxTokens)) return false;
   if (ctx->gemv_wide >= 0) return ctx->gemv_wide == 1;
   wg::GemvArgs t = a;
   if (!wg::plan_gemv(t, ctx->num_sms)) return true;
@@ -471,8 +471,11 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
   if (push && M > wg::kGemvMaxTokens)
     return fail(ctx, WG_UNSUPPORTED, "a pushing matmul takes at most %d rows (got %d)", wg::kGemvMaxTokens, M);
   // Many rows: the tcgen05 GEMM (src/engine.ts:4684: more rows than the
-  // split path takes go to the prompt matmul).
-  if (M > wg::kGemvMaxTokens && wg::gemm_supported()) {
+  // split path takes go to the prompt matmul). Measured on B200, the GEMM
+  // (latency-bound near 18 us at 4096 x 4096) beats the GEMV from 17 rows
+  // on; pushes and epilogues stay in the GEMV, which has them.
+  const bool gemm_rows = M > wg::kGemvMaxTokens || (M > 16 && !push && epi == wg::kEpiNone);
+  if (gemm_rows && wg::gemm_supported()) {
     wg::GemmArgs g{};
     g.nib = m->nib;
     g.scl = m->scl;

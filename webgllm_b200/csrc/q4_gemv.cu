@@ -90,7 +90,10 @@ __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a0, const u
 
 // One 16 x 64 tile: four K steps of mma.m16n8k16 per token group, two
 // 32-weight blocks each scaled in fp32 into acc.
-template <int NG, bool ZEROS>
+// SPLIT: the block's two 16-wide K steps accumulate separately (two
+// independent MMAs, then added), for kernels with few warps to hide the MMA
+// latency; otherwise they chain into one accumulator.
+template <int NG, bool ZEROS, bool SPLIT = false>
 __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_scl, const uint8_t *s_zro,
                                          const __half *xt, int stride, int M, int lane, float acc[NG][4]) {
   const int g = lane >> 2;
@@ -109,8 +112,6 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
       lo_g8 = zp_lo((zz >> 8) & 15u);
       hi_g8 = zp_hi((zz >> 8) & 15u);
     }
-    // the block's two 16-wide K steps accumulate separately (independent
-    // MMAs), then add
     float blk[2][NG][4];
 #pragma unroll
     for (int js = 0; js < 2; js++)
@@ -129,17 +130,18 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
         uint2 b = make_uint2(0, 0);
         if (tok < M) b = *reinterpret_cast<const uint2 *>(xt + (size_t)tok * stride + 16 * j);
         // fragment k {2t,2t+1 | 2t+8,2t+9} <-> K offset {4t,4t+1 | 4t+2,4t+3}
-        mma_16816(blk[js][ng], P[0], P[2], P[1], P[3], b.x, b.y);
+        mma_16816(blk[SPLIT ? js : 0][ng], P[0], P[2], P[1], P[3], b.x, b.y);
       }
     }
     const uint32_t sp = bsel ? sv.y : sv.x;
     const float2 sc = __half22float2(*reinterpret_cast<const __half2 *>(&sp));
 #pragma unroll
     for (int ng = 0; ng < NG; ng++) {
-      acc[ng][0] = fmaf(sc.x, blk[0][ng][0] + blk[1][ng][0], acc[ng][0]);
-      acc[ng][1] = fmaf(sc.x, blk[0][ng][1] + blk[1][ng][1], acc[ng][1]);
-      acc[ng][2] = fmaf(sc.y, blk[0][ng][2] + blk[1][ng][2], acc[ng][2]);
-      acc[ng][3] = fmaf(sc.y, blk[0][ng][3] + blk[1][ng][3], acc[ng][3]);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float v = SPLIT ? blk[0][ng][e] + blk[1][ng][e] : blk[0][ng][e];
+        acc[ng][e] = fmaf(e < 2 ? sc.x : sc.y, v, acc[ng][e]);
+      }
     }
   }
 }
@@ -511,6 +513,7 @@ __global__ void __launch_bounds__(kThreads) prologue_kernel(const Prologue p, in
 // stay in shared memory and the cluster reduces them once at the end.
 
 constexpr int kWideXBudget = 96 * 1024;   // x slice per CTA
+constexpr int kWideMaxTokens = 32;        // rows (4 token groups of 8)
 constexpr int kWideSmemMax = 200 * 1024;
 constexpr int kWWarps = 16;                // warps of a wide CTA (one CTA per SM)
 constexpr int kWThreads = kWWarps * 32;
@@ -522,18 +525,19 @@ struct WideSmem {
 
 __host__ __device__ inline WideSmem wide_smem(int M, int ktc, int S, int J, int C, bool zeros) {
   WideSmem w;
+  const int NG = (M + 7) / 8;
   w.xstride = ktc * kTileK + 16;
   w.stage_bytes = align_to(ktc * (kTileNibBytes + kTileSclBytes + (zeros ? kTileZroBytes : 0)), 128);
   w.x = 0;
   w.stage = align_to(w.x + M * w.xstride * 2, 128);
   w.bars = align_to(w.stage + S * w.stage_bytes, 8);
   w.red = align_to(w.bars + (S + 1) * 8, 16);  // + the x barrier
-  w.part = w.red + kWWarps * 128 * 4;
-  w.total = w.part + (C > 1 ? J * 128 * 4 : 0);
+  w.part = w.red + kWWarps * NG * 128 * 4;
+  w.total = w.part + (C > 1 ? J * NG * 128 * 4 : 0);
   return w;
 }
 
-template <bool ZEROS, int PRO>
+template <int NG, bool ZEROS, int PRO>
 __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -545,8 +549,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   const int kt1 = min(a.KT, kt0 + a.kt_per_cta);
   const int ktc = kt1 - kt0;
   const int J = (a.NT - g + G - 1) / G;  // columns of this CTA: g, g + G, ...
-  const int Jmax = (a.NT + G - 1) / G;
-  const WideSmem L = wide_smem(a.M, a.kt_per_cta, S, Jmax, C, ZEROS);
+  const WideSmem L = wide_smem(a.M, a.kt_per_cta, S, a.part_cols, C, ZEROS);
   const int tpw = (a.kt_per_cta + kWWarps - 1) / kWWarps;
   const int wt0 = min(ktc, warp * tpw), wt1 = min(ktc, wt0 + tpw);  // this warp's K tiles
   __half *xs = reinterpret_cast<__half *>(smem + L.x);
@@ -641,72 +644,80 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   if (a.trigger_at <= 1) pdl_trigger();
   if (a.trace && threadIdx.x == 0) ts[3] = globaltimer();
 
-  // 3. Columns.
-  constexpr int kOut = 16 * 8;
+  // 3. Columns. With a K split, the per-column sums wait in `part` (Jc
+  //    columns at a time) and the cluster reduces them a chunk at a time:
+  //    rank c takes entries c, c + C, ... of the chunk.
+  constexpr int kOut = 16 * 8 * NG;
+  const int Jc = a.part_cols;
+  auto flush = [&](int j0, int j1) {  // columns [j0, j1), all CTAs of the cluster together
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int per = a.epi == kEpiNone ? kOut : kOut / 2;  // outputs per column
+    for (int idx = crank + C * (int)threadIdx.x; idx < (j1 - j0) * per; idx += C * kWThreads) {
+      const int jj = idx / per, o = idx - jj * per;
+      const int r = o / (8 * NG), tok = o - r * (8 * NG);
+      float sum = 0.0f, up = 0.0f;
+      for (int c = 0; c < C; c++) {
+        const float *pc = cluster.map_shared_rank(part, c) + jj * kOut;
+        sum += pc[o];
+        if (a.epi != kEpiNone) up += pc[o + kOut / 2];  // row r + 8: index + 8 * 8NG
+      }
+      if (a.epi == kEpiNone)
+        emit(a, parity, g + (j0 + jj) * G, r, tok, sum);
+      else
+        emit_pair(a, g + (j0 + jj) * G, r, tok, sum, up);
+    }
+    cluster.sync();
+  };
   for (int j = 0; j < J; j++) {
-    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+    float acc[NG][4];
+#pragma unroll
+    for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) acc[ng][e] = 0.0f;
     const int st = j % S;
     mbar_wait_bounded(&bars[st], (j / S) & 1, a.flags);
     const uint8_t *sb = stages + st * L.stage_bytes;
 #pragma unroll 2
     for (int i = wt0; i < wt1; i++)
-      tile_mma<1, ZEROS>(sb + i * kTileNibBytes, sb + nib_b + i * kTileSclBytes,
+      tile_mma<NG, ZEROS, NG == 1>(sb + i * kTileNibBytes, sb + nib_b + i * kTileSclBytes,
                          sb + nib_b + scl_b + i * kTileZroBytes, xs + i * kTileK + 4 * t, L.xstride, M, lane, acc);
 #pragma unroll
-    for (int e = 0; e < 4; e++) red[(warp * 4 + e) * 32 + lane] = acc[0][e];
+    for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) red[((warp * NG + ng) * 4 + e) * 32 + lane] = acc[ng][e];
     __syncthreads();
     if (threadIdx.x == 0 && j + S < J) issue(j + S);  // every warp is done with the stage
     const int nt = g + j * G;
     auto warp_sum_at = [&](int r, int tok) {
-      const int ln = 4 * (r & 7) + (tok >> 1);
-      const int e = ((r >> 3) << 1) | (tok & 1);
+      const int ng = tok >> 3, tk = tok & 7;
+      const int ln = 4 * (r & 7) + (tk >> 1);
+      const int e = ((r >> 3) << 1) | (tk & 1);
       float sum = 0.0f;
 #pragma unroll
-      for (int w2 = 0; w2 < kWWarps; w2++) sum += red[(w2 * 4 + e) * 32 + ln];
+      for (int w2 = 0; w2 < kWWarps; w2++) sum += red[((w2 * NG + ng) * 4 + e) * 32 + ln];
       return sum;
     };
     if (C > 1 || a.epi == kEpiNone) {
       for (int o = threadIdx.x; o < kOut; o += kWThreads) {
-        const int r = o / 8, tok = o - r * 8;
+        const int r = o / (8 * NG), tok = o - r * (8 * NG);
         const float sum = warp_sum_at(r, tok);
         if (C > 1)
-          part[j * kOut + o] = sum;
+          part[(j % Jc) * kOut + o] = sum;
         else
           emit(a, parity, nt, r, tok, sum);
       }
     } else {
       for (int o = threadIdx.x; o < kOut / 2; o += kWThreads) {
-        const int r = o / 8, tok = o - r * 8;
+        const int r = o / (8 * NG), tok = o - r * (8 * NG);
         emit_pair(a, nt, r, tok, warp_sum_at(r, tok), warp_sum_at(r + 8, tok));
       }
     }
     __syncthreads();  // red is reused by the next column
+    if (C > 1 && (j % Jc == Jc - 1 || j == J - 1)) flush(j - j % Jc, j + 1);
   }
   if (a.trigger_at == 2) pdl_trigger();
   if (a.trace && threadIdx.x == 0) ts[4] = globaltimer();
-
-  // 4. K split: sum the per-column partials over the cluster (rank c takes
-  //    entries c, c + C, ... of every column).
-  if (C > 1) {
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    const int per = a.epi == kEpiNone ? kOut : kOut / 2;  // outputs per column
-    for (int idx = crank + C * (int)threadIdx.x; idx < J * per; idx += C * kWThreads) {
-      const int j = idx / per, o = idx - j * per;
-      const int r = o / 8, tok = o - r * 8;
-      float sum = 0.0f, up = 0.0f;
-      for (int c = 0; c < C; c++) {
-        const float *pc = cluster.map_shared_rank(part, c) + j * kOut;
-        sum += pc[o];
-        if (a.epi != kEpiNone) up += pc[o + kOut / 2];  // row r + 8
-      }
-      if (a.epi == kEpiNone)
-        emit(a, parity, g + j * G, r, tok, sum);
-      else
-        emit_pair(a, g + j * G, r, tok, sum, up);
-    }
-    cluster.sync();
-  }
   // No copy may still be writing shared memory at exit (only possible after
   // a timed-out wait).
   if (threadIdx.x == 0) {
@@ -729,7 +740,7 @@ int wide_max_clusters(int C, int smem, int num_sms) {
   const auto key = std::make_pair(C, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  auto kern = gemv_wide_kernel<false, kProNone>;
+  auto kern = gemv_wide_kernel<1, false, kProNone>;
   int n = 0;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMax) == cudaSuccess &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
@@ -752,12 +763,11 @@ int wide_max_clusters(int C, int smem, int num_sms) {
   return n;
 }
 
-template <bool ZEROS, int PRO>
+template <int NG, bool ZEROS, int PRO>
 cudaError_t launch_wide_t(const GemvArgs &a, cudaStream_t stream, bool pdl) {
   const int G = a.groups;
-  const int Jmax = (a.NT + G - 1) / G;
-  const WideSmem L = wide_smem(a.M, a.kt_per_cta, a.stages, Jmax, a.cluster, ZEROS);
-  auto kern = gemv_wide_kernel<ZEROS, PRO>;
+  const WideSmem L = wide_smem(a.M, a.kt_per_cta, a.stages, a.part_cols, a.cluster, ZEROS);
+  auto kern = gemv_wide_kernel<NG, ZEROS, PRO>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMax);
@@ -829,7 +839,7 @@ bool plan_gemv(GemvArgs &a, int num_sms) {
 }
 
 bool plan_gemv_wide(GemvArgs &a, int num_sms) {
-  if (a.M < 1 || a.M > kProMaxTokens) return false;
+  if (a.M < 1 || a.M > kWideMaxTokens || (a.pro.kind != kProNone && a.M > kProMaxTokens)) return false;
   const bool zeros = a.zro != nullptr;
   int C = 1;
   while (a.M * ((a.KT + C - 1) / C) * kTileK * 2 > kWideXBudget) C++;
@@ -840,28 +850,43 @@ bool plan_gemv_wide(GemvArgs &a, int num_sms) {
   int G = num_sms / C;
   if (G < 1) G = 1;
   if (G > a.NT) G = a.NT;
+  // stages, then the columns whose K-split sums wait for a cluster reduction
+  // (a few at least; the rest go in later chunks)
   int S = 4;
-  while (S > 1 && wide_smem(a.M, ktc, S, (a.NT + G - 1) / G * 2, C, zeros).total > kWideSmemMax) S--;
+  while (S > 1 && wide_smem(a.M, ktc, S, 4, C, zeros).total > kWideSmemMax) S--;
+  if (wide_smem(a.M, ktc, S, 1, C, zeros).total > kWideSmemMax) return false;
+  int Jc = (a.NT + G - 1) / G * 2;
+  while (Jc > 1 && wide_smem(a.M, ktc, S, Jc, C, zeros).total > kWideSmemMax) Jc--;
   // one wave: no more clusters than fit at once
-  const int fit = wide_max_clusters(C, wide_smem(a.M, ktc, S, (a.NT + G - 1) / G * 2, C, zeros).total, num_sms);
+  const int fit = wide_max_clusters(C, wide_smem(a.M, ktc, S, Jc, C, zeros).total, num_sms);
   if (G > fit) G = fit;
   const int J = (a.NT + G - 1) / G;
-  if (wide_smem(a.M, ktc, S, J, C, zeros).total > kWideSmemMax) return false;
+  if (Jc > J) Jc = J;
   a.kt_per_cta = ktc;
   a.cluster = C;
   a.groups = G;
   a.stages = S;
+  a.part_cols = Jc;
   return true;
 }
 
 cudaError_t launch_gemv_wide(const GemvArgs &a, cudaStream_t stream, bool pdl) {
   const bool z = a.zro != nullptr;
+  const int NG = (a.M + 7) / 8;
+  if (a.pro.kind != kProNone && NG != 1) return cudaErrorInvalidValue;
   switch (a.pro.kind) {
-    case kProNone: return z ? launch_wide_t<true, kProNone>(a, stream, pdl) : launch_wide_t<false, kProNone>(a, stream, pdl);
+    case kProNone:
+      switch (NG) {
+        case 1: return z ? launch_wide_t<1, true, kProNone>(a, stream, pdl) : launch_wide_t<1, false, kProNone>(a, stream, pdl);
+        case 2: return z ? launch_wide_t<2, true, kProNone>(a, stream, pdl) : launch_wide_t<2, false, kProNone>(a, stream, pdl);
+        case 3: return z ? launch_wide_t<3, true, kProNone>(a, stream, pdl) : launch_wide_t<3, false, kProNone>(a, stream, pdl);
+        case 4: return z ? launch_wide_t<4, true, kProNone>(a, stream, pdl) : launch_wide_t<4, false, kProNone>(a, stream, pdl);
+        default: return cudaErrorInvalidValue;
+      }
     case kProRmsNorm:
-      return z ? launch_wide_t<true, kProRmsNorm>(a, stream, pdl) : launch_wide_t<false, kProRmsNorm>(a, stream, pdl);
+      return z ? launch_wide_t<1, true, kProRmsNorm>(a, stream, pdl) : launch_wide_t<1, false, kProRmsNorm>(a, stream, pdl);
     case kProSwiglu:
-      return z ? launch_wide_t<true, kProSwiglu>(a, stream, pdl) : launch_wide_t<false, kProSwiglu>(a, stream, pdl);
+      return z ? launch_wide_t<1, true, kProSwiglu>(a, stream, pdl) : launch_wide_t<1, false, kProSwiglu>(a, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

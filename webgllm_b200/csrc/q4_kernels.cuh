@@ -68,7 +68,8 @@ struct GemvArgs {
   int trigger_at;  // when dependents may launch: 0 entry, 1 x staged, 2 multiplies done
   Prologue pro;    // kProNone: x as given; else x is made from pro (M <= kProMaxTokens)
   int groups;      // wide GEMV: column groups (grid.y)
-  int stages;      // wide GEMV: weight ring stages per warp
+  int stages;      // wide GEMV: weight ring stages
+  int part_cols;   // wide GEMV with a K split: columns reduced across the cluster at a time
   int push_on;     // outputs go to every rank's exchange buffer (comm.cuh), not y
   CommDev push;
   int epi;         // kEpiNone, or kEpiSwigluPairs: y [M][N/2] = silu(rows 16t..16t+7) * rows 16t+8..16t+15

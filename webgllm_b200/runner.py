@@ -85,3 +85,54 @@ def measure(cfg, batch: int, prompt_len: int, gen_len: int, tp=None, seed: int =
     del m
     torch.cuda.empty_cache()
     return res
+
+
+def measure_speculative(cfg, batch: int, prompt_len: int, gen_len: int, k: int = 4, seed: int = 0) -> dict:
+    """Config 4's speculative workload on one GPU: a random-init draft of
+    config 2's layout (the target's vocabulary) proposes k tokens a round.
+    With independent random weights the draft almost never agrees with the
+    target, so a round yields about one token per sequence: the acceptance
+    rate is reported with the throughput."""
+    from .speculative import SpeculativeDecoder, draft_config
+
+    ctx_len = prompt_len + gen_len + 2 * (k + 1) + 8
+    t = DecoderModel(cfg, seed=seed, max_ctx=ctx_len, max_rows=batch * prompt_len, batch=batch)
+    d = DecoderModel(draft_config(cfg), seed=seed + 100, max_ctx=ctx_len, max_rows=batch * prompt_len, batch=batch)
+    spec = SpeculativeDecoder(t, d, k=k, max_new=gen_len)
+    g = torch.Generator().manual_seed(seed + 1)
+    prompts = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=g).to("cuda", torch.int32)
+    spec.prefill(prompts)
+    spec.step()
+    spec.capture()
+    t.reset()
+    d.reset()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record(s)
+    spec.prefill(prompts)
+    ev[1].record(s)
+    rounds = 0
+    # rounds until every sequence has gen_len tokens (checked every 16 rounds)
+    while True:
+        for _ in range(16):
+            spec.graph.replay()
+        rounds += 16
+        if int(spec.out_len.min().item()) >= gen_len or rounds >= 4 * gen_len:
+            break
+    ev[2].record(s)
+    torch.cuda.synchronize()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    decode_ms = ev[1].elapsed_time(ev[2])
+    produced = int(spec.out_len.sum().item()) - batch  # after the prefill's token
+    res = {
+        "model": cfg.name, "draft": d.cfg.name, "k": k, "batch": batch, "rounds": rounds,
+        "decode_ms_per_round": decode_ms / rounds, "decode_tok_s": produced / (decode_ms / 1e3),
+        "acceptance": float(spec.accepted.sum().item()) / (rounds * batch * k),
+        "prefill_ms": prefill_ms,
+    }
+    spec.graph = None
+    del spec, t, d
+    torch.cuda.empty_cache()
+    return res
+
