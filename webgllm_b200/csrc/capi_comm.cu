@@ -109,12 +109,12 @@ int wg_comm_init(wg_ctx *ctx, int world, int rank, void *const *buffers, size_t 
   c->bytes = bytes;
   c->dev.world = world;
   c->dev.rank = rank;
-  // data: 2 parities x world slots, each slot a multiple of 16 floats
-  c->dev.slot = (long long)((bytes - wg::kCommHeaderBytes) / (2 * (size_t)world * sizeof(float))) / 16 * 16;
+  // data: 2 parities x world slots, each slot a multiple of 16 words
+  c->dev.slot = (long long)((bytes - wg::kCommHeaderBytes) / (2 * (size_t)world * sizeof(unsigned long long))) / 16 * 16;
   for (int r = 0; r < world; r++) {
     uint8_t *b = static_cast<uint8_t *>(buffers[r]);
     c->dev.hdr[r] = reinterpret_cast<unsigned long long *>(b);
-    c->dev.inbox[r] = reinterpret_cast<float *>(b + wg::kCommHeaderBytes);
+    c->dev.inbox[r] = reinterpret_cast<unsigned long long *>(b + wg::kCommHeaderBytes);
   }
   *out = c;
   return WG_OK;

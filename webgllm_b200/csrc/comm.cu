@@ -1,5 +1,6 @@
 // The consumer side of the push all-reduce (comm.cuh): wait for every rank's
-// partial of the next exchange, then sum them from this rank's own buffer.
+// partial of the next exchange (word by word), then sum them from this
+// rank's own buffer.
 #include <cooperative_groups.h>
 
 #include "comm.cuh"
@@ -9,46 +10,30 @@ namespace wg {
 namespace {
 
 constexpr int kReduceThreads = 256;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s, then give up and report
 
 __global__ void __launch_bounds__(kReduceThreads) comm_reduce_kernel(const CommDev c, int M, int N, float *out,
                                                                      unsigned *flags) {
   pdl_trigger();
   pdl_wait();  // this rank's own push (the previous kernel) is complete
-  __shared__ unsigned long long s_e;
-  __shared__ bool s_last;
+  __shared__ unsigned s_e;
   unsigned long long *hdr = c.hdr[c.rank];
-  if (threadIdx.x == 0) {
-    const unsigned long long e = *(volatile unsigned long long *)(hdr + kCommConsSeq) + 1;
-    s_e = e;
-    const unsigned long long t0 = globaltimer();
-    for (int r = 0; r < c.world; r++) {
-      while (ld_acquire_sys(hdr + kCommFlag0 + 8 * r) < e) {
-        if (globaltimer() - t0 > kWaitNs) {  // a rank never pushed: report, carry on
-          raise_flag(flags, kFlagTimeout);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-  }
+  if (threadIdx.x == 0) s_e = (unsigned)(*(volatile unsigned long long *)(hdr + kCommConsSeq) + 1);
   __syncthreads();
-  const int parity = (int)(s_e & 1);
-  const float *base = c.inbox[c.rank] + (long long)parity * c.world * c.slot;
+  const unsigned e = s_e;
+  const unsigned long long *base = c.inbox[c.rank] + (long long)(e & 1) * c.world * c.slot;
   const int total = M * N;
   for (int i = blockIdx.x * kReduceThreads + threadIdx.x; i < total; i += gridDim.x * kReduceThreads) {
     // slot layout [n][token]; out [token][n]
     const int n = i / M, tok = i - n * M;
     float v = 0.0f;
-    for (int r = 0; r < c.world; r++) v += base[(long long)r * c.slot + i];
+    for (int r = 0; r < c.world; r++) v += comm_wait_word(base + (long long)r * c.slot + i, e, flags);
     out[(size_t)tok * N + n] = v;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned *count = reinterpret_cast<unsigned *>(hdr + kCommConsCount);
-    s_last = atomicAdd(count, 1u) == gridDim.x - 1;
-    if (s_last) {
-      *(volatile unsigned long long *)(hdr + kCommConsSeq) = s_e;
+    if (atomicAdd(count, 1u) == gridDim.x - 1) {
+      *(volatile unsigned long long *)(hdr + kCommConsSeq) = e;
       *count = 0;
     }
   }
@@ -58,8 +43,8 @@ __global__ void __launch_bounds__(kReduceThreads) comm_reduce_kernel(const CommD
 // CTAs per row (each CTA a K/CL slice, its sum of squares shared through
 // distributed shared memory): x fp16 = rmsnorm(a + b) * w, optional
 // resid_out = a + b. With COMM, b is the sum over ranks of the next
-// exchange's partials (layout [k][row]) after waiting for every rank's flag
-// — the all-reduce, the residual add and the norm in one launch.
+// exchange's partials (layout [k][row]), each word waited for — the
+// all-reduce, the residual add and the norm in one launch.
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxPerThread = 16;  // K / CL / 256 values kept in registers
 
@@ -76,25 +61,10 @@ __global__ void __launch_bounds__(kNormThreads) addnorm_kernel(const float *a, c
   const int Kc = K / CL, k0 = cr * Kc;
   __shared__ float s_part[kNormThreads / 32];
   __shared__ float s_ss;
-  __shared__ unsigned long long s_e;
-  __shared__ bool s_last;
-  const float *base = nullptr;
+  __shared__ unsigned s_e;
+  const unsigned long long *base = nullptr;
   if (COMM) {
-    unsigned long long *hdr = c.hdr[c.rank];
-    if (threadIdx.x == 0) {
-      const unsigned long long e = *(volatile unsigned long long *)(hdr + kCommConsSeq) + 1;
-      s_e = e;
-      const unsigned long long t0 = globaltimer();
-      for (int r = 0; r < c.world; r++) {
-        while (ld_acquire_sys(hdr + kCommFlag0 + 8 * r) < e) {
-          if (globaltimer() - t0 > 2000000000ull) {
-            raise_flag(flags, kFlagTimeout);
-            break;
-          }
-          __nanosleep(64);
-        }
-      }
-    }
+    if (threadIdx.x == 0) s_e = (unsigned)(*(volatile unsigned long long *)(c.hdr[c.rank] + kCommConsSeq) + 1);
     __syncthreads();
     base = c.inbox[c.rank] + (long long)(s_e & 1) * c.world * c.slot;
   }
@@ -107,7 +77,7 @@ __global__ void __launch_bounds__(kNormThreads) addnorm_kernel(const float *a, c
     if (threadIdx.x + j * kNormThreads < Kc) {
       float add = 0.0f;
       if (COMM) {
-        for (int r = 0; r < c.world; r++) add += base[(long long)r * c.slot + (long long)k * M + m];
+        for (int r = 0; r < c.world; r++) add += comm_wait_word(base + (long long)r * c.slot + (long long)k * M + m, s_e, flags);
       } else if (b) {
         add = b[(size_t)m * K + k];
       }
@@ -139,8 +109,7 @@ __global__ void __launch_bounds__(kNormThreads) addnorm_kernel(const float *a, c
     if (threadIdx.x == 0) {
       unsigned long long *hdr = c.hdr[c.rank];
       unsigned *count = reinterpret_cast<unsigned *>(hdr + kCommConsCount);
-      s_last = atomicAdd(count, 1u) == gridDim.x * gridDim.y - 1;
-      if (s_last) {
+      if (atomicAdd(count, 1u) == gridDim.x * gridDim.y - 1) {
         *(volatile unsigned long long *)(hdr + kCommConsSeq) = s_e;
         *count = 0;
       }

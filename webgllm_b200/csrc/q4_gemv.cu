@@ -161,7 +161,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f +
 // The final value of output row n (tile nt, row r) for token tok: stored,
 // pushed to the exchange, or (SwiGLU pairs, only rows r < 8 of a tile,
 // given the paired up value) activated into y [M][N/2].
-__device__ __forceinline__ void emit(const GemvArgs &a, int parity, int nt, int r, int tok, float v) {
+__device__ __forceinline__ void emit(const GemvArgs &a, unsigned parity, int nt, int r, int tok, float v) {
   const int n = nt * kTileRows + r;
   if (n >= a.N || tok >= a.M) return;
   if (a.push_on)
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L.bar) + warp;
   __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
-  const int parity = a.push_on ? push_parity(a.push) : 0;
+  const unsigned parity = a.push_on ? push_seq(a.push) : 0u;  // the exchange's sequence number
 
   // 1. Each warp starts the copies of its own tiles (the TMA engine, one
   //    mbarrier a warp): weights depend on nothing the previous kernel
@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   const int nib_b = ktc * kTileNibBytes, scl_b = ktc * kTileSclBytes;
   __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
-  const int parity = a.push_on ? push_parity(a.push) : 0;
+  const unsigned parity = a.push_on ? push_seq(a.push) : 0u;  // the exchange's sequence number
 
   auto issue = [&](int j) {  // thread 0: column g + j*G (this CTA's K range) into stage j % S
     const int st = j % S;
