@@ -57,6 +57,15 @@ int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int batch, int H, int Hk
 int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                  const void *v_cache, int cache_len, const int32_t *pos, void *out);
 
+/* wg_rope_kv followed by wg_attention for a decode step (one row per
+ * sequence: rows = batch), in one launch: each CTA forms its heads' rotated
+ * queries itself and the CTA whose key slice holds the new position appends
+ * the new key and value to the caches. Same results as the two calls;
+ * Dh in {64, 128, 256}. */
+int wg_rope_attention(wg_ctx *ctx, const float *qkv, int batch, int H, int Hkv, int Dh, const int32_t *pos,
+                      float theta, const float *q_norm, const float *k_norm, float eps, void *k_cache, void *v_cache,
+                      int cache_len, void *out);
+
 /* SwiGLU (REDUCE_SWIGLU, src/gpu/kernels.ts:1066-1077): gate_up fp32
  * [rows][2I] (gate | up) -> out[r][i] = silu(gate) * up, in out_dtype. */
 int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int out_dtype);

@@ -180,6 +180,37 @@ def test_rope_and_attention_batched_sequences():
         assert (out[sl].float() - want).abs().max().item() < 2e-3 * max(1.0, want.abs().max().item())
 
 
+@pytest.mark.parametrize("B,H,Hkv,Dh,qk", [(1, 32, 4, 64, False), (3, 24, 8, 64, True), (8, 32, 8, 128, False),
+                                         (2, 16, 1, 256, True)])
+def test_rope_attention_equals_the_two_kernels(B, H, Hkv, Dh, qk):
+    """The fused decode launch gives the same caches and outputs as wg_rope_kv
+    followed by wg_attention."""
+    g = gen(B * 100 + H + Dh)
+    cache_len = 700
+    pos0 = [int(v) for v in torch.randint(0, 650, (B,), generator=torch.Generator().manual_seed(B))]
+    qkv = torch.randn((B, (H + 2 * Hkv) * Dh), generator=g, device="cuda")
+    qn = torch.rand(Dh, generator=g, device="cuda") + 0.5 if qk else None
+    kn = torch.rand(Dh, generator=g, device="cuda") + 0.5 if qk else None
+    kc = torch.randn((B, Hkv, cache_len, Dh), generator=g, device="cuda").half()
+    vc = torch.randn_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    pos = torch.tensor(pos0, dtype=torch.int32, device="cuda")
+    q = torch.empty((B, H, Dh), dtype=torch.float16, device="cuda")
+    out1 = torch.empty((B, H, Dh), dtype=torch.float16, device="cuda")
+    out2 = torch.empty_like(out1)
+    call(lib().wg_rope_kv, ptr(qkv), B, B, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4), ptr(qn), ptr(kn),
+         ctypes.c_float(1e-5), ptr(q), ptr(kc), ptr(vc), cache_len)
+    call(lib().wg_attention, ptr(q), B, B, H, Hkv, Dh, ptr(kc), ptr(vc), cache_len, ptr(pos), ptr(out1))
+    call(lib().wg_rope_attention, ptr(qkv), B, H, Hkv, Dh, ptr(pos), ctypes.c_float(1e4), ptr(qn), ptr(kn),
+         ctypes.c_float(1e-5), ptr(kc2), ptr(vc2), cache_len, ptr(out2))
+    assert torch.equal(vc2, vc)
+    # keys: the qk-norm's sum runs in another order (a warp, not the CTA)
+    assert (kc2.float() - kc.float()).abs().max().item() <= 1e-3 * kc.float().abs().max().item()
+    if not qk:
+        assert torch.equal(kc2, kc)
+    assert (out2.float() - out1.float()).abs().max().item() <= 2e-3 * max(1.0, out1.float().abs().max().item())
+
+
 def test_short_conv_batched_states():
     B, rps, D, W = 2, 5, 256, 3
     g = gen(5)

@@ -68,6 +68,7 @@ SIGNATURES = {
     "wg_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _P, _I]),
     "wg_rope_kv": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, ctypes.c_float, _P, _P, _P, _I]),
     "wg_attention": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P]),
+    "wg_rope_attention": (_I, [_P, _P, _I, _I, _I, _I, _P, ctypes.c_float, _P, _P, ctypes.c_float, _P, _P, _I, _P]),
     "wg_swiglu": (_I, [_P, _P, _I, _I, _P, _I]),
     "wg_swiglu_pairs": (_I, [_P, _P, _I, _I, _P, _I]),
     "wg_short_conv": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),

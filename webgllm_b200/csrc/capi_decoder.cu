@@ -99,6 +99,21 @@ int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv
                 "wg_attention");
 }
 
+int wg_rope_attention(wg_ctx *ctx, const float *qkv, int batch, int H, int Hkv, int Dh, const int32_t *pos,
+                      float theta, const float *q_norm, const float *k_norm, float eps, void *k_cache, void *v_cache,
+                      int cache_len, void *out) {
+  WG_BEGIN(ctx);
+  if (batch < 0 || H <= 0 || Hkv <= 0 || H % Hkv || H / Hkv > 16 || !(Dh == 64 || Dh == 128 || Dh == 256) ||
+      cache_len <= 0)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_rope_attention: bad shape (H %d, Hkv %d, Dh %d)", H, Hkv, Dh);
+  if (!batch) return WG_OK;
+  if (!qkv || !pos || !k_cache || !v_cache || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_rope_attention: null");
+  return finish(ctx,
+                wg::launch_rope_attention(qkv, batch, H, Hkv, Dh, pos, theta, q_norm, k_norm, eps, k_cache, v_cache,
+                                          cache_len, out, ctx->d_flags, ctx->num_sms, ctx->stream, ctx->pdl),
+                "wg_rope_attention");
+}
+
 int wg_swiglu(wg_ctx *ctx, const float *gate_up, int rows, int I, void *out, int out_dtype) {
   WG_BEGIN(ctx);
   if (rows < 0 || I <= 0) return dfail(ctx, WG_INVALID_SHAPE, "wg_swiglu: bad shape");

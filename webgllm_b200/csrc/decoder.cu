@@ -216,10 +216,55 @@ __device__ __forceinline__ void load_halves(const __half *p, float v[DPL]) {
   }
 }
 
-template <int DPL>  // head dims per lane: Dh = 32 * DPL
+// With ROPE (decode: one row per sequence), the kernel also does
+// rope_kv_kernel's work: every CTA turns its heads' q rows of qkv into
+// rotated, scaled fp16 queries itself, and the CTA whose key slice holds the
+// new position computes that key and value, appends them to the caches and
+// patches them into its shared-memory tile — one launch instead of two.
+struct RopeArgs {
+  const float *qkv;  // [rows][(H + 2 Hkv) Dh]
+  float theta;
+  const float *q_norm, *k_norm;  // or null
+  float eps;
+  unsigned *flags;
+};
+
+// q / k rows of qkv for one head, as rope_kv_kernel computes them: optional
+// RMS norm over Dh, rotate-half RoPE at position pos, scale; lane l holds
+// dims l + 32 i (i < DPL), so the rotate-half pairs (i, i + DPL/2) sit in
+// one lane. Values are rounded to fp16 as the separate kernel stores them.
+template <int DPL>
+__device__ __forceinline__ void rope_head(const float *src, const float *nw, float eps, float theta, int pos,
+                                          float scale, int lane, float out[DPL]) {
+  constexpr int Dh = 32 * DPL;
+  float v[DPL];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < DPL; i++) {
+    v[i] = src[lane + 32 * i];
+    ss += v[i] * v[i];
+  }
+  if (nw) {
+    const float inv = rsqrtf(warp_sum(ss) / (float)Dh + eps);
+#pragma unroll
+    for (int i = 0; i < DPL; i++) v[i] *= inv * nw[lane + 32 * i];
+  }
+#pragma unroll
+  for (int i = 0; i < DPL / 2; i++) {
+    const int j = lane + 32 * i;  // pairs (j, j + Dh/2)
+    const float freq = powf(theta, -2.0f * (float)j / (float)Dh);
+    float sn, cs;
+    sincosf((float)pos * freq, &sn, &cs);
+    const float a = v[i], b = v[i + DPL / 2];
+    out[i] = __half2float(__float2half_rn((a * cs - b * sn) * scale));
+    out[i + DPL / 2] = __half2float(__float2half_rn((b * cs + a * sn) * scale));
+  }
+}
+
+template <int DPL, bool ROPE>  // head dims per lane: Dh = 32 * DPL
 __global__ void __launch_bounds__(kAttnThreads)
-    attention_kernel(const __half *q, int rps, int H, int Hkv, const __half *k_cache, const __half *v_cache,
-                     int cache_len, const int *pos0, __half *out) {
+    attention_kernel(const __half *q, int rps, int H, int Hkv, __half *k_cache, __half *v_cache, int cache_len,
+                     const int *pos0, __half *out, const RopeArgs ra) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
   pdl_wait();     // inputs come from the previous kernel
   constexpr int Dh = 32 * DPL;
@@ -251,8 +296,36 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int t0 = min(L, c * per), t1 = min(L, t0 + per);
 
   // queries of the group (already scaled by 1/sqrt(Dh))
-  const __half *qg = q + ((size_t)r * H + (size_t)hk * G) * Dh;
-  for (int i = tid; i < G * Dh; i += kAttnThreads) sq[i] = __half2float(qg[i]);
+  const int pnew = pos0[bseq] + (r - bseq * rps);  // this row's position (ROPE: its new key)
+  const bool owner = ROPE && t0 <= pnew && pnew < t1;  // this CTA's slice holds the new key
+  float knew[DPL], vnew[DPL];
+  if (ROPE) {
+    const float *row = ra.qkv + (size_t)r * (H + 2 * Hkv) * Dh;
+    for (int g = warp; g < G; g += kAttnWarps) {
+      float qv[DPL];
+      rope_head<DPL>(row + (size_t)(hk * G + g) * Dh, ra.q_norm, ra.eps, ra.theta, pnew, rsqrtf((float)Dh), lane,
+                     qv);
+#pragma unroll
+      for (int i = 0; i < DPL; i++) sq[g * Dh + lane + 32 * i] = qv[i];
+    }
+    if (pnew < 0 || pnew >= cache_len) {
+      if (c == 0 && tid == 0) raise_flag(ra.flags, kFlagBadArgument);
+    } else if (owner && warp == 0) {
+      rope_head<DPL>(row + (size_t)(H + hk) * Dh, ra.k_norm, ra.eps, ra.theta, pnew, 1.0f, lane, knew);
+      const float *vs = row + (size_t)(H + Hkv + hk) * Dh;
+      __half *kc = k_cache + (((size_t)bseq * Hkv + hk) * cache_len + pnew) * Dh;
+      __half *vc = v_cache + (((size_t)bseq * Hkv + hk) * cache_len + pnew) * Dh;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) {
+        vnew[i] = __half2float(__float2half_rn(vs[lane + 32 * i]));
+        kc[lane + 32 * i] = __float2half_rn(knew[i]);
+        vc[lane + 32 * i] = __float2half_rn(vnew[i]);
+      }
+    }
+  } else {
+    const __half *qg = q + ((size_t)r * H + (size_t)hk * G) * Dh;
+    for (int i = tid; i < G * Dh; i += kAttnThreads) sq[i] = __half2float(qg[i]);
+  }
   for (int g = tid; g < G; g += kAttnThreads) {
     sm[g] = -INFINITY;
     sl[g] = 0.0f;
@@ -271,6 +344,16 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     cp_async_wait_all();
     __syncthreads();
+    if (owner && tt <= pnew && pnew < tt + nt) {  // the new key's row: not in the cache when the tile was read
+      if (warp == 0) {
+#pragma unroll
+        for (int i = 0; i < DPL; i++) {
+          sk[(pnew - tt) * kstride + lane + 32 * i] = __float2half_rn(knew[i]);
+          sv[(pnew - tt) * Dh + lane + 32 * i] = __float2half_rn(vnew[i]);
+        }
+      }
+      __syncthreads();
+    }
     // scores: entry i = g * tile + t (a warp shares g: q reads broadcast)
     for (int i = tid; i < G * kAttnTile; i += kAttnThreads) {
       const int g = i / kAttnTile, t = i - g * kAttnTile;
@@ -915,13 +998,13 @@ cudaError_t launch_rope_kv(const float *qkv, int rows, int batch, int H, int Hkv
                   reinterpret_cast<__half *>(v_cache), cache_len, flags);
 }
 
-template <int DPL>
+template <int DPL, bool ROPE>
 cudaError_t launch_attention_t(const void *q, int rows, int rps, int H, int Hkv, const void *k_cache,
                                const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
-                               cudaStream_t s, bool pdl) {
+                               cudaStream_t s, bool pdl, const RopeArgs &ra) {
   const AttnSmem lay(32 * DPL, H / Hkv);
   const size_t smem = lay.total;
-  auto kern = attention_kernel<DPL>;
+  auto kern = attention_kernel<DPL, ROPE>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -952,8 +1035,9 @@ cudaError_t launch_attention_t(const void *q, int rows, int rps, int H, int Hkv,
   cfg.attrs = at;
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const __half *>(q), rps, H, Hkv,
-                            reinterpret_cast<const __half *>(k_cache), reinterpret_cast<const __half *>(v_cache),
-                            cache_len, pos0, reinterpret_cast<__half *>(out));
+                            reinterpret_cast<__half *>(const_cast<void *>(k_cache)),
+                            reinterpret_cast<__half *>(const_cast<void *>(v_cache)), cache_len, pos0,
+                            reinterpret_cast<__half *>(out), ra);
 }
 
 cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
@@ -961,15 +1045,39 @@ cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv,
                              cudaStream_t s, bool pdl) {
   if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
   const int rps = rows / batch;
+  const RopeArgs ra{};
   switch (Dh) {
     case 32:
-      return launch_attention_t<1>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
+      return launch_attention_t<1, false>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s,
+                                          pdl, ra);
     case 64:
-      return launch_attention_t<2>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
+      return launch_attention_t<2, false>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s,
+                                          pdl, ra);
     case 128:
-      return launch_attention_t<4>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
+      return launch_attention_t<4, false>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s,
+                                          pdl, ra);
     case 256:
-      return launch_attention_t<8>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s, pdl);
+      return launch_attention_t<8, false>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s,
+                                          pdl, ra);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_rope_attention(const float *qkv, int batch, int H, int Hkv, int Dh, const int *pos0, float theta,
+                                  const float *q_norm, const float *k_norm, float eps, void *k_cache, void *v_cache,
+                                  int cache_len, void *out, unsigned *flags, int num_sms, cudaStream_t s, bool pdl) {
+  if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
+  const RopeArgs ra{qkv, theta, q_norm, k_norm, eps, flags};
+  switch (Dh) {
+    case 64:
+      return launch_attention_t<2, true>(nullptr, batch, 1, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms,
+                                         s, pdl, ra);
+    case 128:
+      return launch_attention_t<4, true>(nullptr, batch, 1, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms,
+                                         s, pdl, ra);
+    case 256:
+      return launch_attention_t<8, true>(nullptr, batch, 1, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms,
+                                         s, pdl, ra);
     default: return cudaErrorInvalidValue;
   }
 }

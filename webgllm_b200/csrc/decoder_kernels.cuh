@@ -21,6 +21,10 @@ cudaError_t launch_rope_kv(const float *qkv, int rows, int batch, int H, int Hkv
 cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                              const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
                              cudaStream_t s, bool pdl);
+// Decode (one row per sequence): rope_kv + attention in one launch.
+cudaError_t launch_rope_attention(const float *qkv, int batch, int H, int Hkv, int Dh, const int *pos0, float theta,
+                                  const float *q_norm, const float *k_norm, float eps, void *k_cache, void *v_cache,
+                                  int cache_len, void *out, unsigned *flags, int num_sms, cudaStream_t s, bool pdl);
 cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s, bool pdl);
 cudaError_t launch_swiglu_pairs(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s,
                                 bool pdl);
