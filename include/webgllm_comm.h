@@ -9,9 +9,10 @@
  * produces a partial [M][N] that must be summed across ranks). NCCL's
  * all-reduce does the same in a separate launch; here the matmul's own
  * epilogue stores its partial into every rank's exchange buffer (P2P
- * stores) and its last CTA raises a per-rank flag (system-scope release);
- * wg_comm_reduce waits for the flags (at most ~2 s, then WG_TIMEOUT from
- * wg_sync) and sums the partials from local memory.
+ * stores of 64-bit words, each carrying its value and the exchange's
+ * sequence number, so no flag or fence orders them); wg_comm_reduce polls
+ * its local buffer until every word carries the expected sequence number
+ * (at most ~2 s, then WG_TIMEOUT from wg_sync) and sums the partials.
  *
  * Setup, per rank (one process per GPU): wg_ipc_alloc a buffer, exchange
  * the 64-byte handles (e.g. an all-gather over torch.distributed),

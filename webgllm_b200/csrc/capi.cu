@@ -559,6 +559,28 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
   return WG_OK;
 }
 
+// The device form of a caller's prologue, checked: a known kind, its inputs
+// present and 16-byte aligned, resid_out aliasing neither input.
+int to_prologue(wg_ctx *ctx, const wg_prologue *pro, const char *who, wg::Prologue *p) {
+  *p = wg::Prologue{};
+  p->kind = pro->kind;
+  p->a = pro->a;
+  p->b = pro->b;
+  p->w = pro->weight;
+  p->eps = pro->eps;
+  p->out = pro->resid_out;
+  if (p->kind != WG_PRO_RMSNORM && p->kind != WG_PRO_SWIGLU)
+    return fail(ctx, WG_INVALID_ARGUMENT, "%s: unknown prologue kind %d", who, p->kind);
+  if (!p->a || (p->kind == WG_PRO_RMSNORM && !p->w))
+    return fail(ctx, WG_INVALID_ARGUMENT, "%s: null prologue input", who);
+  if (!aligned16(p->a) || !aligned16(p->b) || !aligned16(p->w) || !aligned16(p->out))
+    return fail(ctx, WG_INVALID_ARGUMENT, "%s: prologue tensors must be 16-byte aligned", who);
+  if (p->out && (p->out == p->a || (p->b && p->out == p->b)))
+    return fail(ctx, WG_INVALID_ARGUMENT, "%s: resid_out must not alias the residual or the addend", who);
+  if (p->kind == WG_PRO_SWIGLU) p->b = nullptr, p->w = nullptr, p->out = nullptr;
+  return WG_OK;
+}
+
 int check_matmul(wg_ctx *ctx, const wg_q4mat *m, int M, const void *y, int y_dtype) {
   if (M < 0) return fail(ctx, WG_INVALID_ARGUMENT, "negative row count %d", M);
   if (!y && M) return fail(ctx, WG_INVALID_ARGUMENT, "null y");
@@ -599,20 +621,8 @@ int wg_q4_matmul_push(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, co
     return fail(ctx, WG_UNSUPPORTED, "%d x %d outputs exceed the exchange slot (%lld floats)", M, m->d.N,
                 (long long)comm->dev.slot);
   if (pro) {
-    wg::Prologue p{};
-    p.kind = pro->kind;
-    p.a = pro->a;
-    p.b = pro->b;
-    p.w = pro->weight;
-    p.eps = pro->eps;
-    p.out = pro->resid_out;
-    if (p.kind != WG_PRO_RMSNORM && p.kind != WG_PRO_SWIGLU)
-      return fail(ctx, WG_INVALID_ARGUMENT, "unknown prologue kind %d", p.kind);
-    if (!p.a || (p.kind == WG_PRO_RMSNORM && !p.w))
-      return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_push: null prologue input");
-    if (!aligned16(p.a) || !aligned16(p.b) || !aligned16(p.w) || !aligned16(p.out))
-      return fail(ctx, WG_INVALID_ARGUMENT, "prologue tensors must be 16-byte aligned");
-    if (p.kind == WG_PRO_SWIGLU) p.b = nullptr, p.w = nullptr, p.out = nullptr;
+    wg::Prologue p;
+    if (int st = to_prologue(ctx, pro, "wg_q4_matmul_push", &p)) return st;
     return run_matmul(ctx, m, nullptr, WG_F16, M, nullptr, WG_F32, &p, comm);
   }
   if (!x || !aligned16(x)) return fail(ctx, WG_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer");
@@ -630,22 +640,8 @@ int wg_q4_matmul_ex(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, cons
     return fail(ctx, WG_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   const int epi = epilogue == WG_EPI_SWIGLU_PAIRS ? wg::kEpiSwigluPairs : wg::kEpiNone;
   if (pro) {
-    wg::Prologue p{};
-    p.kind = pro->kind;
-    p.a = pro->a;
-    p.b = pro->b;
-    p.w = pro->weight;
-    p.eps = pro->eps;
-    p.out = pro->resid_out;
-    if (p.kind != WG_PRO_RMSNORM && p.kind != WG_PRO_SWIGLU)
-      return fail(ctx, WG_INVALID_ARGUMENT, "unknown prologue kind %d", p.kind);
-    if (!p.a || (p.kind == WG_PRO_RMSNORM && !p.w))
-      return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_ex: null prologue input");
-    if (!aligned16(p.a) || !aligned16(p.b) || !aligned16(p.w) || !aligned16(p.out))
-      return fail(ctx, WG_INVALID_ARGUMENT, "prologue tensors must be 16-byte aligned");
-    if (p.out && (p.out == p.a || (p.b && p.out == p.b)))
-      return fail(ctx, WG_INVALID_ARGUMENT, "resid_out must not alias the residual or the addend");
-    if (p.kind == WG_PRO_SWIGLU) p.b = nullptr, p.w = nullptr, p.out = nullptr;
+    wg::Prologue p;
+    if ((st = to_prologue(ctx, pro, "wg_q4_matmul_ex", &p))) return st;
     return run_matmul(ctx, m, nullptr, WG_F16, M, y, y_dtype, &p, nullptr, epi);
   }
   if (!x || !aligned16(x)) return fail(ctx, WG_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer");
@@ -658,22 +654,8 @@ int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, i
   int st = check_matmul(ctx, m, M, y, y_dtype);
   if (st) return st;
   if (M == 0) return WG_OK;
-  wg::Prologue p{};
-  p.kind = pro->kind;
-  p.a = pro->a;
-  p.b = pro->b;
-  p.w = pro->weight;
-  p.eps = pro->eps;
-  p.out = pro->resid_out;
-  if (p.kind != WG_PRO_RMSNORM && p.kind != WG_PRO_SWIGLU)
-    return fail(ctx, WG_INVALID_ARGUMENT, "unknown prologue kind %d", p.kind);
-  if (!p.a || (p.kind == WG_PRO_RMSNORM && !p.w))
-    return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_fused: null prologue input");
-  if (!aligned16(p.a) || !aligned16(p.b) || !aligned16(p.w) || !aligned16(p.out))
-    return fail(ctx, WG_INVALID_ARGUMENT, "prologue tensors must be 16-byte aligned");
-  if (p.out && (p.out == p.a || (p.b && p.out == p.b)))
-    return fail(ctx, WG_INVALID_ARGUMENT, "resid_out must not alias the residual or the addend");
-  if (p.kind == WG_PRO_SWIGLU) p.b = nullptr, p.w = nullptr, p.out = nullptr;
+  wg::Prologue p;
+  if ((st = to_prologue(ctx, pro, "wg_q4_matmul_fused", &p))) return st;
   return run_matmul(ctx, m, nullptr, WG_F16, M, y, y_dtype, &p);
 }
 
