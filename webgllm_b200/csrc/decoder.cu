@@ -127,37 +127,58 @@ __global__ void rope_kv_kernel(const float *qkv, int rps, int H, int Hkv, int Dh
 }
 
 // ---- causal GQA attention (scores / attend kernels.ts:2386-2579) -----------
-// Split-K ("flash decoding") over a thread-block cluster: a cluster of CL
-// CTAs (CL = 8 when few (row, KV head) pairs share the GPU, down to 1 for
-// large batches or prompts, so the grid stays about one wave) serves one
-// (query row, KV head) pair and every query head of its group; CTA c takes
-// the c-th slice of the row's keys 0..pos.
-// Per slice, tiles of 128 keys (64 for Dh = 256) of K and V are staged in shared memory with
-// cp.async (all copies in flight at once; K rows padded by 16 bytes so that
-// row-strided reads hit distinct banks). Scores: one thread per (head, key).
-// An online softmax keeps (max, sum, acc) per head. P.V: warp w takes the
-// w-th quarter of the tile's keys, lane l the head dims l*DPL .. +DPL-1,
-// and each V element it loads serves four heads at once; the warps' sums
-// meet in shared memory. The slices are merged through distributed shared
-// memory: CTA c finishes outputs c*128 + i (mod 8*128) of the group's
-// G * Dh. No global scratch: one launch per step and nothing to allocate.
+// A (query row, KV head) pair is served by HS x CL CTAs: its G query heads
+// split over HS CTAs (each owns whole softmax rows), and, for caches longer
+// than kAttnSliceKeys positions, its keys 0..pos split over a thread-block
+// cluster of CL CTAs ("flash decoding"; CTA c takes the c-th slice). CL,
+// then HS, are as large as keeps the grid within about one wave.
+// Per slice, tiles of 128 keys (64 for Dh = 256) of K and V are staged in
+// shared memory with cp.async (all copies in flight at once; the first
+// tile's while the queries are made; K rows padded by 16 bytes so that
+// row-strided reads hit distinct banks). Scores: the tile's (head, key)
+// pairs spread over all threads. An online softmax keeps (max, sum, acc)
+// per head. P.V: warp w takes the w-th quarter of the tile's keys, lane l the
+// head dims l*DPL .. +DPL-1, and each V element it loads serves four heads
+// at once; the warps' sums meet in shared memory. The key slices are merged
+// at the cluster's leader: every CTA pushes (max, sum, acc) into the
+// leader's shared memory (distributed shared memory stores), one cluster
+// barrier, and the leader writes the outputs. No global scratch: one launch
+// per step and nothing to allocate.
 
 constexpr int kAttnCluster = 8;  // largest cluster
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxGroup = 16;
 constexpr int kAttnHeadChunk = 4;
+constexpr int kAttnSliceKeys = 128;  // cache positions per CTA before the keys are split over a cluster
 
 // Keys per tile: 128 (one tile covers a decode step's slice up to 1024
 // positions) while shared memory allows, 64 for Dh = 256.
 __host__ __device__ constexpr int attn_tile(int Dh) { return Dh <= 128 ? 128 : 64; }
 
+// Shared memory of one attention CTA. q, corr, m, l and acc live for the
+// whole kernel; k, v, p and red are per-tile scratch. gather receives the
+// cluster's (m, l, acc) slices at the leader: its own slots when they fit
+// (the CTAs push without a first barrier), else overlaid on the scratch
+// (alias: one more cluster barrier, so that no push lands on a tile still in
+// use).
+constexpr size_t kAttnGatherBudget = 200 * 1024;
 struct AttnSmem {
-  size_t q, k, v, p, corr, m, l, acc, red, total;  // byte offsets
+  size_t q, corr, m, l, acc, k, v, p, red, gather, total;  // byte offsets
+  bool alias;
   __host__ __device__ AttnSmem(int Dh, int G) {
     const int kAttnTile = attn_tile(Dh);
+    const size_t gpad = ((size_t)G * 4 + 15) / 16 * 16;  // every region 16-byte aligned
     size_t o = 0;
     q = o;
+    o += (size_t)G * Dh * 4;
+    corr = o;
+    o += gpad;
+    m = o;
+    o += gpad;
+    l = o;
+    o += gpad;
+    acc = o;
     o += (size_t)G * Dh * 4;
     k = o;
     o += (size_t)kAttnTile * (Dh + 8) * 2;
@@ -165,17 +186,12 @@ struct AttnSmem {
     o += (size_t)kAttnTile * Dh * 2;
     p = o;
     o += (size_t)G * kAttnTile * 4;
-    corr = o;
-    o += (size_t)G * 4;
-    m = o;
-    o += (size_t)G * 4;
-    l = o;
-    o += (size_t)G * 4;
-    acc = o;
-    o += (size_t)G * Dh * 4;
     red = o;
     o += (size_t)kAttnWarps * G * Dh * 4;
-    total = o;
+    const size_t gbytes = (size_t)kAttnCluster * (2 * G + G * Dh) * 4;
+    alias = o + gbytes > kAttnGatherBudget;
+    gather = alias ? k : o;
+    total = alias ? (k + gbytes > o ? k + gbytes : o) : o + gbytes;
   }
 };
 
@@ -233,9 +249,23 @@ struct RopeArgs {
 // RMS norm over Dh, rotate-half RoPE at position pos, scale; lane l holds
 // dims l + 32 i (i < DPL), so the rotate-half pairs (i, i + DPL/2) sit in
 // one lane. Values are rounded to fp16 as the separate kernel stores them.
+// The rotation of the lane's pairs at one position: cs / sn of
+// pos * theta^(-2j / Dh), j = lane + 32 i (computed once per thread: every
+// head of the row shares it).
 template <int DPL>
-__device__ __forceinline__ void rope_head(const float *src, const float *nw, float eps, float theta, int pos,
-                                          float scale, int lane, float out[DPL]) {
+__device__ __forceinline__ void rope_angles(float theta, int pos, int lane, float *cs, float *sn) {
+  constexpr int Dh = 32 * DPL;
+#pragma unroll
+  for (int i = 0; i < DPL / 2; i++) {
+    const int j = lane + 32 * i;
+    const float freq = powf(theta, -2.0f * (float)j / (float)Dh);
+    sincosf((float)pos * freq, &sn[i], &cs[i]);
+  }
+}
+
+template <int DPL>
+__device__ __forceinline__ void rope_head(const float *src, const float *nw, float eps, const float *cs,
+                                          const float *sn, float scale, int lane, float out[DPL]) {
   constexpr int Dh = 32 * DPL;
   float v[DPL];
   float ss = 0.0f;
@@ -250,14 +280,10 @@ __device__ __forceinline__ void rope_head(const float *src, const float *nw, flo
     for (int i = 0; i < DPL; i++) v[i] *= inv * nw[lane + 32 * i];
   }
 #pragma unroll
-  for (int i = 0; i < DPL / 2; i++) {
-    const int j = lane + 32 * i;  // pairs (j, j + Dh/2)
-    const float freq = powf(theta, -2.0f * (float)j / (float)Dh);
-    float sn, cs;
-    sincosf((float)pos * freq, &sn, &cs);
+  for (int i = 0; i < DPL / 2; i++) {  // pairs (j, j + Dh/2), j = lane + 32 i
     const float a = v[i], b = v[i + DPL / 2];
-    out[i] = __half2float(__float2half_rn((a * cs - b * sn) * scale));
-    out[i + DPL / 2] = __half2float(__float2half_rn((b * cs + a * sn) * scale));
+    out[i] = __half2float(__float2half_rn((a * cs[i] - b * sn[i]) * scale));
+    out[i + DPL / 2] = __half2float(__float2half_rn((b * cs[i] + a * sn[i]) * scale));
   }
 }
 
@@ -266,15 +292,35 @@ __global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const __half *q, int rps, int H, int Hkv, __half *k_cache, __half *v_cache, int cache_len,
                      const int *pos0, __half *out, const RopeArgs ra) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  // While the previous kernel finishes: an L2 prefetch of this CTA's slice
+  // of the caches (rows written by earlier steps; a prefetch is only a hint
+  // and L2 is where writes land, so a position read early or a row still
+  // being written cannot make anything stale).
+  if (threadIdx.x == 0) {
+    const int r = blockIdx.z, bq = r / rps, CLx = (int)gridDim.x;
+    const int Lg = max(0, min(pos0[bq] + (r - bq * rps) + 1, cache_len));
+    const int pg = (Lg + CLx - 1) / CLx;
+    const int a0 = min(Lg, (int)blockIdx.x * pg), a1 = min(Lg, a0 + pg);
+    if (a1 > a0) {
+      const int Dh = 32 * DPL, hkx = blockIdx.y / (gridDim.y / Hkv);
+      const size_t row0 = ((size_t)bq * Hkv + hkx) * cache_len + a0;
+      prefetch_l2(k_cache + row0 * Dh, (uint32_t)(a1 - a0) * Dh * 2);
+      prefetch_l2(v_cache + row0 * Dh, (uint32_t)(a1 - a0) * Dh * 2);
+    }
+  }
   pdl_wait();     // inputs come from the previous kernel
   constexpr int Dh = 32 * DPL;
+  constexpr int kHalfDpl = DPL / 2 > 0 ? DPL / 2 : 1;  // rotate-half pairs per lane (ROPE: DPL >= 2)
   constexpr int kAttnTile = attn_tile(Dh);
   constexpr int kPerLane = kAttnTile / 32;  // scores per lane in the softmax
   constexpr int vecs = Dh / 8;  // 16-byte vectors per key row
   constexpr int kstride = Dh + 8;
   extern __shared__ __align__(16) unsigned char smem[];
   cg::cluster_group cluster = cg::this_cluster();
-  const int G = H / Hkv;
+  // grid: x the cluster's key slices, y KV head x HS head groups, z rows
+  const int HS = gridDim.y / Hkv;
+  const int G = H / Hkv / HS;        // query heads of this CTA
+  const int qh0 = blockIdx.y * G;    // its first query head
   const AttnSmem lay(Dh, G);
   float *sq = reinterpret_cast<float *>(smem + lay.q);
   __half *sk = reinterpret_cast<__half *>(smem + lay.k);
@@ -285,45 +331,62 @@ __global__ void __launch_bounds__(kAttnThreads)
   float *sl = reinterpret_cast<float *>(smem + lay.l);
   float *sacc = reinterpret_cast<float *>(smem + lay.acc);
   float *sred = reinterpret_cast<float *>(smem + lay.red);
+  float *sgather = reinterpret_cast<float *>(smem + lay.gather);
 
   const int c = (int)cluster.block_rank();
   const int CL = (int)cluster.num_blocks();
-  const int hk = blockIdx.y, r = blockIdx.z;
+  const int hk = blockIdx.y / HS, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bseq = r / rps;  // sequence of this query row (rps rows per sequence)
   const int L = max(0, min(pos0[bseq] + (r - bseq * rps) + 1, cache_len));
   const int per = (L + CL - 1) / CL;
   const int t0 = min(L, c * per), t1 = min(L, t0 + per);
 
+  const __half *kb = k_cache + ((size_t)bseq * Hkv + hk) * cache_len * Dh;
+  const __half *vb = v_cache + ((size_t)bseq * Hkv + hk) * cache_len * Dh;
+  auto issue_tile = [&](int tt, int nt) {  // every copy of the tile in flight at once
+    for (int i = tid; i < nt * vecs; i += kAttnThreads) {
+      const int t = i / vecs, e = i - t * vecs;
+      cp_async16(sk + t * kstride + e * 8, kb + (size_t)(tt + t) * Dh + e * 8);
+      cp_async16(sv + t * Dh + e * 8, vb + (size_t)(tt + t) * Dh + e * 8);
+    }
+  };
+  // the first tile's keys and values load while the queries are made
+  if (t0 < t1) issue_tile(t0, min(kAttnTile, t1 - t0));
+
   // queries of the group (already scaled by 1/sqrt(Dh))
   const int pnew = pos0[bseq] + (r - bseq * rps);  // this row's position (ROPE: its new key)
   const bool owner = ROPE && t0 <= pnew && pnew < t1;  // this CTA's slice holds the new key
   float knew[DPL], vnew[DPL];
-  if (ROPE) {
+  if constexpr (ROPE) {
     const float *row = ra.qkv + (size_t)r * (H + 2 * Hkv) * Dh;
+    float cs[kHalfDpl], sn[kHalfDpl];
+    rope_angles<DPL>(ra.theta, pnew, lane, cs, sn);
     for (int g = warp; g < G; g += kAttnWarps) {
       float qv[DPL];
-      rope_head<DPL>(row + (size_t)(hk * G + g) * Dh, ra.q_norm, ra.eps, ra.theta, pnew, rsqrtf((float)Dh), lane,
-                     qv);
+      rope_head<DPL>(row + (size_t)(qh0 + g) * Dh, ra.q_norm, ra.eps, cs, sn, rsqrtf((float)Dh), lane, qv);
 #pragma unroll
       for (int i = 0; i < DPL; i++) sq[g * Dh + lane + 32 * i] = qv[i];
     }
     if (pnew < 0 || pnew >= cache_len) {
       if (c == 0 && tid == 0) raise_flag(ra.flags, kFlagBadArgument);
     } else if (owner && warp == 0) {
-      rope_head<DPL>(row + (size_t)(H + hk) * Dh, ra.k_norm, ra.eps, ra.theta, pnew, 1.0f, lane, knew);
+      rope_head<DPL>(row + (size_t)(H + hk) * Dh, ra.k_norm, ra.eps, cs, sn, 1.0f, lane, knew);
       const float *vs = row + (size_t)(H + Hkv + hk) * Dh;
       __half *kc = k_cache + (((size_t)bseq * Hkv + hk) * cache_len + pnew) * Dh;
       __half *vc = v_cache + (((size_t)bseq * Hkv + hk) * cache_len + pnew) * Dh;
+      const bool writer = blockIdx.y % HS == 0;  // one head group appends to the caches
 #pragma unroll
       for (int i = 0; i < DPL; i++) {
         vnew[i] = __half2float(__float2half_rn(vs[lane + 32 * i]));
-        kc[lane + 32 * i] = __float2half_rn(knew[i]);
-        vc[lane + 32 * i] = __float2half_rn(vnew[i]);
+        if (writer) {
+          kc[lane + 32 * i] = __float2half_rn(knew[i]);
+          vc[lane + 32 * i] = __float2half_rn(vnew[i]);
+        }
       }
     }
   } else {
-    const __half *qg = q + ((size_t)r * H + (size_t)hk * G) * Dh;
+    const __half *qg = q + ((size_t)r * H + qh0) * Dh;
     for (int i = tid; i < G * Dh; i += kAttnThreads) sq[i] = __half2float(qg[i]);
   }
   for (int g = tid; g < G; g += kAttnThreads) {
@@ -332,15 +395,11 @@ __global__ void __launch_bounds__(kAttnThreads)
   }
   for (int i = tid; i < G * Dh; i += kAttnThreads) sacc[i] = 0.0f;
 
-  const __half *kb = k_cache + ((size_t)bseq * Hkv + hk) * cache_len * Dh;
-  const __half *vb = v_cache + ((size_t)bseq * Hkv + hk) * cache_len * Dh;
   for (int tt = t0; tt < t1; tt += kAttnTile) {
     const int nt = min(kAttnTile, t1 - tt);
-    __syncthreads();  // previous tile fully consumed
-    for (int i = tid; i < nt * vecs; i += kAttnThreads) {  // every copy in flight at once
-      const int t = i / vecs, e = i - t * vecs;
-      cp_async16(sk + t * kstride + e * 8, kb + (size_t)(tt + t) * Dh + e * 8);
-      cp_async16(sv + t * Dh + e * 8, vb + (size_t)(tt + t) * Dh + e * 8);
+    if (tt != t0) {
+      __syncthreads();  // previous tile fully consumed
+      issue_tile(tt, nt);
     }
     cp_async_wait_all();
     __syncthreads();
@@ -354,23 +413,26 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
       __syncthreads();
     }
-    // scores: entry i = g * tile + t (a warp shares g: q reads broadcast)
-    for (int i = tid; i < G * kAttnTile; i += kAttnThreads) {
-      const int g = i / kAttnTile, t = i - g * kAttnTile;
-      float sc = -INFINITY;
-      if (t < nt) {
-        const uint4 *kr = reinterpret_cast<const uint4 *>(sk + t * kstride);
-        const float *qr = sq + g * Dh;
-        float a0 = 0.0f, a1 = 0.0f;
+    // scores of the tile's nt keys for the G heads, spread over all threads
+    // (consecutive threads take consecutive keys of one head: q reads
+    // broadcast), stored at sp[g * tile + t]; slots t >= nt hold -inf
+    for (int i = tid; i < G * nt; i += kAttnThreads) {
+      const int g = i / nt, t = i - g * nt;
+      const uint4 *kr = reinterpret_cast<const uint4 *>(sk + t * kstride);
+      const float *qr = sq + g * Dh;
+      float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-        for (int e = 0; e < vecs; e += 2) {
-          a0 += dot8(kr[e], qr + e * 8);
-          if (e + 1 < vecs) a1 += dot8(kr[e + 1], qr + e * 8 + 8);
-        }
-        sc = a0 + a1;
+      for (int e = 0; e < vecs; e += 2) {
+        a0 += dot8(kr[e], qr + e * 8);
+        if (e + 1 < vecs) a1 += dot8(kr[e + 1], qr + e * 8 + 8);
       }
-      sp[i] = sc;
+      sp[g * kAttnTile + t] = a0 + a1;
     }
+    if (nt < kAttnTile)
+      for (int i = tid; i < G * (kAttnTile - nt); i += kAttnThreads) {
+        const int g = i / (kAttnTile - nt);
+        sp[g * kAttnTile + nt + (i - g * (kAttnTile - nt))] = -INFINITY;
+      }
     __syncthreads();
     // per head: new max, rescale factor, probabilities (one warp per head)
     for (int g = warp; g < G; g += kAttnWarps) {
@@ -400,10 +462,12 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
     }
     __syncthreads();
-    // P.V for this warp's quarter of the keys, four heads per pass over V
+    // P.V for this warp's quarter of the tile's keys, four heads per pass
+    // over V
     {
-      const int kw0 = warp * (kAttnTile / kAttnWarps);
-      const int kw1 = min(nt, kw0 + kAttnTile / kAttnWarps);
+      const int kper = (nt + kAttnWarps - 1) / kAttnWarps;
+      const int kw0 = warp * kper;
+      const int kw1 = min(nt, kw0 + kper);
       for (int g0 = 0; g0 < G; g0 += kAttnHeadChunk) {
         float a[kAttnHeadChunk][DPL];
 #pragma unroll
@@ -437,31 +501,48 @@ __global__ void __launch_bounds__(kAttnThreads)
       sacc[i] = sacc[i] * scorr[g] + s;
     }
   }
-  cluster.sync();
-  // merge the slices: this CTA finishes outputs c * 128 + tid, + CL * 128, ...
-  for (int i = c * kAttnThreads + tid; i < G * Dh; i += CL * kAttnThreads) {
-    const int g = i / Dh;
-    float mj[kAttnCluster];
-    float M = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kAttnCluster; j++) {
-      if (j >= CL) break;
-      mj[j] = cluster.map_shared_rank(sm, j)[g];
-      M = fmaxf(M, mj[j]);
+  // merge the slices at the leader (rank 0): every CTA with keys pushes its
+  // (m, l, acc) into the leader's gather slots (stores to distributed shared
+  // memory: no round trip), one cluster barrier, and the leader combines them
+  // from its own shared memory while the others exit.
+  if (lay.alias) cluster.sync();  // the gather overlays tiles a peer may still read
+  if (t0 < t1) {
+    float *gl = cluster.map_shared_rank(sgather, 0);
+    for (int g = tid; g < G; g += kAttnThreads) {
+      gl[c * G + g] = sm[g];
+      gl[(kAttnCluster + c) * G + g] = sl[g];
     }
-    float lsum = 0.0f, a = 0.0f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int j = 0; j < kAttnCluster; j++) {
-        if (j >= CL) break;
-        const float w = mj[j] == -INFINITY ? 0.0f : expf(mj[j] - M);
-        lsum += cluster.map_shared_rank(sl, j)[g] * w;
-        a += cluster.map_shared_rank(sacc, j)[i] * w;
-      }
-    }
-    out[((size_t)r * H + (size_t)hk * G) * Dh + i] = __float2half_rn(lsum > 0.0f ? a / lsum : 0.0f);
+    float *ga = gl + 2 * kAttnCluster * G + (size_t)c * G * Dh;
+    for (int i = tid; i < G * Dh / 4; i += kAttnThreads)
+      reinterpret_cast<float4 *>(ga)[i] = reinterpret_cast<const float4 *>(sacc)[i];
   }
-  cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+  cluster.sync();
+  if (c != 0) return;  // nothing reads this CTA's shared memory any more
+  // weights of each slice per head: w[j][g] = exp(m_j - M) / sum_j' l_j' exp(m_j' - M)
+  // (slices without keys carry none; sred is free scratch now unless the
+  // gather overlays it: then the corr slots hold the per-head sums)
+  const int nslices = min(CL, (L + per - 1) / max(per, 1));  // slices holding keys
+  float *wts = sp;  // G * kAttnCluster floats of the probability tile (free now)
+  if (lay.alias) wts = reinterpret_cast<float *>(smem + lay.q);  // q is free too
+  for (int g = tid; g < G; g += kAttnThreads) {
+    float M = -INFINITY;
+    for (int j = 0; j < nslices; j++) M = fmaxf(M, sgather[j * G + g]);
+    float lsum = 0.0f;
+    for (int j = 0; j < nslices; j++) {
+      const float w = M == -INFINITY ? 0.0f : expf(sgather[j * G + g] - M);
+      wts[j * G + g] = w;
+      lsum += sgather[(kAttnCluster + j) * G + g] * w;
+    }
+    scorr[g] = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+  }
+  __syncthreads();
+  const float *gacc = sgather + 2 * kAttnCluster * G;
+  for (int i = tid; i < G * Dh; i += kAttnThreads) {
+    const int g = i / Dh;
+    float a = 0.0f;
+    for (int j = 0; j < nslices; j++) a += gacc[(size_t)j * G * Dh + i] * wts[j * G + g];
+    out[((size_t)r * H + qh0) * Dh + i] = __float2half_rn(a * scorr[g]);
+  }
 }
 
 // ---- SwiGLU (REDUCE_SWIGLU kernels.ts:1066-1077) ---------------------------
@@ -1002,21 +1083,33 @@ template <int DPL, bool ROPE>
 cudaError_t launch_attention_t(const void *q, int rows, int rps, int H, int Hkv, const void *k_cache,
                                const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
                                cudaStream_t s, bool pdl, const RopeArgs &ra) {
-  const AttnSmem lay(32 * DPL, H / Hkv);
+  // Work split of each (row, KV head) pair, within about one wave of CTAs:
+  // first its keys over a cluster of CL CTAs, until a slice of the cache is
+  // at most kAttnSliceKeys positions (the split that divides each CTA's K / V
+  // bytes; slices merged through distributed shared memory), then its G
+  // query heads over HS CTAs with the CTAs left (each owns whole softmax
+  // rows: nothing more to merge, the K / V tile is read again from L2).
+  const int G = H / Hkv;
+  const long long pairs = (long long)rows * Hkv;
+  auto per_sm = [](size_t smem) { return smem <= 100 * 1024 ? 2 : 1; };
+  const long long wave = (long long)num_sms * per_sm(AttnSmem(32 * DPL, G).total);
+  int CL = 1;
+  while (CL < kAttnCluster && (long long)CL * kAttnSliceKeys < cache_len && pairs * CL * 2 <= wave) CL *= 2;
+  int HS = 1;
+  for (int hs = G; hs > 1; hs--)
+    if (G % hs == 0 && pairs * CL * hs <= (long long)num_sms * per_sm(AttnSmem(32 * DPL, G / hs).total)) {
+      HS = hs;
+      break;
+    }
+  const AttnSmem lay(32 * DPL, G / HS);
   const size_t smem = lay.total;
   auto kern = attention_kernel<DPL, ROPE>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  // cluster size: split each pair's keys over up to 8 CTAs while the grid
-  // stays within about one wave (CTAs per SM by shared memory)
-  const int per_sm = smem <= 100 * 1024 ? 2 : 1;
-  const long long pairs = (long long)rows * Hkv;
-  int CL = kAttnCluster;
-  while (CL > 1 && pairs * CL > (long long)num_sms * per_sm) CL /= 2;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)CL, (unsigned)Hkv, (unsigned)rows);
+  cfg.gridDim = dim3((unsigned)CL, (unsigned)(Hkv * HS), (unsigned)rows);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
