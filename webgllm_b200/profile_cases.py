@@ -64,14 +64,20 @@ def gemv(M: int, N: int, K: int, reps: int):
 
 
 def gemm(M: int, N: int, K: int, reps: int):
+    """The prefill GEMM over `copies` distinct matrices (rotating, > L2 when
+    the weights dominate the bytes)."""
     c = context()
-    m = _q4(N, K)
+    copies = max(1, min(8, (256 << 20) // (N * K * 18 // 32) + 1)) if M <= 256 else 1
+    mats = [_q4(N, K, i) for i in range(copies)]
     x = torch.randn((M, K), device="cuda").half()
     y = torch.empty((M, N), device="cuda", dtype=torch.float16)
     L = _lib.lib()
     c.use_torch_stream()
+    i = [0]
 
     def run():
+        m = mats[i[0] % copies]
+        i[0] += 1
         _lib.check(L.wg_q4_matmul(P(c.handle), P(m.handle), P(x.data_ptr()), _lib.WG_F16, M, P(y.data_ptr()),
                                   _lib.WG_F16), c.handle)
 
@@ -134,6 +140,8 @@ def decode(config: str, batch: int, reps: int):
 CASES = {
     "gemv_config1_m1": lambda r: gemv(1, 4096, 4096, r),
     "gemv_wide_m8": lambda r: gemv(8, 28672, 4096, r),
+    "gemm_m64": lambda r: gemm(64, 4096, 4096, r),
+    "gemm_m256": lambda r: gemm(256, 4096, 4096, r),
     "gemm_m1024": lambda r: gemm(1024, 4096, 4096, r),
     "gemm_m4096_down": lambda r: gemm(4096, 4096, 14336, r),
     "attention_config4_b8": lambda r: attention(8, 32, 8, 128, 640, r),
