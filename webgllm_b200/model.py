@@ -18,6 +18,7 @@ pick.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -51,6 +52,10 @@ class DecoderConfig:
             self.layer_types = ["attn"] * self.layers
         assert len(self.layer_types) == self.layers
 
+
+# Decode batches of up to this many sequences run RoPE + KV append inside the
+# attention launch (WG_FUSED_ROPE_MAX_ROWS overrides: tuning).
+_FUSED_ROPE_MAX_ROWS = int(os.environ.get("WG_FUSED_ROPE_MAX_ROWS", "4"))
 
 # Llama-style 1.1B.
 CONFIG2 = DecoderConfig("llama-1.1b", 22, 2048, 32, 4, 64, 5632, 32000, 1e-5, 1e4)
@@ -294,8 +299,8 @@ class DecoderModel:
         qn, kn = lay.get("q_norm"), lay.get("k_norm")
         # decode of a few sequences: one launch (measured: configs 2 / 3 gain
         # 3-5 %; at batch 8 every CTA's own query RoPE costs more than the
-        # launch it saves)
-        if rows == self.batch and rows <= 4 and Dh % 64 == 0:
+        # launch it saves: 3.24 vs 3.19 ms a config-4 step)
+        if rows == self.batch and rows <= _FUSED_ROPE_MAX_ROWS and Dh % 64 == 0:
             self._c(L.wg_rope_attention(c, P(self.qkv.data_ptr()), rows, H, Hkv, Dh, P(self.pos.data_ptr()), cfg.theta,
                                         P(qn.data_ptr() if qn is not None else None),
                                         P(kn.data_ptr() if kn is not None else None), cfg.eps, P(kc.data_ptr()),
