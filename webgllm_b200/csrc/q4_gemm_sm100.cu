@@ -775,9 +775,19 @@ size_t plan_gemm(GemmArgs &a, int num_sms) {
   // CTAs of one K range (the pair kernel runs one per SM, the 1-SM kernel two)
   const int tiles = pair ? 2 * ((a.NT + 15) / 16) * ((a.M + BM - 1) / BM)
                          : ((a.NT + 7) / 8) * ((a.M + BM - 1) / BM);
-  // Split K until the grid covers the SMs, keeping >= 4 stages per split.
+  // Split K while the grid fits two CTAs per SM (both resident at once: the
+  // shared-memory padding allows two), keeping >= 4 stages per split.
+  // Measured at 4096 x 4096: M = 64, 17 us with 9 splits vs 19 with 4-5;
+  // M = 256, 26 us with 4 splits vs 31 with 2. WG_GEMM_SPLITS overrides
+  // (tuning).
+  static int force = -1;
+  if (force < 0) {
+    const char *e = getenv("WG_GEMM_SPLITS");
+    force = e ? atoi(e) : 0;
+  }
   int splits = 1;
-  while (tiles * splits < num_sms && a.KT / (splits + 1) >= 4) splits++;
+  while (tiles * (splits + 1) <= 2 * num_sms && a.KT / (splits + 1) >= 4) splits++;
+  if (force > 0) splits = force < a.KT ? force : a.KT;
   a.kt_per_split = (a.KT + splits - 1) / splits;
   a.splits = (a.KT + a.kt_per_split - 1) / a.kt_per_split;
   return a.splits > 1 ? (size_t)a.splits * a.M * a.N * sizeof(float) : 0;
