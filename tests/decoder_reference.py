@@ -57,15 +57,15 @@ def attention(q, k_cache, v_cache, pos0, H, Hkv):
     row r attends keys 0..pos0+r. Returns fp32 [rows][H][Dh]."""
     rows, _, Dh = q.shape
     G = H // Hkv
+    L = pos0 + rows
     out = torch.zeros((rows, H, Dh), dtype=torch.float32, device=q.device)
-    for r in range(rows):
-        L = pos0 + r + 1
-        for h in range(H):
-            kk = k_cache[h // G, :L].float()
-            vv = v_cache[h // G, :L].float()
-            s = kk @ q[r, h].float()
-            p = torch.softmax(s, dim=0)
-            out[r, h] = p @ vv
+    keys = torch.arange(L, device=q.device)
+    masked = keys[None, :] > (pos0 + torch.arange(rows, device=q.device))[:, None]  # [rows][L]
+    for h in range(H):
+        kk = k_cache[h // G, :L].float()
+        vv = v_cache[h // G, :L].float()
+        s = (q[:, h].float() @ kk.T).masked_fill(masked, float("-inf"))
+        out[:, h] = torch.softmax(s, dim=1) @ vv
     return out
 
 

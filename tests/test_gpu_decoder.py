@@ -130,6 +130,8 @@ def test_rope_kv_position_past_cache_is_reported():
 @pytest.mark.parametrize("rows,H,Hkv,Dh,pos0", [
     (1, 32, 4, 64, 0), (1, 32, 4, 64, 1023), (1, 24, 8, 64, 300), (1, 32, 8, 128, 2047), (4, 16, 2, 64, 517),
     (40, 8, 8, 64, 0), (1, 16, 1, 256, 130), (2, 6, 2, 32, 70),
+    # prompts (>= 16 rows a sequence, Dh 64 / 128): the tensor-core flash kernel
+    (64, 32, 8, 128, 0), (100, 32, 8, 128, 37), (200, 16, 2, 64, 500), (17, 8, 1, 64, 3), (130, 24, 8, 64, 1800),
 ])
 def test_attention_causal_gqa(rows, H, Hkv, Dh, pos0):
     g = gen(rows * 7 + H * 3 + pos0)
@@ -149,6 +151,31 @@ def test_attention_causal_gqa(rows, H, Hkv, Dh, pos0):
     want = R.attention(q, kc, vc, pos0, H, Hkv)
     assert torch.isfinite(out.float()).all()
     assert (out.float() - want).abs().max().item() < 2e-3 * max(1.0, want.abs().max().item())
+
+
+@pytest.mark.parametrize("Dh,H,Hkv", [(128, 32, 8), (64, 32, 4)])
+def test_flash_prefill_batched_sequences(Dh, H, Hkv):
+    """Prompts of 3 sequences (70 rows each, at their own positions and
+    caches) through the flash kernel: each equals the single-sequence
+    reference."""
+    B, rps, cache_len = 3, 70, 512
+    g = gen(Dh + H)
+    pos0 = [0, 130, 400]
+    kc = torch.zeros((B, Hkv, cache_len, Dh), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    for b in range(B):
+        L = pos0[b] + rps
+        kc[b, :, :L] = (torch.randn((Hkv, L, Dh), generator=g, device="cuda") * 2).half()
+        vc[b, :, :L] = torch.randn((Hkv, L, Dh), generator=g, device="cuda").half()
+    q = (torch.randn((B * rps, H, Dh), generator=g, device="cuda") / math.sqrt(Dh)).half()
+    pos = torch.tensor(pos0, dtype=torch.int32, device="cuda")
+    out = torch.empty((B * rps, H, Dh), dtype=torch.float16, device="cuda")
+    call(lib().wg_attention, ptr(q), B * rps, B, H, Hkv, Dh, ptr(kc), ptr(vc), cache_len, ptr(pos), ptr(out))
+    for b in range(B):
+        want = R.attention(q[b * rps:(b + 1) * rps], kc[b], vc[b], pos0[b], H, Hkv)
+        got = out[b * rps:(b + 1) * rps].float()
+        assert torch.isfinite(got).all()
+        assert (got - want).abs().max().item() < 2e-3 * max(1.0, want.abs().max().item()), b
 
 
 def test_rope_and_attention_batched_sequences():

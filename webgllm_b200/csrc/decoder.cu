@@ -7,6 +7,8 @@
 // come from a device counter so that a decode step can be replayed from a
 // CUDA graph without re-recording.
 #include <cooperative_groups.h>
+
+#include <cstdlib>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -1138,6 +1140,9 @@ cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv,
                              cudaStream_t s, bool pdl) {
   if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
   const int rps = rows / batch;
+  static const bool no_flash = getenv("WG_NO_FLASH_PREFILL") != nullptr;  // the CUDA-core kernel (comparison)
+  if (flash_prefill_supported(rps, Dh) && !no_flash)
+    return launch_flash_prefill(q, rps, batch, H, Hkv, Dh, k_cache, v_cache, cache_len, pos0, out, s, pdl);
   const RopeArgs ra{};
   switch (Dh) {
     case 32:

@@ -21,6 +21,14 @@ cudaError_t launch_rope_kv(const float *qkv, int rows, int batch, int H, int Hkv
 cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                              const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
                              cudaStream_t s, bool pdl);
+// Prompts (attention_prefill.cu): flash attention on the tensor cores for
+// rows / batch >= kFaPrefillMinRows query rows per sequence and Dh 64 / 128;
+// launch_attention routes those shapes to it.
+constexpr int kFaPrefillMinRows = 16;
+bool flash_prefill_supported(int rps, int Dh);
+cudaError_t launch_flash_prefill(const void *q, int rps, int batch, int H, int Hkv, int Dh, const void *k_cache,
+                                 const void *v_cache, int cache_len, const int *pos0, void *out, cudaStream_t s,
+                                 bool pdl);
 // Decode (one row per sequence): rope_kv + attention in one launch.
 cudaError_t launch_rope_attention(const float *qkv, int batch, int H, int Hkv, int Dh, const int *pos0, float theta,
                                   const float *q_norm, const float *k_norm, float eps, void *k_cache, void *v_cache,
