@@ -107,6 +107,30 @@ def attention(batch: int, H: int, Hkv: int, Dh: int, ctx_len: int, reps: int):
     print(f"attention batch={batch} H={H} Hkv={Hkv} Dh={Dh} ctx={ctx_len}: {us:.2f} us, {kv / us / 1e3:.1f} GB/s KV")
 
 
+def prefill_attention(batch: int, rps: int, H: int, Hkv: int, Dh: int, reps: int):
+    """Causal attention of `batch` prompts of `rps` rows each (the flash
+    kernel for rps >= 16); reports tensor FLOP/s of the causal work."""
+    c = context()
+    cache = rps + 64
+    kc = torch.randn((batch, Hkv, cache, Dh), device="cuda").half()
+    vc = torch.randn_like(kc)
+    q = (torch.randn((batch * rps, H, Dh), device="cuda") / Dh ** 0.5).half()
+    o = torch.empty_like(q)
+    pos = torch.zeros((batch,), dtype=torch.int32, device="cuda")
+    L = _lib.lib()
+    c.use_torch_stream()
+
+    def run():
+        _lib.check(L.wg_attention(P(c.handle), P(q.data_ptr()), batch * rps, batch, H, Hkv, Dh, P(kc.data_ptr()),
+                                  P(vc.data_ptr()), cache, P(pos.data_ptr()), P(o.data_ptr())), c.handle)
+
+    run()
+    us = _time(run, reps)
+    flops = 4.0 * batch * H * Dh * rps * (rps + 1) / 2  # QK^T and PV over the causal triangle
+    print(f"prefill attention batch={batch} rows={rps} H={H} Hkv={Hkv} Dh={Dh}: {us:.2f} us, "
+          f"{flops / us / 1e6:.1f} TFLOP/s")
+
+
 def head(rows: int, D: int, V: int, reps: int):
     c = context()
     W = (torch.randn((V, D), device="cuda") * 0.02).half()
@@ -145,6 +169,7 @@ CASES = {
     "gemm_m1024": lambda r: gemm(1024, 4096, 4096, r),
     "gemm_m4096_down": lambda r: gemm(4096, 4096, 14336, r),
     "attention_config4_b8": lambda r: attention(8, 32, 8, 128, 640, r),
+    "attention_prefill_config4_b8": lambda r: prefill_attention(8, 512, 32, 8, 128, r),
     "attention_config2": lambda r: attention(1, 32, 4, 64, 256, r),
     "head_config2": lambda r: head(1, 2048, 32000, r),
     "head_config4_b8": lambda r: head(8, 4096, 128256, r),
