@@ -164,6 +164,7 @@ def decode(config: str, batch: int, reps: int):
 CASES = {
     "gemv_config1_m1": lambda r: gemv(1, 4096, 4096, r),
     "gemv_wide_m8": lambda r: gemv(8, 28672, 4096, r),
+    "gemv_m1_28672x4096": lambda r: gemv(1, 28672, 4096, r),
     "gemm_m64": lambda r: gemm(64, 4096, 4096, r),
     "gemm_m256": lambda r: gemm(256, 4096, 4096, r),
     "gemm_m1024": lambda r: gemm(1024, 4096, 4096, r),
