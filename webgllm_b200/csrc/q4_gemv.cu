@@ -301,33 +301,32 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
   }
   {
     // Up to 4 loads in flight per lane before any store (one L2 round trip
-    // for the usual M * 8 tiles <= 128 chunks).
+    // for the usual M * 8 tiles <= 128 chunks). Entry idx = m * 64 + c
+    // (token m, chunk c of 8 K values; a warp has at most 64 chunks), so
+    // that shifts, not divisions, split it.
+    static_assert(kMaxTilesPerWarp * (kTileK / 8) == 64, "64 chunks per warp at most");
     const int chunks = nw * (kTileK / 8);
     const int kbase = (kt0 + wt0) * kTileK;
-    for (int base = 0; base < M * chunks; base += 4 * 32) {
+    for (int base = 0; base < M * 64; base += 4 * 32) {
       uint4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const int idx = base + u * 32 + lane;
+        const int m = idx >> 6, c = idx & 63;
+        const int k = kbase + c * 8;
         v[u] = make_uint4(0, 0, 0, 0);
-        if (idx < M * chunks) {
-          const int m = idx / chunks, c = idx - m * chunks;
-          const int k = kbase + c * 8;
-          if (k < a.K) {
-            if constexpr (PRO == kProNone)
-              v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
-            else
-              v[u] = prologue_x8<PRO>(a.pro, a.K, m, k, PRO == kProRmsNorm ? s_inv[m] : 0.0f);
-          }
+        if (m < M && c < chunks && k < a.K) {
+          if constexpr (PRO == kProNone)
+            v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
+          else
+            v[u] = prologue_x8<PRO>(a.pro, a.K, m, k, PRO == kProRmsNorm ? s_inv[m] : 0.0f);
         }
       }
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const int idx = base + u * 32 + lane;
-        if (idx < M * chunks) {
-          const int m = idx / chunks, c = idx - m * chunks;
-          *reinterpret_cast<uint4 *>(xw + (size_t)m * stride + c * 8) = v[u];
-        }
+        const int m = idx >> 6, c = idx & 63;
+        if (m < M && c < chunks) *reinterpret_cast<uint4 *>(xw + (size_t)m * stride + c * 8) = v[u];
       }
     }
   }
@@ -611,32 +610,32 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
     }
     mbar_wait_bounded(xbar, 0, a.flags);
   } else {
+    // entry idx = m << sh | c (token m, chunk c of 8 K values, 2^sh >=
+    // chunks): shifts, not divisions, split it
     const int chunks = ktc * (kTileK / 8);
     const int kbase = kt0 * kTileK;
-    for (int base = 0; base < M * chunks; base += 4 * kWThreads) {
+    int sh = 0;
+    while ((1 << sh) < chunks) sh++;
+    for (int base = 0; base < (M << sh); base += 4 * kWThreads) {
       uint4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const int idx = base + u * kWThreads + threadIdx.x;
+        const int m = idx >> sh, c = idx & ((1 << sh) - 1);
+        const int k = kbase + c * 8;
         v[u] = make_uint4(0, 0, 0, 0);
-        if (idx < M * chunks) {
-          const int m = idx / chunks, c = idx - m * chunks;
-          const int k = kbase + c * 8;
-          if (k < a.K) {
-            if constexpr (PRO == kProNone)
-              v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
-            else
-              v[u] = prologue_x8<PRO>(a.pro, a.K, m, k, PRO == kProRmsNorm ? s_inv[m] : 0.0f);
-          }
+        if (m < M && c < chunks && k < a.K) {
+          if constexpr (PRO == kProNone)
+            v[u] = load_x8_f16(a.x, a.x_dtype, (size_t)m * a.K + k);
+          else
+            v[u] = prologue_x8<PRO>(a.pro, a.K, m, k, PRO == kProRmsNorm ? s_inv[m] : 0.0f);
         }
       }
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const int idx = base + u * kWThreads + threadIdx.x;
-        if (idx < M * chunks) {
-          const int m = idx / chunks, c = idx - m * chunks;
-          *reinterpret_cast<uint4 *>(xs + (size_t)m * L.xstride + c * 8) = v[u];
-        }
+        const int m = idx >> sh, c = idx & ((1 << sh) - 1);
+        if (m < M && c < chunks) *reinterpret_cast<uint4 *>(xs + (size_t)m * L.xstride + c * 8) = v[u];
       }
     }
   }
