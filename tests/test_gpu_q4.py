@@ -143,6 +143,20 @@ def test_gemv_shapes(N, K):
         check_close(y, O.c_ref_f64(blocks, x16, N, K), f"{N}x{K} M={M}")
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 14336),   # one stage: a column at a time
+                                   (8, 28672, 4096),   # three stages, ~12 columns a CTA
+                                   (8, 6144, 4096), (4, 4096, 4096), (2, 20480, 2048),
+                                   (3, 2560, 8192), (8, 4096, 14336)])  # the last: K split over a cluster
+def test_wide_gemv_many_columns(M, N, K):
+    # shapes where the wide GEMV's CTAs walk several tile columns through
+    # their shared-memory stages (the two warp groups alternate columns)
+    blocks, m, host = make(N, K, M * 7 + N)
+    y, x16 = run(m, O.config_activations(M, K, 5))
+    check_close(y, O.c_ref_f64(blocks, x16, N, K), f"{M}x{N}x{K} vs fp64")
+    if N * K <= 4096 * 4096:
+        check_close(y, O.c_split_emulate(host, x16), f"{M}x{N}x{K} vs emulation")
+
+
 @pytest.mark.parametrize("xd", ["float32", "float16", "bfloat16"])
 @pytest.mark.parametrize("yd", ["float32", "float16", "bfloat16"])
 def test_gemv_dtypes(xd, yd):

@@ -146,6 +146,12 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
   }
 }
 
+// Barrier `id` (1..15) over the `threads` threads (a multiple of 32) of the
+// warps that reach it.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ float warp_sum_f(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -514,6 +520,9 @@ __global__ void __launch_bounds__(kThreads) prologue_kernel(const Prologue p, in
 constexpr int kWideXBudget = 96 * 1024;   // x slice per CTA
 constexpr int kWideMaxTokens = 32;        // rows (4 token groups of 8)
 constexpr int kWideSmemMax = 200 * 1024;
+// The two-group column walk (gemv_wide_kernel) wants an even stage count:
+// it may use up to this much (the attribute is set to it for every launch).
+constexpr int kWideSmemMaxGroups = 224 * 1024;
 constexpr int kWWarps = 16;                // warps of a wide CTA (one CTA per SM)
 constexpr int kWThreads = kWWarps * 32;
 
@@ -564,8 +573,9 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
   const unsigned parity = a.push_on ? push_seq(a.push) : 0u;  // the exchange's sequence number
 
-  auto issue = [&](int j) {  // thread 0: column g + j*G (this CTA's K range) into stage j % S
-    const int st = j % S;
+  // column g + j*G (this CTA's K range) into stage st (j % S, or the warp
+  // groups' own rings: the first S columns land in stage j either way)
+  auto issue_to = [&](int j, int st) {
     uint8_t *dst = stages + st * L.stage_bytes;
     const size_t tile = (size_t)(g + j * G) * a.KT + kt0;
     mbar_expect_tx(&bars[st], nib_b + scl_b + (ZEROS ? ktc * kTileZroBytes : 0));
@@ -573,6 +583,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
     bulk_g2s(dst + nib_b, reinterpret_cast<const uint8_t *>(a.scl) + tile * kTileSclBytes, scl_b, &bars[st]);
     if (ZEROS) bulk_g2s(dst + nib_b + scl_b, a.zro + tile * kTileZroBytes, ktc * kTileZroBytes, &bars[st]);
   };
+  auto issue = [&](int j) { issue_to(j, j % S); };
 
   // 1. Weight copies of the first S columns: they depend on nothing the
   //    previous kernel writes.
@@ -668,6 +679,69 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
     }
     cluster.sync();
   };
+  if (a.wide_groups) {
+    // (planned only without a K split and with an even S.) Two independent
+    // groups of 8 warps take alternate columns (group 0 the even ones), each
+    // with its own named barrier, its half of `red` and its own ring of S / 2
+    // stages (group q: stages q, q + 2, ...): a group's barriers wait for 8
+    // warps, not 16, one group's barrier and reduction overlap the other
+    // group's multiplies, and every stage is filled and drained by one group
+    // in column order, so a parity wait is never two phases behind. The
+    // group refills the stage it has just drained with its column j + S.
+    const int grp = warp >> 3, gw = warp & 7, gtid = threadIdx.x & 255;
+    const int Sg = S >> 1;
+    const int gtpw = (ktc + 7) / 8;
+    const int gt0 = min(ktc, gw * gtpw), gt1 = min(ktc, gt0 + gtpw);
+    float *gred = red + grp * (8 * NG * 128);
+    int l = 0;  // the group's column count
+    for (int j = grp; j < J; j += 2, l++) {
+      float acc[NG][4];
+#pragma unroll
+      for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[ng][e] = 0.0f;
+      const int st = grp + 2 * (l % Sg);
+      mbar_wait_bounded(&bars[st], (l / Sg) & 1, a.flags);
+      const uint8_t *sb = stages + st * L.stage_bytes;
+#pragma unroll 2
+      for (int i = gt0; i < gt1; i++)
+        tile_mma<NG, ZEROS, NG == 1>(sb + i * kTileNibBytes, sb + nib_b + i * kTileSclBytes,
+                                     sb + nib_b + scl_b + i * kTileZroBytes, xs + i * kTileK + 4 * t, L.xstride, M,
+                                     lane, acc);
+#pragma unroll
+      for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) gred[((gw * NG + ng) * 4 + e) * 32 + lane] = acc[ng][e];
+      named_bar_sync(1 + grp, 256);
+      if (gtid == 0 && j + S < J) issue_to(j + S, st);  // the group's next column for this stage
+      const int nt = g + j * G;
+      auto gsum_at = [&](int r, int tok) {
+        const int ng = tok >> 3, tk = tok & 7;
+        const int ln = 4 * (r & 7) + (tk >> 1);
+        const int e = ((r >> 3) << 1) | (tk & 1);
+        float sum = 0.0f;
+#pragma unroll
+        for (int w2 = 0; w2 < 8; w2++) sum += gred[((w2 * NG + ng) * 4 + e) * 32 + ln];
+        return sum;
+      };
+      if (a.epi == kEpiNone) {
+        for (int o = gtid; o < kOut; o += 256) {
+          const int r = o / (8 * NG), tok = o - r * (8 * NG);
+          emit(a, parity, nt, r, tok, gsum_at(r, tok));
+        }
+      } else {
+        for (int o = gtid; o < kOut / 2; o += 256) {
+          const int r = o / (8 * NG), tok = o - r * (8 * NG);
+          emit_pair(a, nt, r, tok, gsum_at(r, tok), gsum_at(r + 8, tok));
+        }
+      }
+      named_bar_sync(1 + grp, 256);  // the group's half of red is reused next
+    }
+    // No copy may still be writing shared memory at exit (only possible
+    // after a timed-out wait): the group's last use of each of its stages.
+    if (gtid == 0)
+      for (int q = max(0, l - Sg); q < l; q++) mbar_wait_bounded(&bars[grp + 2 * (q % Sg)], (q / Sg) & 1, a.flags);
+  } else
   for (int j = 0; j < J; j++) {
     float acc[NG][4];
 #pragma unroll
@@ -721,7 +795,8 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   // a timed-out wait).
   if (threadIdx.x == 0) {
     if (x_bulk) mbar_wait_bounded(xbar, 0, a.flags);
-    for (int j = max(0, J - S); j < J; j++) mbar_wait_bounded(&bars[j % S], (j / S) & 1, a.flags);
+    if (!a.wide_groups)
+      for (int j = max(0, J - S); j < J; j++) mbar_wait_bounded(&bars[j % S], (j / S) & 1, a.flags);
   }
   if (a.push_on) push_signal(a.push);
   if (a.trace && threadIdx.x == 0) {
@@ -741,7 +816,7 @@ int wide_max_clusters(int C, int smem, int num_sms) {
   if (it != cache.end()) return it->second;
   auto kern = gemv_wide_kernel<1, false, kProNone>;
   int n = 0;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMax) == cudaSuccess &&
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMaxGroups) == cudaSuccess &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)C, (unsigned)(num_sms / C > 0 ? num_sms / C : 1), 1);
@@ -769,13 +844,13 @@ cudaError_t launch_wide_t(const GemvArgs &a, cudaStream_t stream, bool pdl) {
   auto kern = gemv_wide_kernel<NG, ZEROS, PRO>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMax);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWideSmemMaxGroups);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  if (L.total > kWideSmemMax) return cudaErrorInvalidValue;
+  if (L.total > (a.wide_groups ? kWideSmemMaxGroups : kWideSmemMax)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)a.cluster, (unsigned)G, 1);
   cfg.blockDim = dim3(kWThreads, 1, 1);
@@ -854,6 +929,26 @@ bool plan_gemv_wide(GemvArgs &a, int num_sms) {
   int S = 4;
   while (S > 1 && wide_smem(a.M, ktc, S, 4, C, zeros).total > kWideSmemMax) S--;
   if (wide_smem(a.M, ktc, S, 1, C, zeros).total > kWideSmemMax) return false;
+  // Without a K split, two warp groups walk alternate columns through
+  // their own stage rings (an even S). WG_GEMV_WIDE_GROUPS (comparison): 0
+  // off, 1 within the 200 KB budget, 2 (default) within 224 KB — measured
+  // on B200: M = 8 at 28672x4096 25.2 us (off), 23.6 (1: two stages), 20.6
+  // (2: four stages).
+  static int groups_on = -1;
+  if (groups_on < 0) {
+    const char *e = getenv("WG_GEMV_WIDE_GROUPS");
+    groups_on = e ? atoi(e) : 2;
+  }
+  a.wide_groups = 0;
+  if (groups_on && C == 1) {
+    const int budget = groups_on == 2 ? kWideSmemMaxGroups : kWideSmemMax;
+    int S2 = 4;
+    while (S2 > 2 && wide_smem(a.M, ktc, S2, 1, C, zeros).total > budget) S2 -= 2;
+    if (wide_smem(a.M, ktc, S2, 1, C, zeros).total <= budget) {
+      S = S2;
+      a.wide_groups = 1;
+    }
+  }
   int Jc = (a.NT + G - 1) / G * 2;
   while (Jc > 1 && wide_smem(a.M, ktc, S, Jc, C, zeros).total > kWideSmemMax) Jc--;
   // one wave: no more clusters than fit at once

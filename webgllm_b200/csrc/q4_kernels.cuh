@@ -73,6 +73,7 @@ struct GemvArgs {
   int push_on;     // outputs go to every rank's exchange buffer (comm.cuh), not y
   CommDev push;
   int epi;         // kEpiNone, or kEpiSwigluPairs: y [M][N/2] = silu(rows 16t..16t+7) * rows 16t+8..16t+15
+  int wide_groups; // wide GEMV without a K split: two 8-warp groups take alternate columns
 };
 enum EpiKind { kEpiNone = 0, kEpiSwigluPairs = 1 };
 
