@@ -680,7 +680,8 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
     cluster.sync();
   };
   if (a.wide_groups) {
-    // (planned only without a K split and with an even S.) Two independent
+    // (planned with an even S, and with a K split only when `part` holds
+    // every column of the walk.) Two independent
     // groups of 8 warps take alternate columns (group 0 the even ones), each
     // with its own named barrier, its half of `red` and its own ring of S / 2
     // stages (group q: stages q, q + 2, ...): a group's barriers wait for 8
@@ -724,7 +725,12 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
         for (int w2 = 0; w2 < 8; w2++) sum += gred[((w2 * NG + ng) * 4 + e) * 32 + ln];
         return sum;
       };
-      if (a.epi == kEpiNone) {
+      if (C > 1) {  // every output of the column waits for the cluster reduction
+        for (int o = gtid; o < kOut; o += 256) {
+          const int r = o / (8 * NG), tok = o - r * (8 * NG);
+          part[j * kOut + o] = gsum_at(r, tok);
+        }
+      } else if (a.epi == kEpiNone) {
         for (int o = gtid; o < kOut; o += 256) {
           const int r = o / (8 * NG), tok = o - r * (8 * NG);
           emit(a, parity, nt, r, tok, gsum_at(r, tok));
@@ -741,6 +747,10 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
     // after a timed-out wait): the group's last use of each of its stages.
     if (gtid == 0)
       for (int q = max(0, l - Sg); q < l; q++) mbar_wait_bounded(&bars[grp + 2 * (q % Sg)], (q / Sg) & 1, a.flags);
+    // With a K split: one cluster reduction of all J columns (planned only
+    // when `part` holds them all). Every thread of every CTA of the cluster
+    // gets here: the CTAs of a cluster share g, hence J.
+    if (C > 1) flush(0, J);
   } else
   for (int j = 0; j < J; j++) {
     float acc[NG][4];
@@ -954,8 +964,34 @@ bool plan_gemv_wide(GemvArgs &a, int num_sms) {
   // one wave: no more clusters than fit at once
   const int fit = wide_max_clusters(C, wide_smem(a.M, ktc, S, Jc, C, zeros).total, num_sms);
   if (G > fit) G = fit;
-  const int J = (a.NT + G - 1) / G;
+  int J = (a.NT + G - 1) / G;
   if (Jc > J) Jc = J;
+  // With a K split the group walk keeps every column's partial sums in
+  // `part` and reduces them across the cluster once, after the walk: only
+  // when all J columns fit (the cluster count, hence J, depends on the
+  // shared memory it is planned with). Not yet for the tensor-parallel push
+  // exchange (its K-split launches keep the per-chunk walk, the one measured
+  // on several GPUs).
+  if (groups_on && C > 1 && !a.push_on) {
+    const int budget = groups_on == 2 ? kWideSmemMaxGroups : kWideSmemMax;
+    const int Gmax = min(num_sms / C > 0 ? num_sms / C : 1, a.NT);
+    const int Jest = (a.NT + Gmax - 1) / Gmax;
+    int S2 = 4;
+    while (S2 > 2 && wide_smem(a.M, ktc, S2, Jest, C, zeros).total > budget) S2 -= 2;
+    const int smem2 = wide_smem(a.M, ktc, S2, Jest, C, zeros).total;
+    if (smem2 <= budget) {
+      const int G2 = min(Gmax, wide_max_clusters(C, smem2, num_sms));
+      const int J2 = (a.NT + G2 - 1) / G2;
+      if (J2 <= Jest) {
+        S = S2;
+        G = G2;
+        J = J2;
+        Jc = J2;
+        a.wide_groups = 1;
+      }
+    }
+  }
+  (void)J;
   a.kt_per_cta = ktc;
   a.cluster = C;
   a.groups = G;
