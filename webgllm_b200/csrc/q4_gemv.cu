@@ -991,7 +991,6 @@ bool plan_gemv_wide(GemvArgs &a, int num_sms) {
       }
     }
   }
-  (void)J;
   a.kt_per_cta = ktc;
   a.cluster = C;
   a.groups = G;
