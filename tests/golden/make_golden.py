@@ -1,7 +1,7 @@
 """Writes the golden fixtures of this directory. Run it where the reference
 tree exists (it is read as text, never executed):
 
-    python tests/golden/make_golden.py [--reference <webgllm package dir>]
+    python tests/golden/make_golden.py --reference <webgllm package dir>
 
 Two files come out:
 
@@ -31,7 +31,6 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-DEFAULT_REF = Path("/root/reference/packages/webgllm")
 
 
 class Source:
@@ -130,7 +129,8 @@ def config0(path: Path) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=DEFAULT_REF)
+    ap.add_argument("--reference", type=Path, required=True,
+                    help="the webgllm package directory (packages/webgllm of the reference tree)")
     args = ap.parse_args()
     vec = reference_vectors(args.reference)
     (HERE / "reference_vectors.json").write_text(json.dumps(vec, indent=1) + "\n")
