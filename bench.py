@@ -422,7 +422,10 @@ def run_e2e(args, ctx, mats, x, ys, per_launch, world, barrier, max_over_ranks):
 
 
 def run_sweep(mats, stream, hbm, bf16):
-    """Config 1's row counts on 8 rotating matrices (informational)."""
+    """Config 1's row counts on 8 rotating matrices (informational), each
+    row count's chain of launches captured as a CUDA graph as the main step
+    is (eager launches one by one would time the host's launch rate at small
+    M); a row whose capture fails is timed eagerly and says so."""
     import torch
 
     import webgllm_b200 as wg
@@ -435,23 +438,38 @@ def run_sweep(mats, stream, hbm, bf16):
             xm = torch.from_numpy(synthetic.activations(M, K_IN, 1)).to("cuda", torch.float16)
             ym = torch.empty((M, N_OUT), device="cuda", dtype=torch.float16)
             reps = 8 if M <= 64 else 2
-            for r in range(nm):
-                wg.matmul(xm, mats[r], out=ym)
+
+            def chain():
+                for r in range(nm):
+                    wg.matmul(xm, mats[r], out=ym)
+
+            chain()  # first launches size the scratch and configure the kernels
             stream.synchronize()
+            graph, timing = None, "cuda graph"
+            try:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    chain()
+                graph.replay()
+                stream.synchronize()
+            except Exception as e:  # noqa: BLE001 - informational rows fall back to eager timing
+                graph, timing = None, f"eager ({type(e).__name__})"
+                torch.cuda.synchronize()
+            run = graph.replay if graph is not None else chain
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s0.record(stream)
             for _ in range(reps):
-                for r in range(nm):
-                    wg.matmul(xm, mats[r], out=ym)
+                run()
             s1.record(stream)
             stream.synchronize()
+            del graph
             t = s0.elapsed_time(s1) / 1e3 / (reps * nm)
             b = algorithmic_bytes(M, N_OUT, K_IN)
             f = 2.0 * M * N_OUT * K_IN
             sweep.append({"M": M, "us": round(t * 1e6, 2), "GB/s": round(b / t / 1e9, 1),
                           "TFLOP/s": round(f / t / 1e12, 2),
                           "frac_hbm": round(b / t / 1e9 / hbm, 3),
-                          "frac_bf16": round(f / t / 1e12 / bf16, 3)})
+                          "frac_bf16": round(f / t / 1e12 / bf16, 3), "timing": timing})
     return sweep
 
 
