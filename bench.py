@@ -155,8 +155,10 @@ def cpu_baseline(seconds: float = 10.0) -> dict:
 
 def run_reference(args) -> None:
     """The reference arm: the oracle's restatement of the reference's shader
-    arithmetic on all host threads (rank 0 only). Each step is a row slice of
-    the M=1 4096x4096 GEMV, sized so that warmup + steps fit ~90 s."""
+    arithmetic on all host threads (rank 0 only). Each step repeats the full
+    M=1 4096x4096 GEMV `reps` times, so that the timed region lasts at least
+    ~10 s (a short region times a cold CPU); only when the requested steps
+    would exceed ~90 s is a step cut to a row slice of one GEMV."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -167,32 +169,46 @@ def run_reference(args) -> None:
     full = O.HostQuantMatrix(N_OUT, K_IN)
     O.c_pack_q4_0(full, 0, blocks, N_OUT)
     x = O.config_activations(M_ROWS, K_IN, 0)
-    t0 = time.perf_counter()
-    O.c_split_emulate(full, x, threads)
-    t_full = time.perf_counter() - t0
-    budget = 90.0 / max(1, args.steps + args.warmup)
-    rows = int(min(N_OUT, max(64, N_OUT * budget / max(t_full, 1e-9)))) // 64 * 64
-    rows = max(64, rows)
-    sub = O.HostQuantMatrix(rows, K_IN)
-    O.c_pack_q4_0(sub, 0, blocks[: rows * (K_IN // 32) * 18], rows)
+    # warm the threads and caches (~1 s), then time one full GEMV
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 1.0:
+        O.c_split_emulate(full, x, threads)
+        n += 1
+    t_full = (time.perf_counter() - t0) / n
+    steps = max(1, args.steps)
+    per_step = min(max(10.0 / steps, t_full), 90.0 / (steps + args.warmup))
+    if per_step >= t_full:
+        reps, rows = max(1, round(per_step / t_full)), N_OUT
+        sub = full
+    else:
+        reps = 1
+        rows = max(64, int(N_OUT * per_step / t_full) // 64 * 64)
+        sub = O.HostQuantMatrix(rows, K_IN)
+        O.c_pack_q4_0(sub, 0, blocks[: rows * (K_IN // 32) * 18], rows)
+
+    def step():
+        for _ in range(reps):
+            O.c_split_emulate(sub, x, threads)
+
     for _ in range(args.warmup):
-        O.c_split_emulate(sub, x, threads)
+        step()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        O.c_split_emulate(sub, x, threads)
+    for _ in range(steps):
+        step()
     dt = time.perf_counter() - t0
-    per = algorithmic_bytes(M_ROWS, rows, K_IN, 4, 4)
-    gbs = args.steps * per / dt / 1e9
-    sample = (f"each step: rows 0..{rows} of the M=1 4096x4096 Q4_0 GEMV ({per} bytes) in the "
-              f"oracle's shader emulation, {threads} threads; the reference's WebGL2 path "
-              "(headless Chromium + SwiftShader) is unavailable on this box")
+    per = reps * algorithmic_bytes(M_ROWS, rows, K_IN, 4, 4)
+    gbs = steps * per / dt / 1e9
+    what = f"{reps} x the M=1 4096x4096 Q4_0 GEMV" if rows == N_OUT else f"rows 0..{rows} of the M=1 4096x4096 Q4_0 GEMV"
+    sample = (f"each step: {what} ({per} bytes) in the oracle's shader emulation, {threads} threads; "
+              f"timed region {dt:.1f} s; the reference's WebGL2 path (headless Chromium + SwiftShader) "
+              "is unavailable on this box")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config1 decode GEMV: M=1 row x K=N=4096 Q4_0 (CPU row slice per step)",
-                   "M": M_ROWS, "N": N_OUT, "K": K_IN, "rows_per_step": rows},
+        "config": {"workload": "config1 decode GEMV: M=1 row x K=N=4096 Q4_0 (CPU, repeated per step)",
+                   "M": M_ROWS, "N": N_OUT, "K": K_IN, "rows_per_step": rows, "gemvs_per_step": reps},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -329,6 +345,11 @@ def main() -> None:
     line = make_line(args, world, value, ms_step, per_launch, achieved, hbm, src, traffic, e2e, clock, cpu, sweep)
     line["decode"] = decode
     print(json.dumps(line), flush=True)
+    bad = [d for d in decode or [] if d.get("tokens_match_tp1") is False]
+    if bad:
+        print(f"TENSOR-PARALLEL PARITY FAILED: {len(bad)} run(s) generated tokens that differ from one GPU's "
+              f"(first: {bad[0].get('first_mismatch')})", file=sys.stderr, flush=True)
+        sys.exit(1)
 
 
 def run_decode(world, rank, barrier, max_over_ranks, hbm):
@@ -360,7 +381,28 @@ def run_decode(world, rank, barrier, max_over_ranks, hbm):
             "step_bytes_per_gpu": int(r["step_bytes"]),
             "frac_hbm": round(r["step_bytes"] / (step_ms / 1e3) / 1e9 / hbm, 4),
             "first_tokens": r["tokens_head"][0],
+            "tokens_sha256": r["tokens_sha256"],
         })
+        out[-1]["_tokens"] = r["tokens"]
+    if world > 1:
+        # Parity of the partitioned model: rank 0 also generates config 4 on
+        # its GPU alone (the unsharded model from the same seeds) and every
+        # tensor-parallel run's whole output (batch x generated tokens) must
+        # equal it.
+        barrier()
+        if rank == 0:
+            cfg, batch, prompt, gen = runner.WORKLOADS["4"]
+            r1 = runner.measure(cfg, batch, prompt, gen, tp=None)
+            for o in out:
+                got, want = o["_tokens"], r1["tokens"]
+                diff = (got != want).nonzero()
+                o["tokens_match_tp1"] = bool(diff.numel() == 0)
+                o["tp1_tokens_sha256"] = r1["tokens_sha256"]
+                if diff.numel():
+                    o["first_mismatch"] = {"sequence": int(diff[0, 0]), "token": int(diff[0, 1])}
+        barrier()
+    for o in out:
+        o.pop("_tokens", None)
     if world == 1:
         # config 4's speculative workload (draft k = 4); random-init draft and
         # target rarely agree, so the acceptance rate comes with the rate

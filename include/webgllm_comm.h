@@ -12,7 +12,8 @@
  * stores of 64-bit words, each carrying its value and the exchange's
  * sequence number, so no flag or fence orders them); wg_comm_reduce polls
  * its local buffer until every word carries the expected sequence number
- * (at most ~2 s, then WG_TIMEOUT from wg_sync) and sums the partials.
+ * (at most 2 s by default, wg_comm_set_wait, then WG_TIMEOUT from wg_sync)
+ * and sums the partials.
  *
  * Setup, per rank (one process per GPU): wg_ipc_alloc a buffer, exchange
  * the 64-byte handles (e.g. an all-gather over torch.distributed),
@@ -48,6 +49,16 @@ int wg_ipc_close(wg_ctx *ctx, void *dptr);
  * and mappings. */
 int wg_comm_init(wg_ctx *ctx, int world, int rank, void *const *buffers, size_t bytes, wg_comm **out);
 int wg_comm_destroy(wg_ctx *ctx, wg_comm *comm);
+/* How long a consumer (wg_comm_reduce, wg_comm_reduce_norm) waits for a
+ * peer's partial before it gives up: wait_ns nanoseconds (default 2 s, the
+ * value wg_comm_init sets). A wait that runs out makes the next wg_sync
+ * return WG_TIMEOUT; the launch ends after about one wait (the words still
+ * missing read as 0) and the context stays usable. The limit applies to
+ * launches enqueued after the call (a CUDA graph keeps the value it was
+ * captured with). Replaces the reference's context-loss detection
+ * (GpuError, src/gpu/gl.ts:502; classified in src/worker-errors.ts:14-24). */
+int wg_comm_set_wait(wg_comm *comm, unsigned long long wait_ns);
+
 /* Floats one rank's partial may hold (M * N of a pushing matmul). */
 int wg_comm_slot(const wg_comm *comm, size_t *floats);
 

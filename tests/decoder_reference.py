@@ -54,19 +54,19 @@ def rope_kv(qkv, H, Hkv, Dh, pos0, theta, q_norm=None, k_norm=None, eps=1e-5):
 
 def attention(q, k_cache, v_cache, pos0, H, Hkv):
     """q fp16 [rows][H][Dh] (scaled); caches fp16 [Hkv][cache_len][Dh];
-    row r attends keys 0..pos0+r. Returns fp32 [rows][H][Dh]."""
+    row r attends keys 0..pos0+r. Returns fp32 [rows][H][Dh]. Query head h
+    reads KV head h // (H / Hkv) (grouped-query attention)."""
     rows, _, Dh = q.shape
     G = H // Hkv
     L = pos0 + rows
-    out = torch.zeros((rows, H, Dh), dtype=torch.float32, device=q.device)
     keys = torch.arange(L, device=q.device)
     masked = keys[None, :] > (pos0 + torch.arange(rows, device=q.device))[:, None]  # [rows][L]
-    for h in range(H):
-        kk = k_cache[h // G, :L].float()
-        vv = v_cache[h // G, :L].float()
-        s = (q[:, h].float() @ kk.T).masked_fill(masked, float("-inf"))
-        out[:, h] = torch.softmax(s, dim=1) @ vv
-    return out
+    kk = k_cache[:, :L].float()  # [Hkv][L][Dh]
+    vv = v_cache[:, :L].float()
+    qh = q.float().permute(1, 0, 2).reshape(Hkv, G * rows, Dh)  # entry g * rows + r of KV head j: head j * G + g
+    s = (qh @ kk.transpose(1, 2)).masked_fill(masked.repeat(G, 1)[None], float("-inf"))
+    o = torch.softmax(s, dim=2) @ vv  # [Hkv][G * rows][Dh]
+    return o.reshape(H, rows, Dh).permute(1, 0, 2).contiguous()
 
 
 def swiglu(gu, I):
@@ -95,14 +95,25 @@ def dequant_linear(lin):
     return dequantize_q4_0(lin.blocks, lin.N, lin.K)
 
 
-class ReferenceDecoder:
-    """The same forward as webgllm_b200.model.DecoderModel, in torch fp32,
-    from the model's own weights (its Linears must keep their Q4_0 blocks)."""
+def reference_weights(model):
+    """The model's linears dequantised to fp32 (its Linears must keep their
+    Q4_0 blocks) and its fp16 head as fp32: shared by the references of
+    several sequences."""
+    return {"layers": [{k: dequant_linear(v) for k, v in L.items() if hasattr(v, "blocks")} for L in model.layers],
+            "head": model.head.float()}
 
-    def __init__(self, model):
+
+class ReferenceDecoder:
+    """The same forward as webgllm_b200.model.DecoderModel for one sequence,
+    in torch fp32, from the model's own weights (`weights` from
+    reference_weights(model), or made here)."""
+
+    def __init__(self, model, weights=None):
         self.m = model
         cfg = model.cfg
-        self.W = [{k: dequant_linear(v) for k, v in L.items() if hasattr(v, "blocks")} for L in model.layers]
+        weights = weights or reference_weights(model)
+        self.W = weights["layers"]
+        self.head = weights["head"]
         n_attn = sum(t == "attn" for t in cfg.layer_types)
         n_conv = sum(t == "conv" for t in cfg.layer_types)
         self.k = [torch.zeros((cfg.kv_heads, model.max_ctx, cfg.head_dim), dtype=torch.float16, device="cuda")
@@ -141,6 +152,6 @@ class ReferenceDecoder:
             o = act @ W["down"].t()
             add = o
         x, h = rmsnorm(x[-1:], add[-1:], m.final_norm, cfg.eps)
-        logits = h.half().float() @ m.head.float().t()
+        logits = h.half().float() @ self.head.t()
         self.pos += rows
         return logits[0]

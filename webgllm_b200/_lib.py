@@ -85,6 +85,7 @@ SIGNATURES = {
     "wg_ipc_close": (_I, [_P, _P]),
     "wg_comm_init": (_I, [_P, _I, _I, _P, _SZ, _PP]),
     "wg_comm_destroy": (_I, [_P, _P]),
+    "wg_comm_set_wait": (_I, [_P, ctypes.c_ulonglong]),
     "wg_comm_slot": (_I, [_P, ctypes.POINTER(_SZ)]),
     "wg_q4_matmul_push": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "wg_comm_reduce": (_I, [_P, _P, _I, _I, _P]),

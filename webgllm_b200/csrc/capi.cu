@@ -438,13 +438,11 @@ int wg_q4_matrix_row(wg_ctx *ctx, const wg_q4mat *m, int n, float *out) {
 
 }  // extern "C"
 
-namespace {
-
 // Which GEMV serves a launch of up to 8 rows: the wide one (x resident per
 // CTA, columns streamed) when the tile-column GEMV would need several waves
 // of CTAs or re-stage several rows of x in each of them. WG_GEMV_WIDE=0 / 1
 // forces one or the other (measurement).
-bool use_wide(const wg_ctx *ctx, const wg::GemvArgs &a) {
+bool wg::gemv_use_wide(const wg_ctx *ctx, const wg::GemvArgs &a) {
   if (a.M > 32 || (a.pro.kind != wg::kProNone && a.M > wg::kProMaxTokens)) return false;
   if (ctx->gemv_wide >= 0) return ctx->gemv_wide == 1;
   wg::GemvArgs t = a;
@@ -457,6 +455,8 @@ bool use_wide(const wg_ctx *ctx, const wg::GemvArgs &a) {
   if (a.K >= 8192) return true;
   return a.M >= 2 && a.N >= 16384;
 }
+
+namespace {
 
 // The matmul behind wg_q4_matmul and wg_q4_matmul_fused: y = x . W^T, with
 // x given (pro == null) or made by a prologue. Arguments are checked.
@@ -474,7 +474,7 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
   // split path takes go to the prompt matmul). Measured on B200, the GEMM
   // (latency-bound near 18 us at 4096 x 4096) beats the GEMV from 17 rows
   // on; pushes and epilogues stay in the GEMV, which has them.
-  const bool gemm_rows = M > wg::kGemvMaxTokens || (M > 16 && !push && epi == wg::kEpiNone);
+  const bool gemm_rows = M > wg::kGemvMaxTokens || (M >= wg::kGemmMinRows && !push && epi == wg::kEpiNone);
   if (gemm_rows && wg::gemm_supported()) {
     wg::GemmArgs g{};
     g.nib = m->nib;
@@ -548,7 +548,7 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     }
     a.epi = epi;
     wg::GemvArgs w = a;
-    if (use_wide(ctx, a) && wg::plan_gemv_wide(w, ctx->num_sms)) {
+    if (wg::gemv_use_wide(ctx, a) && wg::plan_gemv_wide(w, ctx->num_sms)) {
       WG_CUDA(ctx, wg::launch_gemv_wide(w, ctx->stream, ctx->pdl));
       continue;
     }

@@ -109,6 +109,7 @@ int wg_comm_init(wg_ctx *ctx, int world, int rank, void *const *buffers, size_t 
   c->bytes = bytes;
   c->dev.world = world;
   c->dev.rank = rank;
+  c->dev.wait_ns = wg::kCommWaitNs;
   // data: 2 parities x world slots, each slot a multiple of 16 words
   c->dev.slot = (long long)((bytes - wg::kCommHeaderBytes) / (2 * (size_t)world * sizeof(unsigned long long))) / 16 * 16;
   for (int r = 0; r < world; r++) {
@@ -127,6 +128,12 @@ int wg_comm_destroy(wg_ctx *ctx, wg_comm *comm) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   }
   delete comm;
+  return WG_OK;
+}
+
+int wg_comm_set_wait(wg_comm *comm, unsigned long long wait_ns) {
+  if (!comm || wait_ns == 0) return WG_INVALID_ARGUMENT;
+  comm->dev.wait_ns = wait_ns;
   return WG_OK;
 }
 

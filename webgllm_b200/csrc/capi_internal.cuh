@@ -55,3 +55,9 @@ struct wg_q4mat {
   size_t bytes;
 };
 
+
+namespace wg {
+struct GemvArgs;
+// Whether a GEMV launch of these arguments goes to the wide kernel (capi.cu).
+bool gemv_use_wide(const wg_ctx *ctx, const GemvArgs &a);
+}  // namespace wg

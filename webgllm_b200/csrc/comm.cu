@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(kReduceThreads) comm_reduce_kernel(const CommD
     // slot layout [n][token]; out [token][n]
     const int n = i / M, tok = i - n * M;
     float v = 0.0f;
-    for (int r = 0; r < c.world; r++) v += comm_wait_word(base + (long long)r * c.slot + i, e, flags);
+    for (int r = 0; r < c.world; r++) v += comm_wait_word(base + (long long)r * c.slot + i, e, flags, c.wait_ns);
     out[(size_t)tok * N + n] = v;
   }
   __syncthreads();
@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(kNormThreads) addnorm_kernel(const float *a, c
     if (threadIdx.x + j * kNormThreads < Kc) {
       float add = 0.0f;
       if (COMM) {
-        for (int r = 0; r < c.world; r++) add += comm_wait_word(base + (long long)r * c.slot + (long long)k * M + m, s_e, flags);
+        for (int r = 0; r < c.world; r++) add += comm_wait_word(base + (long long)r * c.slot + (long long)k * M + m, s_e, flags, c.wait_ns);
       } else if (b) {
         add = b[(size_t)m * K + k];
       }

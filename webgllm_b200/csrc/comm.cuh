@@ -35,17 +35,19 @@ constexpr int kCommProdSeq = 64;       // byte 512
 constexpr int kCommConsSeq = 72;       // byte 576
 constexpr int kCommProdCount = 80;     // byte 640 (u32 counter in a u64 word)
 constexpr int kCommConsCount = 88;     // byte 704
-constexpr unsigned long long kCommWaitNs = 2000000000ull;  // 2 s, then give up and report
+constexpr unsigned long long kCommWaitNs = 2000000000ull;  // default wait: 2 s, then give up and report
 
 struct CommDev {
   unsigned long long *inbox[kCommMaxRanks];  // data region of each rank's buffer
   unsigned long long *hdr[kCommMaxRanks];    // header of each rank's buffer
   int world, rank;
   long long slot;                            // words per slot
+  unsigned long long wait_ns;                // how long a consumer polls one word
 };
 
-// The sequence number of the exchange this launch produces (read at entry:
-// only the launch's last CTA advances it, after every CTA is done).
+// The sequence number of the exchange this launch produces. Only the
+// previous pushing launch's last CTA advances it, so a launch reads it after
+// its dependency wait (griddepcontrol.wait).
 __device__ __forceinline__ unsigned push_seq(const CommDev &c) {
   return (unsigned)(*(volatile unsigned long long *)(c.hdr[c.rank] + kCommProdSeq) + 1);
 }
@@ -74,17 +76,21 @@ __device__ __forceinline__ void push_signal(const CommDev &c) {
 }
 
 // The value of word `w` once it carries sequence number `e`: polls (relaxed,
-// system scope) for at most kCommWaitNs, then raises kFlagTimeout.
-__device__ __forceinline__ float comm_wait_word(const unsigned long long *w, unsigned e, unsigned *flags) {
+// system scope) for at most wait_ns, then raises kFlagTimeout. Once the
+// flag is up (this or an earlier wait ran out) no word is waited for again,
+// so a launch whose peer never pushed ends after one wait_ns.
+__device__ __forceinline__ float comm_wait_word(const unsigned long long *w, unsigned e, unsigned *flags,
+                                                unsigned long long wait_ns) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
   if ((unsigned)(v >> 32) == e) return __uint_as_float((unsigned)v);
+  if (*(volatile unsigned *)flags & kFlagTimeout) return 0.0f;
   const unsigned long long t0 = globaltimer();
   while (true) {
     __nanosleep(32);
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
     if ((unsigned)(v >> 32) == e) return __uint_as_float((unsigned)v);
-    if (globaltimer() - t0 > kCommWaitNs) {
+    if (globaltimer() - t0 > wait_ns || (*(volatile unsigned *)flags & kFlagTimeout)) {
       raise_flag(flags, kFlagTimeout);
       return 0.0f;
     }

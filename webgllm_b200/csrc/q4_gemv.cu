@@ -267,7 +267,6 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L.bar) + warp;
   __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
-  const unsigned parity = a.push_on ? push_seq(a.push) : 0u;  // the exchange's sequence number
 
   // 1. Each warp starts the copies of its own tiles (the TMA engine, one
   //    mbarrier a warp): weights depend on nothing the previous kernel
@@ -295,6 +294,10 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
   if (a.trigger_at == 0) pdl_trigger();
   pdl_wait();
   if (a.trace && threadIdx.x == 0) ts[2] = globaltimer();
+  // The exchange's sequence number, read only after the wait: the previous
+  // pushing launch advances it from its last CTA, and that launch is
+  // complete only once every kernel this one waits on is.
+  const unsigned parity = a.push_on ? push_seq(a.push) : 0u;
 
   // 3. Each warp stages its own K slice of x[0..M) as fp16 (no CTA barrier,
   //    except for the norm prologue's row statistics).
@@ -571,7 +574,6 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   const int nib_b = ktc * kTileNibBytes, scl_b = ktc * kTileSclBytes;
   __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
-  const unsigned parity = a.push_on ? push_seq(a.push) : 0u;  // the exchange's sequence number
 
   // column g + j*G (this CTA's K range) into stage st (j % S, or the warp
   // groups' own rings: the first S columns land in stage j either way)
@@ -598,6 +600,8 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   // 2. x (or its prologue) for this CTA's K range, once.
   pdl_wait();
   if (a.trace && threadIdx.x == 0) ts[2] = globaltimer();
+  // read after the wait, as in gemv_kernel
+  const unsigned parity = a.push_on ? push_seq(a.push) : 0u;
   const int M = a.M;
   __shared__ float s_inv[kProMaxTokens];
   if constexpr (PRO == kProRmsNorm) {

@@ -78,6 +78,10 @@ struct GemvArgs {
 enum EpiKind { kEpiNone = 0, kEpiSwigluPairs = 1 };
 
 constexpr int kGemvMaxTokens = 32;
+// Rows from which a plain matmul (no push, no epilogue) goes to the GEMM;
+// measured on B200, the GEMM (latency-bound near 18 us at 4096 x 4096)
+// beats the GEMV from 17 rows on.
+constexpr int kGemmMinRows = 17;
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl);
 // Plans kt_per_cta / cluster for a shape; false if the shape is too large.
 bool plan_gemv(GemvArgs &a, int num_sms);

@@ -90,7 +90,8 @@ extern "C" int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x
   cudaError_t e = cudaSetDevice(ctx->device);
   if (e != cudaSuccess) return fail_static(ctx, wg::status_of(e), "cudaSetDevice: %s", cudaGetErrorString(e));
 
-  if (M > wg::kGemvMaxTokens && wg::gemm_supported()) {
+  // The same routing as wg_q4_matmul: the GEMM from kGemmMinRows rows on.
+  if (M >= wg::kGemmMinRows && wg::gemm_supported()) {
     wg::GemmArgs g{};
     g.nib = m->nib;
     g.scl = m->scl;
@@ -125,7 +126,8 @@ extern "C" int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x
     return WG_OK;
   }
 
-  // Few rows: the GEMV, which needs no scratch at all.
+  // Few rows: the GEMV (tile-column or wide kernel, chosen as wg_q4_matmul
+  // chooses), which needs no scratch at all.
   const size_t xsz = x_dtype == WG_F32 ? 4 : 2, ysz = y_dtype == WG_F32 ? 4 : 2;
   for (int m0 = 0; m0 < M; m0 += wg::kGemvMaxTokens) {
     const int mc = M - m0 < wg::kGemvMaxTokens ? M - m0 : wg::kGemvMaxTokens;
@@ -144,6 +146,12 @@ extern "C" int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x
     a.y_dtype = y_dtype;
     a.flags = ctx->d_flags;
     a.trigger_at = ctx->trigger_at;
+    wg::GemvArgs w = a;
+    if (wg::gemv_use_wide(ctx, a) && wg::plan_gemv_wide(w, ctx->num_sms)) {
+      e = wg::launch_gemv_wide(w, ctx->stream, ctx->pdl);
+      if (e != cudaSuccess) return fail_static(ctx, wg::status_of(e), "GEMV launch: %s", cudaGetErrorString(e));
+      continue;
+    }
     if (!wg::plan_gemv(a, ctx->num_sms))
       return fail_static(ctx, WG_UNSUPPORTED, "K = %d is beyond the GEMV's largest cluster split", m->d.K);
     e = wg::launch_gemv(a, ctx->stream, ctx->pdl);

@@ -6,6 +6,8 @@ every rank of a tensor-parallel group calls it with the same arguments.
 """
 from __future__ import annotations
 
+import hashlib
+
 import torch
 
 from .model import CONFIGS, DecoderModel
@@ -79,6 +81,8 @@ def measure(cfg, batch: int, prompt_len: int, gen_len: int, tp=None, seed: int =
         "e2e_tok_s": batch * gen_len / ((prefill_ms + decode_ms) / 1e3),
         "step_bytes": step_bytes(m, prompt_len + gen_len / 2),
         "tokens_head": out[:, :8].tolist(),
+        "tokens": out.cpu(),
+        "tokens_sha256": hashlib.sha256(out.cpu().numpy().astype("<i4").tobytes()).hexdigest(),
     }
     m.graph = None
     m.close()
