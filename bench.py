@@ -363,10 +363,18 @@ def run_decode(world, rank, barrier, max_over_ranks, hbm):
 
     runs = [("2", None), ("3", None), ("4", None)] if world == 1 else [("4", True), ("4", False)]
     out = []
+    group = None
+    if world > 1:
+        # the library's own NCCL group; torch.distributed only carries its id
+        import torch
+
+        import webgllm_b200 as wg
+        from webgllm_b200.comm import TensorGroup
+
+        group = TensorGroup.from_torch(wg.context(torch.cuda.current_device()))
     for k, push in runs:
         cfg, batch, prompt, gen = runner.WORKLOADS[k]
-        tp = (rank, world, None) if world > 1 else None
-        r = runner.measure(cfg, batch, prompt, gen, tp=tp, barrier=barrier, push=bool(push))
+        r = runner.measure(cfg, batch, prompt, gen, tp=group, barrier=barrier, push=bool(push))
         step_ms = max_over_ranks(r["decode_ms_per_step"])
         prefill_ms = max_over_ranks(r["prefill_ms"])
         steps = gen - 1
@@ -374,7 +382,7 @@ def run_decode(world, rank, barrier, max_over_ranks, hbm):
         out.append({
             "config": int(k), "model": r["model"], "batch": batch, "prompt_tokens": prompt,
             "generated_tokens": gen, "tensor_parallel": world if k == "4" else 1,
-            "exchange": None if push is None else ("push all-reduce (GEMV epilogue, NVLink P2P)" if push else "NCCL all-reduce"),
+            "exchange": None if push is None else ("push all-reduce (GEMV epilogue, NVLink P2P)" if push else "NCCL all-reduce (through the library, wg_tp_allreduce)"),
             "decode_tok_s": round(batch / (step_ms / 1e3), 1), "decode_ms_per_step": round(step_ms, 4),
             "prefill_ms": round(prefill_ms, 3), "prefill_tok_s": round(batch * prompt / (prefill_ms / 1e3), 1),
             "e2e_tok_s": round(batch * gen / total_s, 1),
@@ -403,6 +411,8 @@ def run_decode(world, rank, barrier, max_over_ranks, hbm):
         barrier()
     for o in out:
         o.pop("_tokens", None)
+    if group is not None:
+        group.close()
     if world == 1:
         # config 4's speculative workload (draft k = 4); random-init draft and
         # target rarely agree, so the acceptance rate comes with the rate

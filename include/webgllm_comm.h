@@ -80,6 +80,55 @@ int wg_comm_reduce(wg_ctx *ctx, wg_comm *comm, int M, int N, float *out);
 int wg_comm_reduce_norm(wg_ctx *ctx, wg_comm *comm, int M, int K, const float *resid, const float *weight, float eps,
                         float *resid_out, void *x_out);
 
+/* ------------------------------------------------------------------------
+ * The tensor-parallel group: NCCL behind the C ABI, so that a host without
+ * PyTorch (the reference's TypeScript host through a Node-API addon) can
+ * join a group, all-reduce and set up the push exchange. The reference runs
+ * one worker per model (src/client.ts:64); here one process per GPU joins a
+ * group of `nranks` (the SURVEY's wg_tp_init(ctx, nranks, rank,
+ * ncclUniqueId) row). NCCL is loaded on first use (dlopen of libnccl.so.2,
+ * or the path in WG_NCCL_LIBRARY): a process that already loaded it shares
+ * that copy, and the library still loads where NCCL is absent (these calls
+ * then return WG_UNSUPPORTED).
+ *
+ * Bootstrap: one rank calls wg_tp_unique_id, the caller sends those
+ * WG_TP_ID_BYTES bytes to every rank by any transport (a worker message, a
+ * file, a store), and every rank calls wg_tp_init with its rank. Every rank
+ * must then issue the same collectives in the same order. */
+#define WG_TP_ID_BYTES 128
+
+/* all-reduce element types and operations */
+enum { WG_TP_F32 = 0, WG_TP_F16 = 1, WG_TP_BF16 = 2, WG_TP_I64 = 3 };
+enum { WG_TP_SUM = 0, WG_TP_MAX = 1 };
+
+typedef struct wg_tp wg_tp;
+
+/* A new group id (ncclGetUniqueId) into id[WG_TP_ID_BYTES]. */
+int wg_tp_unique_id(void *id);
+/* Joins the group `id` as `rank` of `nranks` on ctx's device (blocks until
+ * every rank has joined). */
+int wg_tp_init(wg_ctx *ctx, int nranks, int rank, const void *id, wg_tp **out);
+/* Leaves the group (after the ctx's stream has drained). */
+int wg_tp_destroy(wg_ctx *ctx, wg_tp *tp);
+int wg_tp_info(const wg_tp *tp, int *nranks, int *rank);
+/* In-place all-reduce of `count` elements on ctx's stream (WG_TP_SUM of
+ * f32 / f16 / bf16, WG_TP_MAX of i64): the row-parallel sums of prompt
+ * rows and the vocabulary-parallel greedy pick. Can be captured in a CUDA
+ * graph with the rest of a step. */
+int wg_tp_allreduce(wg_ctx *ctx, wg_tp *tp, void *buf, size_t count, int dtype, int op);
+/* Every rank reaches this point: a one-word all-reduce, waited for on the
+ * host for at most timeout_ms (0: 60 s). If a rank never arrives, the group
+ * is aborted (ncclCommAbort) and WG_TIMEOUT returned; the group is then
+ * unusable (wg_tp_destroy it) while the context stays usable. */
+int wg_tp_barrier(wg_ctx *ctx, wg_tp *tp, int timeout_ms);
+/* The push exchange (wg_q4_matmul_push / wg_comm_reduce) over this group:
+ * allocates this rank's buffer of `bytes`, all-gathers the IPC handles
+ * through NCCL, maps every peer's buffer and returns the communicator.
+ * wg_comm_destroy of such a communicator also unmaps the peers' buffers
+ * and frees this rank's (with a barrier of the group before each, so it
+ * is a collective call). */
+int wg_tp_comm(wg_ctx *ctx, wg_tp *tp, size_t bytes, wg_comm **out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,3 +80,16 @@ def test_error_classes():
     e = _lib.error_for(_lib.WG_OUT_OF_RANGE, "rows 6..10 are outside the matrix")
     assert isinstance(e, IndexError) and isinstance(e, wg.GpuError)
     assert isinstance(_lib.error_for(_lib.WG_DATA_TOO_SHORT, "x"), ValueError)
+
+
+def test_tensor_parallel_group_id_without_a_gpu():
+    """wg_tp_unique_id loads NCCL (libnccl.so.2) on first use and needs no
+    device: the id a host sends to every rank of a group."""
+    from webgllm_b200.comm import unique_id
+
+    a, b = unique_id(), unique_id()
+    assert len(a) == 128 and a != b
+    L = _lib.lib()
+    assert L.wg_tp_unique_id(None) == _lib.WG_INVALID_ARGUMENT
+    assert L.wg_tp_init(None, 2, 0, ctypes.create_string_buffer(128), ctypes.byref(ctypes.c_void_p())) \
+        == _lib.WG_INVALID_ARGUMENT

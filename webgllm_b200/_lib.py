@@ -90,6 +90,13 @@ SIGNATURES = {
     "wg_q4_matmul_push": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "wg_comm_reduce": (_I, [_P, _P, _I, _I, _P]),
     "wg_comm_reduce_norm": (_I, [_P, _P, _I, _I, _P, _P, ctypes.c_float, _P, _P]),
+    "wg_tp_unique_id": (_I, [_P]),
+    "wg_tp_init": (_I, [_P, _I, _I, _P, _PP]),
+    "wg_tp_destroy": (_I, [_P, _P]),
+    "wg_tp_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "wg_tp_allreduce": (_I, [_P, _P, _P, _SZ, _I, _I]),
+    "wg_tp_barrier": (_I, [_P, _P, _I]),
+    "wg_tp_comm": (_I, [_P, _P, _SZ, _PP]),
     "wg_error_string": (ctypes.c_char_p, [_I]),
     "wg_last_error": (ctypes.c_char_p, [_P]),
 }

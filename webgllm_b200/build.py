@@ -60,7 +60,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
     if _stale(LIB, objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs), "-ldl"]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)

@@ -127,8 +127,10 @@ int wg_comm_destroy(wg_ctx *ctx, wg_comm *comm) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   }
+  int st = WG_OK;
+  if (comm->tp) st = wg_tp_comm_release(ctx, comm);
   delete comm;
-  return WG_OK;
+  return st;
 }
 
 int wg_comm_set_wait(wg_comm *comm, unsigned long long wait_ns) {

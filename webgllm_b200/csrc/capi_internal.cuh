@@ -38,12 +38,20 @@ struct wg_ctx {
 
 // A tensor-parallel exchange (comm.cuh): this rank's view of every rank's
 // buffer (the caller owns the buffers and their mappings).
+struct wg_tp;
 struct wg_comm {
   int device;
   int world, rank;
   size_t bytes;
   wg::CommDev dev;
+  // set by wg_tp_comm, which owns the buffers: released by wg_comm_destroy
+  wg_tp *tp = nullptr;
+  void *own = nullptr;
+  void *opened[wg::kCommMaxRanks] = {};
 };
+
+// Releases the buffers of a communicator made by wg_tp_comm (tp_nccl.cu).
+int wg_tp_comm_release(wg_ctx *ctx, wg_comm *comm);
 
 struct wg_q4mat {
   wg::Q4Dims d;

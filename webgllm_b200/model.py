@@ -11,9 +11,10 @@ quantised to Q4_0 by the llama.cpp rule on the device.
 A decode step is captured once as a CUDA graph and replayed: the token ids
 (argmax) and the positions live on the device, so no host round trip is
 needed between tokens. `batch` independent sequences decode together (one
-row each), and with `tp` the model is split across the GPUs of a node
-(webgllm_b200.tp): two NCCL all-reduces per layer and one for the greedy
-pick.
+row each), and with `tp` (a webgllm_b200.comm.TensorGroup) the model is split
+across the GPUs of a node (webgllm_b200.tp): per layer two row-parallel sums
+(the push exchange for decode rows, NCCL's all-reduce through the library
+for prompt rows) and one MAX all-reduce for the greedy pick.
 """
 from __future__ import annotations
 
@@ -129,7 +130,7 @@ class DecoderModel:
     """Weights, caches and the forward pass of one decoder on one GPU (or on
     this rank's GPU of a tensor-parallel group).
 
-    tp: None, or (rank, world, process_group) of an NCCL group; every rank
+    tp: None, or this rank's webgllm_b200.comm.TensorGroup; every rank
     draws the same full random weights and keeps its shard (webgllm_b200.tp),
     so the model is the same for every world size."""
 
@@ -141,7 +142,8 @@ class DecoderModel:
         self.batch = batch
         self.ctx = context(device)
         self.max_ctx, self.max_rows = max_ctx, max_rows
-        rank, world, self.group = tp if tp else (0, 1, None)
+        self.group = tp
+        rank, world = (tp.rank, tp.world) if tp is not None else (0, 1)
         self.world = world
         sh = self.shard = TP.plan(cfg, rank, world) if world > 1 else None
         g = torch.Generator(device="cuda")
@@ -222,9 +224,7 @@ class DecoderModel:
         # for the rest (and for everything when push is False)
         self.comm = None
         if world > 1 and push:
-            from .comm import PushComm
-
-            self.comm = PushComm(self.ctx, rank, world, self.group)
+            self.comm = tp.push_comm()
 
     # -- low level ---------------------------------------------------------
 
@@ -237,11 +237,9 @@ class DecoderModel:
         yd = WG_F16 if y.dtype == torch.float16 else WG_F32
         self._c(L.wg_q4_matmul(P(self.ctx.handle), P(lin.m.handle), P(x.data_ptr()), xd, rows, P(y.data_ptr()), yd))
 
-    def _all_reduce(self, t: torch.Tensor, op=None):
+    def _all_reduce(self, t: torch.Tensor, op: str = "sum"):
         if self.world > 1:
-            import torch.distributed as dist
-
-            dist.all_reduce(t, op=op or dist.ReduceOp.SUM, group=self.group)
+            self.group.all_reduce(t, op)
 
     def reset(self):
         self.pos.zero_()
@@ -361,9 +359,7 @@ class DecoderModel:
                                   P(None if sharded else self.next_id.data_ptr()),
                                   P(self.keys.data_ptr() if sharded else None)))
         if sharded:
-            import torch.distributed as dist
-
-            self._all_reduce(self.keys, dist.ReduceOp.MAX)
+            self._all_reduce(self.keys, "max")
             self._c(L.wg_pick_keys(c, P(self.keys.data_ptr()), B, P(self.next_id.data_ptr())))
         if self.row_picks is not None:
             self.row_picks[last].copy_(self.next_id)
