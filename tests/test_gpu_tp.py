@@ -134,6 +134,44 @@ def _push_worker(rank, world, gid, q):
     q.put((rank, max(errs), xerr))
 
 
+def _spec_worker(rank, world, gid, q, same_draft):
+    """Speculative decoding with the target split over the group: the verify
+    rows go through the row-parallel GEMM and NCCL sums, the per-row picks
+    through one MAX all-reduce; the draft runs whole on each rank (or, with
+    the target's weights, split like it)."""
+    ctx, group = _group(rank, world, gid)
+    from webgllm_b200.model import DecoderConfig, DecoderModel
+    from webgllm_b200.speculative import SpeculativeDecoder
+
+    cfg = _cfg()
+    dcfg = DecoderConfig("tiny-draft", 2, 256, 4, 2, 64, 512, 1000, 1e-5, 1e4)
+    B, k, n_new = 2, 4, 20
+    prompts = torch.randint(0, cfg.vocab, (B, 16), generator=torch.Generator().manual_seed(5)).cuda().to(torch.int32)
+    t = DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=B, tp=group)
+    d = (DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=B, tp=group) if same_draft
+         else DecoderModel(dcfg, seed=8, max_ctx=128, max_rows=64, batch=B))
+    spec = SpeculativeDecoder(t, d, k=k, max_new=64)
+    spec.prefill(prompts)
+    spec.step()  # eager round configures every kernel
+    spec.capture()
+    rounds = 1
+    while int(spec.out_len.min().item()) < n_new and rounds < 40:
+        spec.run_step()
+        rounds += 1
+    torch.cuda.synchronize()
+    got = spec.out[:, :n_new].cpu()
+    acc = spec.accepted.cpu().tolist()
+    spec.graph = None
+    t.close()
+    d.close()
+    if rank == 0:
+        plain = DecoderModel(cfg, seed=7, max_ctx=128, max_rows=64, batch=B)
+        want = plain.generate(prompts, n_new, use_graph=False).cpu()
+        q.put((torch.equal(got, want), acc, rounds))
+    group.barrier(60000)
+    group.close()
+
+
 def _spawn(target, extra=()):
     from webgllm_b200.comm import unique_id
 
@@ -167,3 +205,12 @@ def test_tp2_decodes_like_one_gpu(push, trigger):
     err, same = q.get(timeout=10)
     assert err < 2e-2, err
     assert all(same), same
+
+
+@pytest.mark.parametrize("same_draft", [False, True])
+def test_tp2_speculative_decoding_emits_one_gpu_greedy_tokens(same_draft):
+    q = _spawn(_spec_worker, (same_draft,))
+    same, acc, rounds = q.get(timeout=10)
+    assert same
+    if same_draft:
+        assert acc == [4 * rounds] * 2, (acc, rounds)

@@ -220,6 +220,7 @@ class DecoderModel:
         # speculative verification: greedy picks after every row of each
         # sequence, [rows per sequence][batch] (None: the last row only)
         self.row_picks = None
+        self.row_keys = None  # their packed keys under tensor parallelism, [rows per sequence][batch]
         # row-parallel exchange: the push all-reduce for decode rows, NCCL
         # for the rest (and for everything when push is False)
         self.comm = None
@@ -345,24 +346,35 @@ class DecoderModel:
         B, rps = self.batch, rows // self.batch
         last = rps - 1
         sharded = self.world > 1
+
+        def head(j, argmax, keys):
+            self._c(L.wg_head_rmsnorm(c, P(cur[j].data_ptr()), P(add[j].data_ptr() if add is not None else None),
+                                      P(self.final_norm.data_ptr()), cfg.eps, B, rps, cfg.hidden,
+                                      P(self.head.data_ptr()), self.V, self.vocab_offset, P(self.logits.data_ptr()),
+                                      P(argmax), P(keys)))
+
         if self.row_picks is not None:
+            # speculative verification: a pick after every row of each
+            # sequence (the last row's logits stay in self.logits); sharded,
+            # every row's packed keys go through one MAX all-reduce
             if sharded:
-                raise ValueError("speculative verification runs on one GPU")
-            for j in range(rps - 1):  # every row but the last: its pick only
-                self._c(L.wg_head_rmsnorm(c, P(cur[j].data_ptr()), P(add[j].data_ptr() if add is not None else None),
-                                          P(self.final_norm.data_ptr()), cfg.eps, B, rps, cfg.hidden,
-                                          P(self.head.data_ptr()), self.V, self.vocab_offset,
-                                          P(self.logits.data_ptr()), P(self.row_picks[j].data_ptr()), None))
-        self._c(L.wg_head_rmsnorm(c, P(cur[last].data_ptr()), P(add[last].data_ptr() if add is not None else None),
-                                  P(self.final_norm.data_ptr()), cfg.eps, B, rps, cfg.hidden,
-                                  P(self.head.data_ptr()), self.V, self.vocab_offset, P(self.logits.data_ptr()),
-                                  P(None if sharded else self.next_id.data_ptr()),
-                                  P(self.keys.data_ptr() if sharded else None)))
-        if sharded:
+                if self.row_keys is None or self.row_keys.shape[0] < rps:
+                    self.row_keys = torch.zeros((rps, B), dtype=torch.int64, device="cuda")
+                keys = self.row_keys[:rps]
+                for j in range(rps):
+                    head(j, None, keys[j].data_ptr())
+                self._all_reduce(keys, "max")
+                self._c(L.wg_pick_keys(c, P(keys.data_ptr()), rps * B, P(self.row_picks.data_ptr())))
+            else:
+                for j in range(rps):
+                    head(j, self.row_picks[j].data_ptr(), None)
+            self.next_id.copy_(self.row_picks[last])
+        elif sharded:
+            head(last, None, self.keys.data_ptr())
             self._all_reduce(self.keys, "max")
             self._c(L.wg_pick_keys(c, P(self.keys.data_ptr()), B, P(self.next_id.data_ptr())))
-        if self.row_picks is not None:
-            self.row_picks[last].copy_(self.next_id)
+        else:
+            head(last, self.next_id.data_ptr(), None)
         self._c(L.wg_add_i32(c, P(self.pos.data_ptr()), B, rps))
 
     def _forward_fused(self, ids: torch.Tensor, rows: int):

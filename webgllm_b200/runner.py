@@ -91,17 +91,29 @@ def measure(cfg, batch: int, prompt_len: int, gen_len: int, tp=None, seed: int =
     return res
 
 
-def measure_speculative(cfg, batch: int, prompt_len: int, gen_len: int, k: int = 4, seed: int = 0) -> dict:
-    """Config 4's speculative workload on one GPU: a random-init draft of
-    config 2's layout (the target's vocabulary) proposes k tokens a round.
-    With independent random weights the draft almost never agrees with the
-    target, so a round yields about one token per sequence: the acceptance
-    rate is reported with the throughput."""
+def measure_speculative(cfg, batch: int, prompt_len: int, gen_len: int, k: int = 4, seed: int = 0, tp=None,
+                        same_draft: bool = False, barrier=None) -> dict:
+    """Config 4's speculative workload: a random-init draft of config 2's
+    layout (the target's vocabulary) proposes k tokens a round and the
+    target verifies them. With independent random weights the draft almost
+    never agrees with the target, so a round yields about one token per
+    sequence: the acceptance rate is reported with the throughput.
+    same_draft: the draft is a copy of the target (same config and seed), so
+    every proposal is accepted: the machinery's upper bound.
+    tp: the target is split across the group (its verify rows go through
+    the row-parallel GEMM and NCCL sums, the picks through one MAX
+    all-reduce); the 1.1B draft runs whole on every rank (its 4 KV heads do
+    not split 8 ways, and it is small), the same-weights draft split like
+    the target."""
     from .speculative import SpeculativeDecoder, draft_config
 
     ctx_len = prompt_len + gen_len + 2 * (k + 1) + 8
-    t = DecoderModel(cfg, seed=seed, max_ctx=ctx_len, max_rows=batch * prompt_len, batch=batch)
-    d = DecoderModel(draft_config(cfg), seed=seed + 100, max_ctx=ctx_len, max_rows=batch * prompt_len, batch=batch)
+    t = DecoderModel(cfg, seed=seed, max_ctx=ctx_len, max_rows=batch * prompt_len, batch=batch, tp=tp)
+    if same_draft:
+        d = DecoderModel(cfg, seed=seed, max_ctx=ctx_len, max_rows=batch * prompt_len, batch=batch, tp=tp)
+    else:
+        d = DecoderModel(draft_config(cfg), seed=seed + 100, max_ctx=ctx_len, max_rows=batch * prompt_len,
+                         batch=batch)
     spec = SpeculativeDecoder(t, d, k=k, max_new=gen_len)
     g = torch.Generator().manual_seed(seed + 1)
     prompts = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=g).to("cuda", torch.int32)
@@ -111,6 +123,8 @@ def measure_speculative(cfg, batch: int, prompt_len: int, gen_len: int, k: int =
     t.reset()
     d.reset()
     torch.cuda.synchronize()
+    if barrier:
+        barrier()
     s = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     ev[0].record(s)
@@ -126,16 +140,23 @@ def measure_speculative(cfg, batch: int, prompt_len: int, gen_len: int, k: int =
             break
     ev[2].record(s)
     torch.cuda.synchronize()
+    if barrier:
+        barrier()
     prefill_ms = ev[0].elapsed_time(ev[1])
     decode_ms = ev[1].elapsed_time(ev[2])
     produced = int(spec.out_len.sum().item()) - batch  # after the prefill's token
+    out = spec.out[:, :gen_len].cpu()
     res = {
-        "model": cfg.name, "draft": d.cfg.name, "k": k, "batch": batch, "rounds": rounds,
+        "model": cfg.name, "draft": d.cfg.name + (" (the target's weights)" if same_draft else ""), "k": k,
+        "batch": batch, "rounds": rounds, "tp": t.world,
         "decode_ms_per_round": decode_ms / rounds, "decode_tok_s": produced / (decode_ms / 1e3),
         "acceptance": float(spec.accepted.sum().item()) / (rounds * batch * k),
-        "prefill_ms": prefill_ms,
+        "prefill_ms": prefill_ms, "tokens": out,
+        "tokens_sha256": hashlib.sha256(out.numpy().astype("<i4").tobytes()).hexdigest(),
     }
     spec.graph = None
+    t.close()
+    d.close()
     del spec, t, d
     torch.cuda.empty_cache()
     return res
