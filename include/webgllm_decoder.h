@@ -84,6 +84,23 @@ int wg_swiglu_pairs(wg_ctx *ctx, const float *gate_up, int rows, int I, void *ou
 int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int batch, int D, int W, const float *weight,
                   void *state, void *out, int out_dtype);
 
+/* wg_short_conv that also keeps the state after each prefix of a
+ * sequence's rows (convPrefixes, src/gpu/kernels.ts:1504 and
+ * src/engine.ts:5902, for speculative decoding, which may keep only some of
+ * a draft batch's tokens): prefixes fp16 [batch][slots][W-1][D], slot
+ * slot0 + p - 1 = the state after the first p rows (p = 1 .. rows/batch;
+ * slot0 + rows/batch <= slots). A draft model decoding one row at a time
+ * passes slot0 = its step index. W >= 2. */
+int wg_short_conv_prefixes(wg_ctx *ctx, const float *bcx, int rows, int batch, int D, int W, const float *weight,
+                           void *state, void *out, int out_dtype, void *prefixes, int slot0, int slots);
+
+/* The conv-state rollback of accept (src/engine.ts:8063-8085): per sequence,
+ * kept = pos_after[b] - pos_before[b] tokens of the last `slots`-token draft
+ * batch were kept; when 1 <= kept < slots, state[b] = prefixes[b][kept-1]
+ * (positions on the device, as wg_spec_accept leaves them). */
+int wg_conv_restore(wg_ctx *ctx, const void *prefixes, int slots, int batch, int D, int W, const int32_t *pos_before,
+                    const int32_t *pos_after, void *state);
+
 /* fp16 output head (head, src/engine.ts:8557): logits fp32 [rows][V] =
  * x fp16 [rows][D] . W^T, W fp16 [V][D]; rows <= 8, D % 8 == 0,
  * rows * D <= 51200. If `argmax` is not NULL it also receives each row's
@@ -115,8 +132,8 @@ int wg_argmax(wg_ctx *ctx, const float *logits, int rows, int V, int32_t *out);
 /* Greedy speculative decoding: acceptance of a draft's k proposals per
  * sequence (forwardDraft / accept, src/engine.ts:8035,8063: keys and values
  * past the kept rows are never read before they are written again, so the
- * rollback is the position alone; conv-state prefixes are not kept here, so
- * this serves attention-only models). drafts [batch][k] = the draft's tokens d_1..d_k;
+ * rollback is the position alone for attention layers; conv layers restore
+ * their state with wg_conv_restore). drafts [batch][k] = the draft's tokens d_1..d_k;
  * picks [k+1][batch] = the target's greedy picks after each verified row
  * (rows: the last kept token, then d_1..d_k). Keeps the longest prefix with
  * d_{j+1} == picks[j], appends it and the target's pick after it to

@@ -628,3 +628,47 @@ def test_speculative_decoding_emits_the_target_greedy_tokens(same_draft):
         # every round keeps all k proposals and adds the target's own token
         assert spec.accepted.tolist() == [k * rounds] * B
         assert spec.out_len.tolist() == [1 + (k + 1) * rounds] * B
+
+
+@pytest.mark.parametrize("draft_kind", ["independent", "perturbed", "same"])
+def test_hybrid_speculative_decoding_rolls_back_the_conv_state(draft_kind):
+    """The hybrid (gated short conv + attention) target and draft under
+    speculative decoding: every draft step and the target's verify batch keep
+    the conv state after each token (wg_short_conv_prefixes) and accept sets
+    it back to the kept prefix's (wg_conv_restore; convPrefixes / accept,
+    src/gpu/kernels.ts:1504, src/engine.ts:8063). The emitted tokens equal
+    the target's plain greedy continuation whether the draft never agrees
+    (rollback to one token every round), agrees sometimes (a copy of the
+    target with its final norm perturbed: rollbacks to varying prefixes) or
+    always (nothing to roll back)."""
+    from webgllm_b200.model import DecoderConfig, DecoderModel
+    from webgllm_b200.speculative import SpeculativeDecoder
+
+    cfg = small_config(True)
+    B, k, n_new = 2, 4, 28
+    prompts = torch.randint(0, cfg.vocab, (B, 12), generator=gen(31), device="cuda").to(torch.int32)
+    plain = DecoderModel(cfg, seed=13, max_ctx=128, max_rows=64, batch=B)
+    want = plain.generate(prompts, n_new, use_graph=False)
+    t = DecoderModel(cfg, seed=13, max_ctx=128, max_rows=64, batch=B)
+    if draft_kind == "independent":
+        dcfg = DecoderConfig("tiny-hybrid-draft", 2, 128, 2, 1, 64, 256, 1000, 1e-5, 1e6, ["conv", "attn"], 3, True)
+        d = DecoderModel(dcfg, seed=14, max_ctx=128, max_rows=64, batch=B)
+    else:
+        d = DecoderModel(cfg, seed=13, max_ctx=128, max_rows=64, batch=B)
+        if draft_kind == "perturbed":
+            d.final_norm.mul_(1.0 + 2.0 * torch.rand(cfg.hidden, generator=gen(15), device="cuda"))
+    spec = SpeculativeDecoder(t, d, k=k, max_new=96)
+    spec.prefill(prompts)
+    spec.step()
+    spec.capture()
+    rounds = 1
+    while int(spec.out_len.min().item()) < n_new and rounds < 60:
+        spec.run_step()
+        rounds += 1
+    torch.cuda.synchronize()
+    assert torch.equal(spec.out[:, :n_new], want), (spec.out[:, :n_new], want)
+    acc = spec.accepted.tolist()
+    if draft_kind == "same":
+        assert acc == [k * rounds] * B
+    elif draft_kind == "perturbed":
+        assert 0 < sum(acc) < k * rounds * B, (acc, rounds)  # partial prefixes were kept

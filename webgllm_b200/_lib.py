@@ -72,6 +72,8 @@ SIGNATURES = {
     "wg_swiglu": (_I, [_P, _P, _I, _I, _P, _I]),
     "wg_swiglu_pairs": (_I, [_P, _P, _I, _I, _P, _I]),
     "wg_short_conv": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
+    "wg_short_conv_prefixes": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _P, _I, _I]),
+    "wg_conv_restore": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "wg_head": (_I, [_P, _P, _I, _I, _P, _I, _P, _P]),
     "wg_head_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _I, _P, _I, _I, _P, _P, _P]),
     "wg_pick_keys": (_I, [_P, _P, _I, _P]),

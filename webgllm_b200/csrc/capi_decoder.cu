@@ -140,8 +140,40 @@ int wg_short_conv(wg_ctx *ctx, const float *bcx, int rows, int batch, int D, int
   if (!bcx || !weight || !state || !out || !dtype_ok(out_dtype))
     return dfail(ctx, WG_INVALID_ARGUMENT, "wg_short_conv: argument");
   return finish(ctx,
-                wg::launch_short_conv(bcx, rows, batch, D, W, weight, state, out, out_dtype, ctx->stream, ctx->pdl),
+                wg::launch_short_conv(bcx, rows, batch, D, W, weight, state, out, out_dtype, nullptr, 0, 0,
+                                      ctx->stream, ctx->pdl),
                 "wg_short_conv");
+}
+
+int wg_short_conv_prefixes(wg_ctx *ctx, const float *bcx, int rows, int batch, int D, int W, const float *weight,
+                           void *state, void *out, int out_dtype, void *prefixes, int slot0, int slots) {
+  WG_BEGIN(ctx);
+  if (rows < 0 || D <= 0 || W < 2 || W > 8) return dfail(ctx, WG_INVALID_SHAPE, "wg_short_conv_prefixes: bad shape");
+  if (!rows) return WG_OK;
+  if (int st = check_batch(ctx, "wg_short_conv_prefixes", rows, batch)) return st;
+  if (!bcx || !weight || !state || !out || !prefixes || !dtype_ok(out_dtype))
+    return dfail(ctx, WG_INVALID_ARGUMENT, "wg_short_conv_prefixes: argument");
+  if (slot0 < 0 || slots < 1 || slot0 + rows / batch > slots)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_short_conv_prefixes: %d rows a sequence from slot %d of %d", rows / batch,
+                 slot0, slots);
+  return finish(ctx,
+                wg::launch_short_conv(bcx, rows, batch, D, W, weight, state, out, out_dtype, prefixes, slot0, slots,
+                                      ctx->stream, ctx->pdl),
+                "wg_short_conv_prefixes");
+}
+
+int wg_conv_restore(wg_ctx *ctx, const void *prefixes, int slots, int batch, int D, int W, const int32_t *pos_before,
+                    const int32_t *pos_after, void *state) {
+  WG_BEGIN(ctx);
+  if (batch < 0 || D <= 0 || W < 2 || W > 8 || slots < 1)
+    return dfail(ctx, WG_INVALID_SHAPE, "wg_conv_restore: bad shape");
+  if (!batch) return WG_OK;
+  if (!prefixes || !pos_before || !pos_after || !state)
+    return dfail(ctx, WG_INVALID_ARGUMENT, "wg_conv_restore: argument");
+  return finish(ctx,
+                wg::launch_conv_restore(prefixes, slots, batch, D, W, pos_before, pos_after, state, ctx->stream,
+                                        ctx->pdl),
+                "wg_conv_restore");
 }
 
 static int check_head(wg_ctx *ctx, int rows, int D, int V) {

@@ -589,7 +589,7 @@ constexpr int kMaxConvWidth = 8;
 constexpr int kConvRows = 16;
 
 __global__ void short_conv_kernel(const float *bcx, int rows, int cps, int D, int W, const float *w, __half *state,
-                                  void *out, int out_dtype) {
+                                  void *out, int out_dtype, __half *prefixes, int slot0, int slots) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
   pdl_wait();     // inputs come from the previous kernel
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -629,6 +629,26 @@ __global__ void short_conv_kernel(const float *bcx, int rows, int cps, int D, in
     for (int k = 0; k < kMaxConvWidth; k++)
       if (k < W) a += wk[k] * y[i + k];
     store_out(out, out_dtype, (size_t)(r0 + i) * D + c, cg_[i] * a);
+  }
+  if (prefixes && chunk == 0 && W > 1) {
+    // the state after each prefix of p = 1 .. rows rows (convPrefixes,
+    // src/gpu/kernels.ts:1504): row i is y at t = p - (W-1) + i, the old
+    // state for t < 0; into slot slot0 + p - 1 of this sequence (written
+    // before the state itself is replaced)
+    __half *pf = prefixes + (size_t)seq * slots * (W - 1) * D;
+    for (int pp = 1; pp <= rows && slot0 + pp - 1 < slots; pp++) {
+      for (int i = 0; i < W - 1; i++) {
+        const int t = pp - (W - 1) + i;
+        float v;
+        if (t < 0) {
+          v = __half2float(state[(size_t)(W - 1 + t) * D + c]);
+        } else {
+          const float *row = bcx + (size_t)t * 3 * D;
+          v = row[c] * row[2 * D + c];
+        }
+        pf[((size_t)(slot0 + pp - 1) * (W - 1) + i) * D + c] = __float2half_rn(v);
+      }
+    }
   }
   if (chunk == 0 && W > 1) {
     // new state: y at rows rows-(W-1) .. rows-1 (old state for negative rows)
@@ -1196,12 +1216,41 @@ cudaError_t launch_swiglu_pairs(const float *gu, int rows, int I, void *out, int
 }
 
 cudaError_t launch_short_conv(const float *bcx, int rows, int batch, int D, int W, const float *w, void *state,
-                              void *out, int out_dtype, cudaStream_t s, bool pdl) {
+                              void *out, int out_dtype, void *prefixes, int slot0, int slots, cudaStream_t s,
+                              bool pdl) {
   if (W < 1 || W > kMaxConvWidth) return cudaErrorInvalidValue;
   const int rps = rows / batch, cps = (rps + kConvRows - 1) / kConvRows;
   const dim3 grid((D + 127) / 128, batch * cps);
   return launch_k(short_conv_kernel, grid, dim3(128), 0, s, pdl, bcx, rps, cps, D, W, w,
-                  reinterpret_cast<__half *>(state), out, out_dtype);
+                  reinterpret_cast<__half *>(state), out, out_dtype, reinterpret_cast<__half *>(prefixes), slot0,
+                  slots);
+}
+
+// The rollback of speculative accept (accept, src/engine.ts:8063-8085): per
+// sequence, kept = pos_after - pos_before tokens of the last draft batch were
+// kept; unless that is all `slots` of them, the state becomes the saved
+// state after the kept prefix.
+__global__ void conv_restore_kernel(const __half *prefixes, int slots, int D, int W, const int32_t *pos_before,
+                                    const int32_t *pos_after, __half *state) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.y;
+  const int kept = pos_after[b] - pos_before[b];
+  if (kept < 1 || kept >= slots) return;
+  const size_t n = (size_t)(W - 1) * D;
+  const __half *src = prefixes + ((size_t)b * slots + kept - 1) * n;
+  __half *dst = state + (size_t)b * n;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+cudaError_t launch_conv_restore(const void *prefixes, int slots, int batch, int D, int W, const int32_t *pos_before,
+                                const int32_t *pos_after, void *state, cudaStream_t s, bool pdl) {
+  if (W < 2 || W > kMaxConvWidth || slots < 1) return cudaErrorInvalidValue;
+  const int n = (W - 1) * D;
+  const dim3 grid((n + 255) / 256 < 64 ? (n + 255) / 256 : 64, batch);
+  return launch_k(conv_restore_kernel, grid, dim3(256), 0, s, pdl, reinterpret_cast<const __half *>(prefixes), slots,
+                  D, W, pos_before, pos_after, reinterpret_cast<__half *>(state));
 }
 
 cudaError_t launch_head(const void *x, const float *na, const float *nb, const float *nw, float eps, int rows,

@@ -36,8 +36,13 @@ cudaError_t launch_rope_attention(const float *qkv, int batch, int H, int Hkv, i
 cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s, bool pdl);
 cudaError_t launch_swiglu_pairs(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s,
                                 bool pdl);
+// prefixes (nullable): fp16 [batch][slots][W-1][D], the state after each
+// prefix of a sequence's rows into slots slot0 ...
 cudaError_t launch_short_conv(const float *bcx, int rows, int batch, int D, int W, const float *w, void *state,
-                              void *out, int out_dtype, cudaStream_t s, bool pdl);
+                              void *out, int out_dtype, void *prefixes, int slot0, int slots, cudaStream_t s,
+                              bool pdl);
+cudaError_t launch_conv_restore(const void *prefixes, int slots, int batch, int D, int W, const int32_t *pos_before,
+                                const int32_t *pos_after, void *state, cudaStream_t s, bool pdl);
 // x fp16 [rows][D], or with na != null the norm rmsnorm(na + nb) * nw; input
 // row r is row r * row_stride of x / na / nb.
 cudaError_t launch_head(const void *x, const float *na, const float *nb, const float *nw, float eps, int rows,

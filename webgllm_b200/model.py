@@ -221,6 +221,11 @@ class DecoderModel:
         # sequence, [rows per sequence][batch] (None: the last row only)
         self.row_picks = None
         self.row_keys = None  # their packed keys under tensor parallelism, [rows per sequence][batch]
+        # speculative decoding of conv models: the conv state after each draft
+        # token ([conv layers][batch][slots][W-1][D]) and where this forward's
+        # first row goes (None: not kept)
+        self.conv_prefixes = None
+        self.prefix_slot = None
         # row-parallel exchange: the push all-reduce for decode rows, NCCL
         # for the rest (and for everything when push is False)
         self.comm = None
@@ -334,10 +339,46 @@ class DecoderModel:
 
     def _convolve(self, lay, rows):
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
-        self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, self.batch, cfg.hidden, cfg.conv_width,
-                                P(lay["conv_w"].data_ptr()), P(self.conv_state[lay["slot"]].data_ptr()),
-                                P(self.cv.data_ptr()), WG_F16))
+        s = lay["slot"]
+        if self.prefix_slot is not None:
+            # a draft batch: keep the state after each prefix (speculative accept)
+            self._c(L.wg_short_conv_prefixes(c, P(self.bcx.data_ptr()), rows, self.batch, cfg.hidden,
+                                             cfg.conv_width, P(lay["conv_w"].data_ptr()),
+                                             P(self.conv_state[s].data_ptr()), P(self.cv.data_ptr()), WG_F16,
+                                             P(self.conv_prefixes[s].data_ptr()), self.prefix_slot,
+                                             self.conv_prefixes.shape[2]))
+        else:
+            self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, self.batch, cfg.hidden, cfg.conv_width,
+                                    P(lay["conv_w"].data_ptr()), P(self.conv_state[s].data_ptr()),
+                                    P(self.cv.data_ptr()), WG_F16))
         self._mm(lay["out"], self.cv, self.o, rows)
+
+    @property
+    def has_conv(self) -> bool:
+        return any(t == "conv" for t in self.cfg.layer_types)
+
+    def keep_prefixes(self, slots: int):
+        """Buffers for the conv state after each of `slots` draft tokens
+        (speculative decoding; nothing for attention-only models)."""
+        if self.has_conv and (self.conv_prefixes is None or self.conv_prefixes.shape[2] != slots):
+            n, B, W1, D = self.conv_state.shape
+            self.conv_prefixes = torch.zeros((n, B, slots, W1, D), dtype=torch.float16, device="cuda")
+
+    def restore_prefix(self, pos_before: torch.Tensor):
+        """After speculative accept: each conv layer's state becomes the one
+        after the kept prefix of the last draft batch (kept = self.pos -
+        pos_before per sequence, on the device)."""
+        if not self.has_conv:
+            return
+        cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
+        slots = self.conv_prefixes.shape[2]
+        for lay in self.layers:
+            if lay["type"] != "conv":
+                continue
+            s = lay["slot"]
+            self._c(L.wg_conv_restore(c, P(self.conv_prefixes[s].data_ptr()), slots, self.batch, cfg.hidden,
+                                      cfg.conv_width, P(pos_before.data_ptr()), P(self.pos.data_ptr()),
+                                      P(self.conv_state[s].data_ptr())))
 
     def _head(self, cur, add, rows):
         """Final norm + head on each sequence's last row, greedy pick, and the

@@ -8,9 +8,12 @@ greedy picks, from the last kept token; the extra step puts d_k in its cache
 for when every proposal is kept), the target reads the last kept token and
 d_1..d_k as k + 1 rows per sequence and picks after every row, and
 wg_spec_accept keeps the longest agreeing prefix plus the target's own next
-token, rewinding both models' positions (the caches are indexed by
-position, so nothing else is undone). The emitted tokens are exactly the
-target's greedy continuation, whatever the draft proposes.
+token, rewinding both models' positions (the KV caches are indexed by
+position, so nothing else is undone there); models with gated short-conv
+layers (config 3's hybrid) keep their conv state after every draft token
+(wg_short_conv_prefixes) and set it back to the kept prefix's
+(wg_conv_restore). The emitted tokens are exactly the target's greedy
+continuation, whatever the draft proposes.
 """
 from __future__ import annotations
 
@@ -43,6 +46,13 @@ class SpeculativeDecoder:
         self.out = torch.zeros((B, max_new + k + 1), dtype=torch.int32, device="cuda")
         self.out_len = torch.zeros(B, dtype=torch.int32, device="cuda")
         self.accepted = torch.zeros(B, dtype=torch.int32, device="cuda")
+        # conv models roll their state back to the kept prefix (convPrefixes /
+        # accept, src/gpu/kernels.ts:1504, src/engine.ts:8063): positions
+        # before the round, and the state after each of the k + 1 draft tokens
+        self.pos_t0 = torch.zeros(B, dtype=torch.int32, device="cuda")
+        self.pos_d0 = torch.zeros(B, dtype=torch.int32, device="cuda")
+        target.keep_prefixes(k + 1)
+        draft.keep_prefixes(k + 1)
         self.graph = None
 
     def prefill(self, prompts: torch.Tensor):
@@ -60,21 +70,33 @@ class SpeculativeDecoder:
         """One draft-and-verify round (every sequence gains 1 .. k + 1 tokens)."""
         t, d, k = self.t, self.d, self.k
         self.ver[:, 0].copy_(t.next_id)
+        if d.has_conv:
+            self.pos_d0.copy_(d.pos)
+        if t.has_conv:
+            self.pos_t0.copy_(t.pos)
         for j in range(k + 1):
-            d.decode_step()
+            d.prefix_slot = j if d.has_conv else None
+            try:
+                d.decode_step()
+            finally:
+                d.prefix_slot = None
             if j < k:
                 self.drafts[:, j].copy_(d.next_id)
                 self.ver[:, j + 1].copy_(d.next_id)
         t.row_picks = self.picks
+        t.prefix_slot = 0 if t.has_conv else None
         try:
             t.forward(self.ver.reshape(-1), t.batch * (k + 1))
         finally:
             t.row_picks = None
+            t.prefix_slot = None
         L = _lib.lib()
         t._c(L.wg_spec_accept(P(t.ctx.handle), P(self.drafts.data_ptr()), P(self.picks.data_ptr()), t.batch, k,
                               P(t.pos.data_ptr()), P(d.pos.data_ptr()), P(t.next_id.data_ptr()),
                               P(d.next_id.data_ptr()), P(self.out.data_ptr()), self.out.shape[1],
                               P(self.out_len.data_ptr()), P(self.accepted.data_ptr())))
+        t.restore_prefix(self.pos_t0)
+        d.restore_prefix(self.pos_d0)
 
     def capture(self):
         """Records step() as one CUDA graph (after one eager step)."""
