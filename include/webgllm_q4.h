@@ -69,6 +69,18 @@ int wg_destroy(wg_ctx *ctx);
  * stream: to share that one, pass cudaStreamLegacy). No reference
  * counterpart: WebGL has one implicit queue. */
 int wg_set_stream(wg_ctx *ctx, void *stream);
+
+/* Context options (wg_set_option). */
+/* Matmuls of up to this many rows (default 16; 0 .. 256) run on the decode
+ * GEMV, in launches of up to 32 rows: exact weights, fp32 block scaling —
+ * the reference's split-path arithmetic, which serves its decode rows and
+ * its speculative draft batches (src/engine.ts:4684, forwardDraft :8036);
+ * more rows go to the tensor-core GEMM, whose weights are rounded to fp16 as
+ * the reference's f16 prompt route rounds them (src/gpu/kernels.ts:467).
+ * A speculative verify batch raises it to its rows so that its picks use the
+ * arithmetic of the decode steps they check. */
+#define WG_OPT_EXACT_ROWS 1
+int wg_set_option(wg_ctx *ctx, int option, int value);
 /* Gpu.texture (src/gpu/gl.ts:263): `bytes` of device memory. */
 int wg_alloc(wg_ctx *ctx, size_t bytes, void **dptr);
 /* Gpu.delete (src/gpu/gl.ts:448). */
@@ -147,11 +159,13 @@ int wg_q4_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype,
  * a CUDA graph (no allocation is allowed during stream capture), engines that
  * budget device memory up front, and decode loops that cannot afford the
  * device synchronisation of cudaMalloc / cudaFree. Its scratch (the fp16
- * copy of an f32 / bf16 x and the GEMM's split-K partial sums) is one fixed
+ * copy of an f32 / bf16 x that the GEMM reads) is one fixed
  * 32 MiB array in the library's device memory, held on every GPU that loads
  * the library until the process exits; a call that would need more returns
  * WG_UNSUPPORTED and says how much. The first call on a device looks up the
- * array's device address: make it before capturing a stream. All calls on a
+ * array's device address (kept for the process's life: do not call it again
+ * after a cudaDeviceReset of that device); make it before capturing a
+ * stream. All calls on a
  * device share the array, so calls whose work overlaps on the GPU (other
  * streams or contexts of the same device) race on it. */
 int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x,

@@ -108,6 +108,11 @@ class ReferenceDecoder:
     in torch fp32, from the model's own weights (`weights` from
     reference_weights(model), or made here)."""
 
+    # Matmuls of this many rows or more run on the library's tensor-core
+    # GEMM, whose weights are rounded to fp16 ((q - z) * d, as the reference's
+    # f16 prompt route rounds them): the restatement rounds them too.
+    GEMM_ROWS = 17
+
     def __init__(self, model, weights=None):
         self.m = model
         cfg = model.cfg
@@ -131,6 +136,8 @@ class ReferenceDecoder:
         add = None
         for li, L in enumerate(m.layers):
             W = self.W[li]
+            if rows >= self.GEMM_ROWS:
+                W = {k: v.half().float() for k, v in W.items()}
             x, h = rmsnorm(x, add, L["norm1"], cfg.eps)
             h = h.half().float()
             if L["type"] == "attn":

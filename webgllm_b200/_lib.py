@@ -26,6 +26,7 @@ WG_NO_DEVICE = 10
 WG_F32, WG_F16, WG_BF16 = 0, 1, 2
 WG_PRO_RMSNORM, WG_PRO_SWIGLU = 1, 2
 WG_EPI_SWIGLU_PAIRS = 1
+WG_OPT_EXACT_ROWS = 1
 
 
 class wg_prologue(ctypes.Structure):
@@ -43,6 +44,7 @@ SIGNATURES = {
     "wg_init": (_I, [_I, _PP]),
     "wg_destroy": (_I, [_P]),
     "wg_set_stream": (_I, [_P, _P]),
+    "wg_set_option": (_I, [_P, _I, _I]),
     "wg_alloc": (_I, [_P, _SZ, _PP]),
     "wg_free": (_I, [_P, _P]),
     "wg_host_alloc": (_I, [_P, _SZ, _PP]),

@@ -190,6 +190,18 @@ int wg_init(int device, wg_ctx **out) {
   return WG_OK;
 }
 
+int wg_set_option(wg_ctx *ctx, int option, int value) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  switch (option) {
+    case WG_OPT_EXACT_ROWS:
+      if (value < 0 || value > 256) return fail(ctx, WG_INVALID_ARGUMENT, "exact rows %d (0 .. 256)", value);
+      ctx->exact_rows = value;
+      return WG_OK;
+    default:
+      return fail(ctx, WG_INVALID_ARGUMENT, "unknown option %d", option);
+  }
+}
+
 int wg_destroy(wg_ctx *ctx) {
   if (!ctx) return WG_INVALID_ARGUMENT;
   cudaSetDevice(ctx->device);
@@ -471,10 +483,11 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
   if (push && M > wg::kGemvMaxTokens)
     return fail(ctx, WG_UNSUPPORTED, "a pushing matmul takes at most %d rows (got %d)", wg::kGemvMaxTokens, M);
   // Many rows: the tcgen05 GEMM (src/engine.ts:4684: more rows than the
-  // split path takes go to the prompt matmul). Measured on B200, the GEMM
-  // (latency-bound near 18 us at 4096 x 4096) beats the GEMV from 17 rows
-  // on; pushes and epilogues stay in the GEMV, which has them.
-  const bool gemm_rows = M > wg::kGemvMaxTokens || (M >= wg::kGemmMinRows && !push && epi == wg::kEpiNone);
+  // split path takes go to the prompt matmul), from ctx->exact_rows + 1 rows
+  // (WG_OPT_EXACT_ROWS; measured on B200, the GEMM beats the GEMV from 17
+  // rows on); pushes and epilogues stay in the GEMV, which has them (up to
+  // 32 rows).
+  const bool gemm_rows = push || epi != wg::kEpiNone ? M > wg::kGemvMaxTokens : M > ctx->exact_rows;
   if (gemm_rows && wg::gemm_supported()) {
     wg::GemmArgs g{};
     g.nib = m->nib;
@@ -488,9 +501,9 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     g.KT = m->d.KT;
     g.y_dtype = y_dtype;
     g.flags = ctx->d_flags;
-    const size_t ws_bytes = wg::plan_gemm(g, ctx->num_sms);
+    wg::plan_gemm(g, ctx->num_sms);
     const size_t xh_bytes = (x_dtype == WG_F16 && !pro) ? 0 : align_up((size_t)M * K * 2, 256);
-    st = ensure_work(ctx, xh_bytes + ws_bytes);
+    st = ensure_work(ctx, xh_bytes);
     if (st) return st;
     const void *xh = x;
     if (pro) {
@@ -500,8 +513,7 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
       WG_CUDA(ctx, wg::launch_to_f16(x, x_dtype, ctx->work, (size_t)M * K, ctx->stream));
       xh = ctx->work;
     }
-    g.ws = ws_bytes ? reinterpret_cast<float *>(ctx->work + xh_bytes) : nullptr;
-    WG_CUDA(ctx, wg::launch_gemm(g, xh, ctx->stream));
+    WG_CUDA(ctx, wg::launch_gemm(g, xh, ctx->stream, ctx->pdl));
     return WG_OK;
   }
   // A prologue over more rows than one fused GEMV takes runs on its own; so

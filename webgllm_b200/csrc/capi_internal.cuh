@@ -29,6 +29,7 @@ struct wg_ctx {
   bool pdl = true;              // programmatic dependent launch for the GEMV
   int trigger_at = 1;           // GemvArgs::trigger_at (WG_GEMV_TRIGGER overrides)
   int gemv_wide = -1;           // -1: by shape; 0 / 1 forced (WG_GEMV_WIDE)
+  int exact_rows = 16;          // WG_OPT_EXACT_ROWS: up to this many rows on the GEMV
   unsigned long long *trace = nullptr;       // wg_trace buffer (device) or null
   unsigned long long trace_cap = 0;          // records that fit
   unsigned long long *d_trace_next = nullptr;  // device record counter

@@ -21,10 +21,17 @@
 //   warp 1     one thread issues tcgen05.mma (kind::f16, A from TMEM, B from
 //              shared memory, fp32 accumulator in TMEM) and commits each
 //              stage back to the ring;
-//   warps 2-9  epilogue: tcgen05.ld of the accumulator, stored as y (or,
-//              when K is split across CTAs for parallelism, as this split's
-//              fp32 slab of a workspace that a second kernel sums in a fixed
-//              order: deterministic, no atomics).
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator, stored as y. When
+//              K is split across CTAs for parallelism (few token rows), the
+//              splits of a tile form one thread-block cluster: each stages
+//              its fp32 tile in its own shared memory and CTA r sums slice r
+//              of the tile over the cluster's CTAs in rank order through
+//              distributed shared memory (deterministic, no atomics, no
+//              workspace, no second kernel).
+// Launched with programmatic dependent launch: barriers, tensor memory and
+// the first stages' weight copies are set up before the kernel waits for
+// the one that produced x (griddepcontrol.wait), so in a chain of matmuls
+// they overlap the previous kernel's tail.
 // Every wait is bounded (mbar_wait_bounded) and TMEM is freed on every path.
 #include <cuda.h>
 
@@ -39,6 +46,7 @@ namespace wg {
 namespace {
 
 constexpr int kStages = 4;
+constexpr int kMaxSplits = 8;  // K splits of a tile: one portable thread-block cluster
 constexpr int kBN = 128;          // weight rows per CTA = MMA M
 constexpr int kDequantWarps = 8;  // warps 2..9
 constexpr int kGemmThreads = (2 + kDequantWarps) * 32;
@@ -161,6 +169,22 @@ __host__ __device__ constexpr uint32_t idesc_f16(int BM) {
   return (1u << 4) | ((uint32_t)(BM >> 3) << 17) | ((uint32_t)(kBN >> 4) << 24);
 }
 
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t caddr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(caddr) : "memory");
+  return v;
+}
+
 template <int BM, bool ZEROS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_nib,
@@ -212,16 +236,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t bytes = kXStageBytes(BM) + kNibStageBytes + kSclStageBytes + (ZEROS ? kZroStageBytes : 0);
-      for (int it = 0; it < nk; it++) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        wait(&empty[s], ph ^ 1);
-        const int kt = kt_begin + it;
-        mbar_expect_tx(&full[s], bytes);
-        tma_load_2d(smem + L.x + s * kXStageBytes(BM), &tm_x, kt * kTileK, m0, &full[s]);
+      auto load_w = [&](int it) {
+        const int s = it % kStages, kt = kt_begin + it;
         tma_load_3d(smem + L.nib + s * kNibStageBytes, &tm_nib, 0, kt, nt0, &full[s]);
         tma_load_3d(smem + L.scl + s * kSclStageBytes, &tm_scl, 0, kt, nt0, &full[s]);
         if (ZEROS) tma_load_3d(smem + L.zro + s * kZroStageBytes, &tm_zro, 0, kt, nt0, &full[s]);
+      };
+      // The first stages' weights depend on no earlier kernel: copied before
+      // the dependency wait; x (the previous kernel's output) after it.
+      const int pre = nk < kStages ? nk : kStages;
+      for (int it = 0; it < pre; it++) {
+        mbar_expect_tx(&full[it], bytes);
+        load_w(it);
+      }
+      pdl_wait();
+      for (int it = 0; it < pre; it++)
+        tma_load_2d(smem + L.x + it * kXStageBytes(BM), &tm_x, (kt_begin + it) * kTileK, m0, &full[it]);
+      for (int it = pre; it < nk; it++) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        wait(&empty[s], ph ^ 1);
+        mbar_expect_tx(&full[s], bytes);
+        tma_load_2d(smem + L.x + s * kXStageBytes(BM), &tm_x, (kt_begin + it) * kTileK, m0, &full[s]);
+        load_w(it);
       }
     }
   } else if (warp == 1) {
@@ -287,25 +324,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 
     // Epilogue: this warp's 32 TMEM lanes (weight rows 32q..32q+31) and half
-    // of the token columns.
+    // of the token columns: into y, or (K split over the cluster) into this
+    // CTA's staging tile red[token][128 rows] over the idle ring.
     wait(accfull, 0);
     tc_fence_after();
+    pdl_wait();  // y may still be read by an earlier kernel until it completes
     const int n = nt0 * kTileRows + 32 * q + lane;
     const int c_begin = sub * (BM / 2), c_end = c_begin + BM / 2;
+    float *red = reinterpret_cast<float *>(smem + L.x);
     for (int c = c_begin; c < c_end; c += 16) {
       float v[16];
       tmem_ld_32x32b_x16(tmem_d + ((uint32_t)(32 * q) << 16) + c, v);
-      if (n < a.N) {
+      if (a.splits > 1) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) red[(c + i) * kBN + 32 * q + lane] = v[i];
+      } else if (n < a.N) {
 #pragma unroll
         for (int i = 0; i < 16; i++) {
           const int tok = m0 + c + i;
-          if (tok < a.M) {
-            if (a.ws) a.ws[((size_t)blockIdx.z * a.M + tok) * a.N + n] = v[i];  // this split's slab
-            else store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, v[i]);
-          }
+          if (tok < a.M) store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, v[i]);
         }
       }
     }
+  }
+  pdl_wait();  // every thread that stores y below (the cluster reduction) has waited
+  pdl_trigger();
+
+  if (a.splits > 1) {
+    // The cluster's CTAs are the K splits of this tile: CTA r sums elements
+    // [r E / C, (r+1) E / C) of the E = BM x 128 tile over ranks 0..C-1 (a
+    // fixed order) and stores them. Every thread of every CTA passes both
+    // cluster barriers on every path (a CTA that skipped one would stall
+    // its peers).
+    cluster_sync_all();  // every split's tile is staged
+    const int C = a.splits;
+    uint32_t crank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+    const int E = BM * kBN;
+    const int e0 = (int)((long long)E * crank / C), e1 = (int)((long long)E * (crank + 1) / C);
+    const uint32_t red_local = smem_u32(smem + L.x);
+    for (int e = e0 + (int)threadIdx.x; e < e1; e += kGemmThreads) {
+      float acc = 0.0f;
+      for (int r = 0; r < C; r++) acc += ld_cluster_f32(map_rank(red_local + (uint32_t)e * 4u, (uint32_t)r));
+      const int tok = m0 + e / kBN, nn = nt0 * kTileRows + (e % kBN);
+      if (tok < a.M && nn < a.N) store_out(a.y, a.y_dtype, (size_t)tok * a.N + nn, acc);
+    }
+    cluster_sync_all();  // no CTA leaves while a peer still reads its tile
   }
 
   tc_fence_before();
@@ -368,11 +432,6 @@ __host__ __device__ inline Gemm2Smem gemm2_smem() {
   return s;
 }
 
-__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
 
 // arrive on an mbarrier given by its shared::cluster address
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
@@ -444,9 +503,6 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 
 template <bool ZEROS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -611,8 +667,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < 16; i++) {
           const int tok = m0 + c + i;
           if (tok < a.M) {
-            if (a.ws) a.ws[((size_t)blockIdx.z * a.M + tok) * a.N + n] = v[i];
-            else store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, v[i]);
+            store_out(a.y, a.y_dtype, (size_t)tok * a.N + n, v[i]);
           }
         }
       }
@@ -634,15 +689,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc2(tmem, kTmemCols2);
-  }
-}
-
-// Sums the K splits' slabs in split order (deterministic) into y.
-__global__ void finalize_kernel(const float *ws, int splits, void *y, int dtype, size_t n) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int z = 0; z < splits; z++) s += ws[(size_t)z * n + i];
-    store_out(y, dtype, i, s);
   }
 }
 
@@ -686,7 +732,7 @@ bool encode_plane(CUtensorMap *m, const void *base, int words, int KT, int NT) {
 }
 
 template <int BM, bool ZEROS>
-cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream) {
+cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream, bool pdl) {
   const GemmSmem L = gemm_smem(BM);
   auto kern = gemm_kernel<BM, ZEROS>;
   static_assert(BM <= tmem_a_col(BM) && tmem_a_col(BM) + kStages * 32 <= tmem_cols(BM), "TMEM columns");
@@ -703,9 +749,28 @@ cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   tz = ts;
   if (ZEROS && !encode_plane(&tz, a.zro, kTileZroBytes / 4, a.KT, a.NT)) return cudaErrorInvalidValue;
-  dim3 grid((unsigned)((a.NT + 7) / 8), (unsigned)((a.M + BM - 1) / BM), (unsigned)a.splits);
-  kern<<<grid, kGemmThreads, smem_bytes, stream>>>(tx, tn, ts, tz, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((a.NT + 7) / 8), (unsigned)((a.M + BM - 1) / BM), (unsigned)a.splits);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = (size_t)smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  if (a.splits > 1) {  // the K splits of a tile form one cluster
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = 1;
+    at[n].val.clusterDim.y = 1;
+    at[n].val.clusterDim.z = (unsigned)a.splits;
+    n++;
+  }
+  if (pdl) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, tx, tn, ts, tz, a);
 }
 
 template <bool ZEROS>
@@ -785,15 +850,19 @@ size_t plan_gemm(GemmArgs &a, int num_sms) {
     const char *e = getenv("WG_GEMM_SPLITS");
     force = e ? atoi(e) : 0;
   }
+  // The splits of a tile form one thread-block cluster (at most a portable 8;
+  // the 2-SM kernel keeps its workspace and does not split).
   int splits = 1;
-  while (tiles * (splits + 1) <= 2 * num_sms && a.KT / (splits + 1) >= 4) splits++;
-  if (force > 0) splits = force < a.KT ? force : a.KT;
+  if (!pair)
+    while (splits < kMaxSplits && tiles * (splits + 1) <= 2 * num_sms && a.KT / (splits + 1) >= 4) splits++;
+  if (force > 0 && !pair) splits = force < kMaxSplits ? force : kMaxSplits;
+  if (splits > a.KT) splits = a.KT;
   a.kt_per_split = (a.KT + splits - 1) / splits;
   a.splits = (a.KT + a.kt_per_split - 1) / a.kt_per_split;
-  return a.splits > 1 ? (size_t)a.splits * a.M * a.N * sizeof(float) : 0;
+  return 0;
 }
 
-cudaError_t launch_gemm(const GemmArgs &args, const void *x_f16, cudaStream_t stream) {
+cudaError_t launch_gemm(const GemmArgs &args, const void *x_f16, cudaStream_t stream, bool pdl) {
   if (!encode_fn()) return cudaErrorNotSupported;
   GemmArgs a = args;
   static int relaxed = -1;
@@ -802,23 +871,17 @@ cudaError_t launch_gemm(const GemmArgs &args, const void *x_f16, cudaStream_t st
     relaxed = e && e[0] == '1' ? 1 : 0;
   }
   a.fwd_relaxed = relaxed;
+  if (a.splits < 1 || a.splits > kMaxSplits) return cudaErrorInvalidValue;
   const int BM = gemm_tile_m(a.M);
-  cudaError_t e;
-  if (a.splits > 1) {
-    if (!a.ws) return cudaErrorInvalidValue;
-  } else {
-    a.ws = nullptr;
-  }
   const bool z = a.zro != nullptr;
-  if (gemm_use_pair(a)) e = z ? launch_pair<true>(a, x_f16, stream) : launch_pair<false>(a, x_f16, stream);
-  else if (BM == 64) e = z ? launch_bm<64, true>(a, x_f16, stream) : launch_bm<64, false>(a, x_f16, stream);
-  else if (BM == 128) e = z ? launch_bm<128, true>(a, x_f16, stream) : launch_bm<128, false>(a, x_f16, stream);
-  else e = z ? launch_bm<256, true>(a, x_f16, stream) : launch_bm<256, false>(a, x_f16, stream);
-  if (e != cudaSuccess || a.splits == 1) return e;
-  const size_t n = (size_t)a.M * a.N;
-  const size_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
-  finalize_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a.ws, a.splits, a.y, a.y_dtype, n);
-  return cudaGetLastError();
+  if (gemm_use_pair(a)) {
+    if (a.splits != 1) return cudaErrorInvalidValue;
+    return z ? launch_pair<true>(a, x_f16, stream) : launch_pair<false>(a, x_f16, stream);
+  }
+  if (BM == 64) return z ? launch_bm<64, true>(a, x_f16, stream, pdl) : launch_bm<64, false>(a, x_f16, stream, pdl);
+  if (BM == 128)
+    return z ? launch_bm<128, true>(a, x_f16, stream, pdl) : launch_bm<128, false>(a, x_f16, stream, pdl);
+  return z ? launch_bm<256, true>(a, x_f16, stream, pdl) : launch_bm<256, false>(a, x_f16, stream, pdl);
 }
 
 namespace {

@@ -75,7 +75,7 @@ __host__ __device__ inline GemvSmem gemv_smem(int M, int ktc, int NG, bool zeros
   s.x_warp = M * s.x_stride;
   s.red = align_to(s.x + kWarps * s.x_warp * 2, 128);
   s.bar = align_to(s.red + (kWarps * NG * 128 + 128 * NG) * 4, 8);
-  s.total = s.bar + kWarps * 8;
+  s.total = s.bar + 2 * kWarps * 8;  // a weight and an x barrier per warp
   return s;
 }
 
@@ -265,6 +265,10 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
   __half *xw = reinterpret_cast<__half *>(smem + L.x) + warp * L.x_warp;
   float *red = reinterpret_cast<float *>(smem + L.red);
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L.bar) + warp;
+  uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + L.bar) + kWarps + warp;
+  // fp16 x without a prologue arrives by bulk copy (one per row), else by
+  // loads and stores that convert or compute it
+  const bool x_bulk = PRO == kProNone && a.x_dtype == WG_F16;
   __shared__ unsigned long long ts[6];  // tracing stamps (thread 0)
   if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
 
@@ -273,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
   //    writes, so this happens before any wait.
   if (lane == 0 && nw > 0) {
     mbar_init(bar, 1);
+    if (x_bulk) mbar_init(xbar, 1);
     fence_mbar_init();
     const size_t tile = (size_t)nt * a.KT + kt0 + wt0;
     mbar_expect_tx(bar, nw * (kTileNibBytes + kTileSclBytes + (ZEROS ? kTileZroBytes : 0)));
@@ -308,7 +313,28 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
     __shared__ float s_part[kWarps * kProMaxTokens];
     rmsnorm_rows(a.pro, M, a.K, s_part, s_inv);
   }
-  {
+  if (x_bulk) {
+    // this warp's K slice of every row: one bulk copy per row (16-byte
+    // aligned: K is a multiple of 32, the slice starts at a tile), the
+    // partial last tile's columns past K zeroed (padding weights are 0, but
+    // 0 * NaN is not)
+    if (nw > 0) {
+      const int kbase = (kt0 + wt0) * kTileK;
+      const int kcols = min(a.K - kbase, nw * kTileK);  // a multiple of 32
+      if (lane == 0) {
+        mbar_expect_tx(xbar, (uint32_t)(M * kcols * 2));
+        for (int m = 0; m < M; m++)
+          bulk_g2s(xw + (size_t)m * stride, reinterpret_cast<const __half *>(a.x) + (size_t)m * a.K + kbase,
+                   kcols * 2, xbar);
+      }
+      const int tail = nw * kTileK - kcols;
+      for (int i = lane; i < M * tail; i += 32) {
+        const int m = i / tail;
+        xw[(size_t)m * stride + kcols + (i - m * tail)] = __float2half_rn(0.0f);
+      }
+      mbar_wait_bounded(xbar, 0, a.flags);
+    }
+  } else {
     // Up to 4 loads in flight per lane before any store (one L2 round trip
     // for the usual M * 8 tiles <= 128 chunks). Entry idx = m * 64 + c
     // (token m, chunk c of 8 K values; a warp has at most 64 chunks), so
@@ -421,7 +447,10 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
 
   // 7. No copy may still be writing this CTA's shared memory when it exits
   //    (only possible after a timed-out wait).
-  if (lane == 0 && nw > 0) mbar_wait_bounded(bar, 0, a.flags);
+  if (lane == 0 && nw > 0) {
+    mbar_wait_bounded(bar, 0, a.flags);
+    if (x_bulk) mbar_wait_bounded(xbar, 0, a.flags);
+  }
   if (a.push_on) push_signal(a.push);
   if (a.trace && threadIdx.x == 0) {
     ts[5] = globaltimer();

@@ -78,10 +78,6 @@ struct GemvArgs {
 enum EpiKind { kEpiNone = 0, kEpiSwigluPairs = 1 };
 
 constexpr int kGemvMaxTokens = 32;
-// Rows from which a plain matmul (no push, no epilogue) goes to the GEMM;
-// measured on B200, the GEMM (latency-bound near 18 us at 4096 x 4096)
-// beats the GEMV from 17 rows on.
-constexpr int kGemmMinRows = 17;
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl);
 // Plans kt_per_cta / cluster for a shape; false if the shape is too large.
 bool plan_gemv(GemvArgs &a, int num_sms);
@@ -96,19 +92,20 @@ struct GemmArgs {
   const uint16_t *scl;
   const uint8_t *zro;  // nullable
   void *y;
-  float *ws;           // fp32 [splits][M][N] workspace when K is split, else null
   int M, N, K, NT, KT;
   int y_dtype;
-  int splits, kt_per_split;
+  int splits, kt_per_split;  // K splits of a tile (one thread-block cluster), K tiles each
   unsigned *flags;
   int fwd_relaxed;  // pair kernel: forward A stages with relaxed arrives (measurement knob)
 };
 
 bool gemm_supported();
-// Chooses the K split (splits, kt_per_split); returns the workspace bytes
-// it needs (0 when K is not split).
+// Chooses the K split (splits, kt_per_split): the splits of a tile reduce on
+// chip across a thread-block cluster, so no workspace is needed (returns 0).
 size_t plan_gemm(GemmArgs &a, int num_sms);
-cudaError_t launch_gemm(const GemmArgs &a, const void *x_f16, cudaStream_t stream);
+// pdl: programmatic dependent launch (weights prefetched before the wait
+// for x's producer).
+cudaError_t launch_gemm(const GemmArgs &a, const void *x_f16, cudaStream_t stream, bool pdl);
 // x (f32 / bf16) -> fp16, saturating like packH2; n a multiple of 8.
 cudaError_t launch_to_f16(const void *x, int dtype, void *out, size_t n, cudaStream_t stream);
 

@@ -1,8 +1,8 @@
 // wg_q4_matmul_static: the Q4 matmul without any device allocation.
 //
-// wg_q4_matmul keeps its scratch (the fp16 copy of x when x is f32 / bf16,
-// and the fp32 partial sums when the GEMM splits K across CTAs) in a buffer
-// that it grows with cudaMalloc on first use of a larger shape. Some callers
+// wg_q4_matmul keeps its scratch (the fp16 copy of x that the GEMM reads when
+// x is f32 / bf16) in a buffer that it grows with cudaMalloc on first use of
+// a larger shape. Some callers
 // cannot let a library allocate: code recording a CUDA graph (allocation is
 // not allowed while a stream is being captured), engines that budget device
 // memory up front and must not see it grow behind their back, and decode
@@ -19,9 +19,12 @@
 // - All calls on a device share the one array and it keeps the last call's
 //   contents: two calls whose work overlaps on the GPU (different streams, or
 //   different contexts of the same device) race on it. Nothing in it needs to
-//   start at zero (each K split writes its whole slab of partial sums).
+//   start at zero (each call writes the whole fp16 copy it then reads).
 // - The first call on a device looks up the array's device address
 //   (cudaGetSymbolAddress); make that first call before capturing a stream.
+//   The address is kept for the life of the process: after a
+//   cudaDeviceReset of that device (which destroys the context the address
+//   belongs to) this entry point must not be called again.
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -90,8 +93,8 @@ extern "C" int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x
   cudaError_t e = cudaSetDevice(ctx->device);
   if (e != cudaSuccess) return fail_static(ctx, wg::status_of(e), "cudaSetDevice: %s", cudaGetErrorString(e));
 
-  // The same routing as wg_q4_matmul: the GEMM from kGemmMinRows rows on.
-  if (M >= wg::kGemmMinRows && wg::gemm_supported()) {
+  // The same routing as wg_q4_matmul: the GEMM above the context's exact rows.
+  if (M > ctx->exact_rows && wg::gemm_supported()) {
     wg::GemmArgs g{};
     g.nib = m->nib;
     g.scl = m->scl;
@@ -104,13 +107,13 @@ extern "C" int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x
     g.KT = m->d.KT;
     g.y_dtype = y_dtype;
     g.flags = ctx->d_flags;
-    const size_t ws_bytes = wg::plan_gemm(g, ctx->num_sms);
+    wg::plan_gemm(g, ctx->num_sms);
     const size_t xh_bytes = x_dtype == WG_F16 ? 0 : round256((size_t)M * m->d.K * 2);
-    if (xh_bytes + ws_bytes > kScratchBytes)
+    if (xh_bytes > kScratchBytes)
       return fail_static(ctx, WG_UNSUPPORTED,
                          "this matmul needs %zu bytes of scratch; the static scratch holds %zu "
                          "(use wg_q4_matmul, which allocates)",
-                         xh_bytes + ws_bytes, kScratchBytes);
+                         xh_bytes, kScratchBytes);
     unsigned char *scratch = nullptr;
     int st = scratch_address(ctx, &scratch);
     if (st) return st;
@@ -120,8 +123,7 @@ extern "C" int wg_q4_matmul_static(wg_ctx *ctx, const wg_q4mat *m, const void *x
       if (e != cudaSuccess) return fail_static(ctx, wg::status_of(e), "x conversion: %s", cudaGetErrorString(e));
       xh = scratch;
     }
-    g.ws = ws_bytes ? reinterpret_cast<float *>(scratch + xh_bytes) : nullptr;
-    e = wg::launch_gemm(g, xh, ctx->stream);
+    e = wg::launch_gemm(g, xh, ctx->stream, ctx->pdl);
     if (e != cudaSuccess) return fail_static(ctx, wg::status_of(e), "GEMM launch: %s", cudaGetErrorString(e));
     return WG_OK;
   }

@@ -68,6 +68,10 @@ class Context:
     def set_stream(self, stream: int | None) -> None:
         self._check(_lib.lib().wg_set_stream(self.handle, ctypes.c_void_p(stream or 0)))
 
+    def set_option(self, option: int, value: int) -> None:
+        """wg_set_option (e.g. WG_OPT_EXACT_ROWS)."""
+        self._check(_lib.lib().wg_set_option(self.handle, option, value))
+
     def sync(self) -> None:
         self._check(_lib.lib().wg_sync(self.handle))
 

@@ -25,6 +25,7 @@ from . import _lib
 from .model import DecoderConfig, DecoderModel
 
 P = ctypes.c_void_p
+_EXACT_ROWS_DEFAULT = 16  # the library's WG_OPT_EXACT_ROWS default
 
 
 def draft_config(target: DecoderConfig) -> DecoderConfig:
@@ -38,6 +39,8 @@ class SpeculativeDecoder:
             raise ValueError("target and draft must share batch and vocabulary")
         if target.max_rows < target.batch * (k + 1):
             raise ValueError(f"the target needs max_rows >= {target.batch * (k + 1)}")
+        if target.batch * (k + 1) > 256:
+            raise ValueError("a verify batch takes at most 256 rows (batch x (k + 1))")
         self.t, self.d, self.k = target, draft, k
         B = target.batch
         self.drafts = torch.zeros((B, max(k, 1)), dtype=torch.int32, device="cuda")
@@ -85,9 +88,14 @@ class SpeculativeDecoder:
                 self.ver[:, j + 1].copy_(d.next_id)
         t.row_picks = self.picks
         t.prefix_slot = 0 if t.has_conv else None
+        # the verify rows take the decode steps' arithmetic (exact weights on
+        # the GEMV), so that each pick is the one plain greedy decoding makes
+        rows = t.batch * (k + 1)
+        t.ctx.set_option(_lib.WG_OPT_EXACT_ROWS, max(rows, _EXACT_ROWS_DEFAULT))
         try:
-            t.forward(self.ver.reshape(-1), t.batch * (k + 1))
+            t.forward(self.ver.reshape(-1), rows)
         finally:
+            t.ctx.set_option(_lib.WG_OPT_EXACT_ROWS, _EXACT_ROWS_DEFAULT)
             t.row_picks = None
             t.prefix_slot = None
         L = _lib.lib()
