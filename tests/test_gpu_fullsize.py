@@ -16,7 +16,12 @@ tokens over a stated prefix for full models"):
   ||got - want|| / ||want|| <= LOGIT_REL_L2 and
   max |got - want| <= LOGIT_REL_MAX * max |want|. (The reference engine's
   own numeric gate for a model is a relative error of 1e-2,
-  packages/webgllm/src/handler.ts:455, SELF_CHECK_MAX; these are tighter.)
+  packages/webgllm/src/handler.ts:455, SELF_CHECK_MAX; these are tighter.
+  The floor any fp16-activation implementation meets here: the same
+  restatement with fp64 instead of fp32 accumulation moves these models'
+  logits by 0.7e-3 (4 layers) to 1.2e-3 (16 layers) relative, as
+  activations cross fp16 rounding boundaries; measured here: 1.8e-3
+  (config 2), 2.1e-3 (config 3), 4.2e-3 (config 4).)
 - tokens: the library's greedy token equals the fp32 forward's argmax at
   every one of those TOKENS steps, except where the two disagree inside the
   logit tolerance (the forward's top-2 margin below 2 * LOGIT_REL_MAX *
@@ -35,8 +40,8 @@ import decoder_reference as R  # noqa: E402
 
 STEPS = 32             # decode steps after the prefill's token
 TOKENS = STEPS + 1     # generated tokens compared per sequence: the prefill's pick + STEPS
-LOGIT_REL_L2 = 1e-2
-LOGIT_REL_MAX = 1e-2
+LOGIT_REL_L2 = 6e-3
+LOGIT_REL_MAX = 6e-3
 MAX_NEAR_TIES = 2
 
 # config: (batch, prompt tokens) — BASELINE's prompt lengths and batches
