@@ -162,3 +162,36 @@ class ReferenceDecoder:
         logits = h.half().float() @ self.head.t()
         self.pos += rows
         return logits[0]
+
+
+def greedy_or_near_tie(plain, prompts, got, want, tol=1e-2):
+    """Checks tokens `got` [batch][n] against plain greedy decoding's `want`
+    (from `plain`, a DecoderModel with the target's weights): equal, or
+    parting only where plain decoding's own pick was a near tie. At each
+    sequence's first difference, plain decoding (which read the same tokens
+    until there) must rank its pick above `got`'s token by no more than
+    tol * max |logit| — a margin that another accumulation order can
+    overturn. Returns the first difference per sequence (None: none)."""
+    n = want.shape[1]
+    firsts = []
+    for b in range(want.shape[0]):
+        d = (got[b, :n] != want[b]).nonzero()
+        firsts.append(int(d[0]) if d.numel() else None)
+    if all(f is None for f in firsts):
+        return firsts
+    # plain decoding again (deterministic), keeping each step's logits
+    plain.reset()
+    plain.prefill(prompts)
+    logits = [plain.logits.clone()]
+    for _ in range(1, max(f for f in firsts if f is not None) + 1):
+        plain.decode_step()
+        logits.append(plain.logits.clone())
+    for b, f in enumerate(firsts):
+        if f is None:
+            continue
+        lg = logits[f][b]
+        w, g = int(want[b, f]), int(got[b, f])
+        assert int(lg.argmax()) == w, "plain decoding is not deterministic"
+        margin = (lg[w] - lg[g]).item() / lg.abs().max().item()
+        assert margin <= tol, f"sequence {b}: token {f} is {g}, plain greedy {w} by a margin of {margin:.3e}"
+    return firsts

@@ -184,6 +184,8 @@ int wg_init(int device, wg_ctx **out) {
   if (pdl && pdl[0] == '0') ctx->pdl = false;
   const char *wide = getenv("WG_GEMV_WIDE");
   if (wide && (wide[0] == '0' || wide[0] == '1')) ctx->gemv_wide = wide[0] - '0';
+  const char *nfb = getenv("WG_NORM_FUSE_BYTES");
+  if (nfb && atol(nfb) >= 0) ctx->norm_fuse_bytes = (size_t)atol(nfb);
   const char *trig = getenv("WG_GEMV_TRIGGER");
   if (trig && trig[0] >= '0' && trig[0] <= '2') ctx->trigger_at = trig[0] - '0';
   *out = ctx;
@@ -517,10 +519,11 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     return WG_OK;
   }
   // A prologue over more rows than one fused GEMV takes runs on its own; so
-  // does a norm whose row statistics would cost every CTA more than 64 KB of
-  // reads (each CTA of the fused form reads all of a and b for them).
+  // does a norm whose row statistics would cost every CTA more than
+  // ctx->norm_fuse_bytes of reads (each CTA of the fused form reads all of a
+  // and b for them; 64 KB by default, WG_NORM_FUSE_BYTES for measurement).
   const bool heavy_norm =
-      pro && pro->kind == wg::kProRmsNorm && (size_t)M * K * 4 * (pro->b ? 2 : 1) > ((size_t)64 << 10);
+      pro && pro->kind == wg::kProRmsNorm && (size_t)M * K * 4 * (pro->b ? 2 : 1) > ctx->norm_fuse_bytes;
   if (pro && (M > wg::kProMaxTokens || heavy_norm)) {
     st = ensure_work(ctx, (size_t)M * K * 2);
     if (st) return st;

@@ -30,6 +30,7 @@ struct wg_ctx {
   int trigger_at = 1;           // GemvArgs::trigger_at (WG_GEMV_TRIGGER overrides)
   int gemv_wide = -1;           // -1: by shape; 0 / 1 forced (WG_GEMV_WIDE)
   int exact_rows = 16;          // WG_OPT_EXACT_ROWS: up to this many rows on the GEMV
+  size_t norm_fuse_bytes = 64 << 10;  // largest row-statistics read a fused norm prologue makes per CTA
   unsigned long long *trace = nullptr;       // wg_trace buffer (device) or null
   unsigned long long trace_cap = 0;          // records that fit
   unsigned long long *d_trace_next = nullptr;  // device record counter

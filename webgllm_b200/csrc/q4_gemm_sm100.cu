@@ -75,8 +75,8 @@ __host__ __device__ inline GemmSmem gemm_smem(int BM) {
   s.scl = s.nib + kStages * kNibStageBytes;
   s.zro = s.scl + kStages * kSclStageBytes;
   s.bar = s.zro + kStages * kZroStageBytes;
-  // full[S], empty[S], afull[S], accfull
-  s.tmem_slot = s.bar + (3 * kStages + 1) * 8;
+  // wfull[S] (weights), xfull[S] (x), empty[S], afull[S], accfull
+  s.tmem_slot = s.bar + (4 * kStages + 1) * 8;
   s.total = s.tmem_slot + 16;
   return s;
 }
@@ -196,8 +196,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const GemmSmem L = gemm_smem(BM);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
-  uint64_t *empty = full + kStages;
+  // weights and x of a stage complete separately: the dequantisers start on
+  // prefetched weights while x is still waiting for its producer
+  uint64_t *wfull = reinterpret_cast<uint64_t *>(smem + L.bar);
+  uint64_t *xfull = wfull + kStages;
+  uint64_t *empty = xfull + kStages;
   uint64_t *afull = empty + kStages;
   uint64_t *accfull = afull + kStages;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
@@ -213,7 +216,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) {
     aborted = 0;
     for (int i = 0; i < kStages; i++) {
-      mbar_init(&full[i], 1);
+      mbar_init(&wfull[i], 1);
+      mbar_init(&xfull[i], 1);
       mbar_init(&empty[i], 1);
       mbar_init(&afull[i], kDequantWarps);
     }
@@ -235,30 +239,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t bytes = kXStageBytes(BM) + kNibStageBytes + kSclStageBytes + (ZEROS ? kZroStageBytes : 0);
+      const uint32_t wbytes = kNibStageBytes + kSclStageBytes + (ZEROS ? kZroStageBytes : 0);
+      const uint32_t xbytes = kXStageBytes(BM);
       auto load_w = [&](int it) {
         const int s = it % kStages, kt = kt_begin + it;
-        tma_load_3d(smem + L.nib + s * kNibStageBytes, &tm_nib, 0, kt, nt0, &full[s]);
-        tma_load_3d(smem + L.scl + s * kSclStageBytes, &tm_scl, 0, kt, nt0, &full[s]);
-        if (ZEROS) tma_load_3d(smem + L.zro + s * kZroStageBytes, &tm_zro, 0, kt, nt0, &full[s]);
+        mbar_expect_tx(&wfull[s], wbytes);
+        tma_load_3d(smem + L.nib + s * kNibStageBytes, &tm_nib, 0, kt, nt0, &wfull[s]);
+        tma_load_3d(smem + L.scl + s * kSclStageBytes, &tm_scl, 0, kt, nt0, &wfull[s]);
+        if (ZEROS) tma_load_3d(smem + L.zro + s * kZroStageBytes, &tm_zro, 0, kt, nt0, &wfull[s]);
       };
-      // The first stages' weights depend on no earlier kernel: copied before
-      // the dependency wait; x (the previous kernel's output) after it.
-      const int pre = nk < kStages ? nk : kStages;
-      for (int it = 0; it < pre; it++) {
-        mbar_expect_tx(&full[it], bytes);
-        load_w(it);
-      }
-      pdl_wait();
-      for (int it = 0; it < pre; it++)
-        tma_load_2d(smem + L.x + it * kXStageBytes(BM), &tm_x, (kt_begin + it) * kTileK, m0, &full[it]);
-      for (int it = pre; it < nk; it++) {
+      auto load_x = [&](int it) {
         const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        wait(&empty[s], ph ^ 1);
-        mbar_expect_tx(&full[s], bytes);
-        tma_load_2d(smem + L.x + s * kXStageBytes(BM), &tm_x, (kt_begin + it) * kTileK, m0, &full[s]);
+        mbar_expect_tx(&xfull[s], xbytes);
+        tma_load_2d(smem + L.x + s * kXStageBytes(BM), &tm_x, (kt_begin + it) * kTileK, m0, &xfull[s]);
+      };
+      // The first stages' weights depend on no earlier kernel: copied (and
+      // dequantised) before the dependency wait; x, the previous kernel's
+      // output, after it.
+      const int pre = nk < kStages ? nk : kStages;
+      for (int it = 0; it < pre; it++) load_w(it);
+      pdl_wait();
+      for (int it = 0; it < pre; it++) load_x(it);
+      for (int it = pre; it < nk; it++) {
+        wait(&empty[it % kStages], ((it / kStages) & 1) ^ 1);
         load_w(it);
+        load_x(it);
       }
     }
   } else if (warp == 1) {
@@ -267,7 +272,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int it = 0; it < nk; it++) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        wait(&full[s], ph);
+        wait(&xfull[s], ph);
         wait(&afull[s], ph);
         tc_fence_after();
         const uint64_t bdesc = sw128_desc(smem_u32(smem + L.x + s * kXStageBytes(BM)));
@@ -288,7 +293,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int it = 0; it < nk; it++) {
       const int s = it % kStages;
       const uint32_t ph = (it / kStages) & 1;
-      wait(&full[s], ph);
+      wait(&wfull[s], ph);
       wait(&empty[s], ph ^ 1);  // the MMA that last read A stage s is done
       tc_fence_after();
       const uint4 wv = *reinterpret_cast<const uint4 *>(smem + L.nib + s * kNibStageBytes + tile * kTileNibBytes +
@@ -381,8 +386,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // No TMA may still be writing this CTA's shared memory when it exits (only
   // possible after a timed-out wait): wait for the last round of each stage.
   if (threadIdx.x == 0 && aborted) {
-    for (int it = nk > kStages ? nk - kStages : 0; it < nk; it++)
-      mbar_wait_bounded(&full[it % kStages], (it / kStages) & 1, a.flags);
+    for (int it = nk > kStages ? nk - kStages : 0; it < nk; it++) {
+      mbar_wait_bounded(&wfull[it % kStages], (it / kStages) & 1, a.flags);
+      mbar_wait_bounded(&xfull[it % kStages], (it / kStages) & 1, a.flags);
+    }
   }
 }
 
