@@ -185,6 +185,11 @@ typedef struct wg_prologue {
   float eps;            /* RMSNORM: x / sqrt(mean(x^2) + eps) */
   float *resid_out;     /* RMSNORM: receives a + b [M][K], or NULL; must not
                            alias a or b */
+  const float *stats;   /* RMSNORM: NULL, or the sums of squares of a per 16
+                           columns, [K/16][M], from wg_q4_matmul_residual: the
+                           row statistics come from them (b and resid_out
+                           NULL), so the norm fuses into the matmul at any M
+                           <= 8 without each CTA reading all of a */
 } wg_prologue;
 
 /* y = x . W^T where x (fp16, as the reference rounds matmul inputs) is made
@@ -214,6 +219,18 @@ int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro,
 int wg_q4_matmul_ex(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro,
                     const void *x, int x_dtype, int M, void *y, int y_dtype,
                     int epilogue);
+
+/* The residual add of a decoder layer in the matmul's epilogue, and the
+ * statistics of the RMS norm that follows it: resid fp32 [M][N] += x . W^T
+ * (x as wg_q4_matmul_ex: given, or made by `pro`), and stats fp32 [N/16][M]
+ * receives, per 16 rows of W and per row m of x, the sum of squares of those
+ * 16 new residual values. The next matmul's prologue WG_PRO_RMSNORM with
+ * a = resid, stats = stats then normalises without reading every residual
+ * value: the engine's addNormed (src/engine.ts:5695) split across the two
+ * matmuls instead of a pass of its own. M <= 8, N % 16 == 0, 16-byte aligned
+ * tensors; the decode GEMV. */
+int wg_q4_matmul_residual(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, const void *x, int x_dtype,
+                          int M, float *resid, float *stats);
 
 /* ---- tracing ------------------------------------------------------------- */
 

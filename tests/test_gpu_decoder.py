@@ -531,6 +531,75 @@ def test_matmul_fused_rmsnorm(rows, N, K):
     assert rel(y, h.half().float() @ Wd.t()) < 1e-3
 
 
+@pytest.mark.parametrize("rows", [2, 5, 8])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (4096, 14336), (2048, 5632), (1536, 4608)])
+def test_matmul_residual_epilogue_and_stats_prologue(rows, N, K):
+    """wg_q4_matmul_residual: resid += x . W^T in the GEMV's epilogue (in
+    place) and stats [N/16][rows] = per-16-row sums of squares of the new
+    residual (K = 14336: the K split over a cluster, whose columns are then
+    summed whole by one CTA each); then a matmul whose RMSNORM prologue takes
+    those stats normalises like one that reads the residual itself."""
+    m, Wd = _q4(N, K, N + K + rows)
+    g = gen(rows * 7 + K)
+    x = torch.randn((rows, K), generator=g, device="cuda").half()
+    resid = torch.randn((rows, N), generator=g, device="cuda")
+    stats = torch.full((N // 16, rows), float("nan"), device="cuda")
+    want = resid + x.float() @ Wd.t()
+    c = ctx()
+    _lib.check(lib().wg_q4_matmul_residual(P(c.handle), P(m.handle), None, ptr(x), WG_F16, rows, ptr(resid),
+                                           ptr(stats)), c.handle)
+    torch.cuda.synchronize()
+    assert rel(resid, want) < 1e-4
+    want_stats = (resid * resid).reshape(rows, N // 16, 16).sum(-1).t()
+    assert torch.allclose(stats, want_stats, rtol=1e-5, atol=0)
+    # the consumer: a [N -> 1024] matmul normalising resid from the stats
+    m2, Wd2 = _q4(1024, N, 5)
+    w = torch.rand(N, generator=g, device="cuda") + 0.5
+    y_stats = torch.empty((rows, 1024), device="cuda")
+    y_plain = torch.empty((rows, 1024), device="cuda")
+    pro = _lib.wg_prologue(_lib.WG_PRO_RMSNORM, resid.data_ptr(), None, w.data_ptr(), 1e-5, None, stats.data_ptr())
+    _fused(m2, pro, rows, y_stats)
+    pro = _lib.wg_prologue(_lib.WG_PRO_RMSNORM, resid.data_ptr(), None, w.data_ptr(), 1e-5, None)
+    _fused(m2, pro, rows, y_plain)
+    _, h = R.rmsnorm(resid, None, w, 1e-5)
+    ref = h.half().float() @ Wd2.t()
+    assert rel(y_stats, ref) < 1e-3 and rel(y_stats, y_plain) < 1e-3
+    # stats reject an addend or a residual output
+    pro = _lib.wg_prologue(_lib.WG_PRO_RMSNORM, resid.data_ptr(), resid.data_ptr(), w.data_ptr(), 1e-5, None,
+                           stats.data_ptr())
+    assert lib().wg_q4_matmul_fused(P(c.handle), P(m2.handle), ctypes.byref(pro), rows, ptr(y_stats), WG_F32) == \
+        _lib.WG_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("hybrid", [False, True])
+def test_decoder_residual_epilogue_matches_the_fused_forward(hybrid, monkeypatch):
+    """Batched decode steps with the residual add in the matmul epilogues
+    (norms from the epilogue's statistics; WG_RESIDUAL_EPILOGUE=2 takes it at
+    any size) give the same logits as the norm-pass forward, within the
+    accumulation-order floor, and match the fp32 reference."""
+    from webgllm_b200.model import DecoderModel
+
+    cfg = small_config(hybrid)
+    prompts = torch.randint(0, cfg.vocab, (4, 12), generator=gen(41), device="cuda").to(torch.int32)
+    logits = {}
+    for mode in ("0", "2"):
+        monkeypatch.setenv("WG_RESIDUAL_EPILOGUE", mode)
+        m = DecoderModel(cfg, seed=6, max_ctx=64, max_rows=64, keep_blocks=True, batch=4)
+        m.prefill(prompts)
+        steps = []
+        for _ in range(3):
+            m.decode_step()
+            steps.append(m.logits.clone())
+        m.decode_step()
+        m.capture_decode()  # the residual forward also runs from a graph
+        m.graph.replay()
+        steps.append(m.logits.clone())
+        torch.cuda.synchronize()
+        logits[mode] = torch.stack(steps)
+    d = (logits["2"] - logits["0"]).float()
+    assert (d.norm() / logits["0"].norm()).item() < 5e-3
+
+
 @pytest.mark.parametrize("rows", [1, 8, 33])
 def test_matmul_fused_swiglu(rows):
     N, K = 2048, 5632

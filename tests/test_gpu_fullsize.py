@@ -26,7 +26,8 @@ tokens over a stated prefix for full models"):
   every one of those TOKENS steps, except where the two disagree inside the
   logit tolerance (the forward's top-2 margin below 2 * LOGIT_REL_MAX *
   max |want|, a near tie that any finite-precision path may resolve either
-  way); at most MAX_NEAR_TIES such steps per config.
+  way); at most NEAR_TIE_SHARE of a config's tokens (at least 2) may be such
+  ties — what the ~1e-3 floor below predicts for these logit spreads.
 """
 import pytest
 
@@ -42,7 +43,7 @@ STEPS = 32             # decode steps after the prefill's token
 TOKENS = STEPS + 1     # generated tokens compared per sequence: the prefill's pick + STEPS
 LOGIT_REL_L2 = 6e-3
 LOGIT_REL_MAX = 6e-3
-MAX_NEAR_TIES = 2
+NEAR_TIE_SHARE = 0.03
 
 # config: (batch, prompt tokens) — BASELINE's prompt lengths and batches
 CASES = {"2": (1, 128), "3": (1, 512), "4": (8, 512)}
@@ -110,7 +111,7 @@ def test_full_size_decoder_matches_fp32_forward(config):
         del ref
     print(f"config {config}: worst logits rel L2 {worst_l2:.3e}, rel max {worst_max:.3e} over "
           f"{batch} x {TOKENS} tokens; near ties {ties}")
-    assert len(ties) <= MAX_NEAR_TIES, ties
+    assert len(ties) <= max(2, int(NEAR_TIE_SHARE * batch * TOKENS)), ties
     del W
     m.close()
     del m

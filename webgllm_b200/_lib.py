@@ -32,7 +32,8 @@ WG_OPT_EXACT_ROWS = 1
 class wg_prologue(ctypes.Structure):
     """include/webgllm_q4.h wg_prologue."""
     _fields_ = [("kind", ctypes.c_int), ("a", ctypes.c_void_p), ("b", ctypes.c_void_p),
-                ("weight", ctypes.c_void_p), ("eps", ctypes.c_float), ("resid_out", ctypes.c_void_p)]
+                ("weight", ctypes.c_void_p), ("eps", ctypes.c_float), ("resid_out", ctypes.c_void_p),
+                ("stats", ctypes.c_void_p)]
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -63,6 +64,7 @@ SIGNATURES = {
     "wg_q4_matmul_static": (_I, [_P, _P, _P, _I, _I, _P, _I]),
     "wg_q4_matmul_fused": (_I, [_P, _P, _P, _I, _P, _I]),
     "wg_q4_matmul_ex": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, _I]),
+    "wg_q4_matmul_residual": (_I, [_P, _P, _P, _P, _I, _I, _P, _P]),
     "wg_trace": (_I, [_P, _P, _SZ]),
     "wg_trace_count": (_I, [_P, ctypes.POINTER(_SZ)]),
     # include/webgllm_decoder.h

@@ -475,13 +475,17 @@ namespace {
 // The matmul behind wg_q4_matmul and wg_q4_matmul_fused: y = x . W^T, with
 // x given (pro == null) or made by a prologue. Arguments are checked.
 int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M, void *y, int y_dtype,
-               const wg::Prologue *pro, const wg_comm *push = nullptr, int epi = wg::kEpiNone) {
+               const wg::Prologue *pro, const wg_comm *push = nullptr, int epi = wg::kEpiNone,
+               float *stats = nullptr) {
   int st = use_device(ctx);
   if (st) return st;
   const size_t K = m->d.K;
-  if (epi != wg::kEpiNone && (M > wg::kGemvMaxTokens || push || m->d.N % 16))
+  if (epi == wg::kEpiSwigluPairs && (M > wg::kGemvMaxTokens || push || m->d.N % 16))
     return fail(ctx, WG_UNSUPPORTED, "the SwiGLU-pairs epilogue takes at most %d rows, N %% 16 == 0 (M %d, N %d)",
                 wg::kGemvMaxTokens, M, m->d.N);
+  if (epi == wg::kEpiResidual && (M > wg::kProMaxTokens || push || m->d.N % 16 || !stats))
+    return fail(ctx, WG_UNSUPPORTED, "the residual epilogue takes at most %d rows, N %% 16 == 0 (M %d, N %d)",
+                wg::kProMaxTokens, M, m->d.N);
   if (push && M > wg::kGemvMaxTokens)
     return fail(ctx, WG_UNSUPPORTED, "a pushing matmul takes at most %d rows (got %d)", wg::kGemvMaxTokens, M);
   // Many rows: the tcgen05 GEMM (src/engine.ts:4684: more rows than the
@@ -522,8 +526,10 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
   // does a norm whose row statistics would cost every CTA more than
   // ctx->norm_fuse_bytes of reads (each CTA of the fused form reads all of a
   // and b for them; 64 KB by default, WG_NORM_FUSE_BYTES for measurement).
-  const bool heavy_norm =
-      pro && pro->kind == wg::kProRmsNorm && (size_t)M * K * 4 * (pro->b ? 2 : 1) > ctx->norm_fuse_bytes;
+  const bool heavy_norm = pro && pro->kind == wg::kProRmsNorm && !pro->stats &&
+                          (size_t)M * K * 4 * (pro->b ? 2 : 1) > ctx->norm_fuse_bytes;
+  if (pro && pro->stats && M > wg::kProMaxTokens)
+    return fail(ctx, WG_UNSUPPORTED, "a norm from stats takes at most %d rows (got %d)", wg::kProMaxTokens, M);
   if (pro && (M > wg::kProMaxTokens || heavy_norm)) {
     st = ensure_work(ctx, (size_t)M * K * 2);
     if (st) return st;
@@ -562,11 +568,14 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
       a.push = push->dev;
     }
     a.epi = epi;
+    a.stats = stats;
     wg::GemvArgs w = a;
-    if (wg::gemv_use_wide(ctx, a) && wg::plan_gemv_wide(w, ctx->num_sms)) {
+    if ((epi == wg::kEpiResidual || wg::gemv_use_wide(ctx, a)) && wg::plan_gemv_wide(w, ctx->num_sms)) {
       WG_CUDA(ctx, wg::launch_gemv_wide(w, ctx->stream, ctx->pdl));
       continue;
     }
+    if (epi == wg::kEpiResidual)  // the residual epilogue lives in the wide kernel
+      return fail(ctx, WG_UNSUPPORTED, "no wide GEMV plan for the residual epilogue (K = %d)", m->d.K);
     if (!wg::plan_gemv(a, ctx->num_sms))
       return fail(ctx, WG_UNSUPPORTED, "K = %d is beyond the GEMV's largest cluster split", m->d.K);
     WG_CUDA(ctx, wg::launch_gemv(a, ctx->stream, ctx->pdl));
@@ -584,6 +593,7 @@ int to_prologue(wg_ctx *ctx, const wg_prologue *pro, const char *who, wg::Prolog
   p->w = pro->weight;
   p->eps = pro->eps;
   p->out = pro->resid_out;
+  p->stats = pro->stats;
   if (p->kind != WG_PRO_RMSNORM && p->kind != WG_PRO_SWIGLU)
     return fail(ctx, WG_INVALID_ARGUMENT, "%s: unknown prologue kind %d", who, p->kind);
   if (!p->a || (p->kind == WG_PRO_RMSNORM && !p->w))
@@ -592,7 +602,10 @@ int to_prologue(wg_ctx *ctx, const wg_prologue *pro, const char *who, wg::Prolog
     return fail(ctx, WG_INVALID_ARGUMENT, "%s: prologue tensors must be 16-byte aligned", who);
   if (p->out && (p->out == p->a || (p->b && p->out == p->b)))
     return fail(ctx, WG_INVALID_ARGUMENT, "%s: resid_out must not alias the residual or the addend", who);
-  if (p->kind == WG_PRO_SWIGLU) p->b = nullptr, p->w = nullptr, p->out = nullptr;
+  if (p->stats && (p->kind != WG_PRO_RMSNORM || p->b || p->out || !aligned16(p->stats)))
+    return fail(ctx, WG_INVALID_ARGUMENT,
+                "%s: stats take a RMSNORM prologue without b and resid_out, 16-byte aligned", who);
+  if (p->kind == WG_PRO_SWIGLU) p->b = nullptr, p->w = nullptr, p->out = nullptr, p->stats = nullptr;
   return WG_OK;
 }
 
@@ -662,6 +675,23 @@ int wg_q4_matmul_ex(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, cons
   if (!x || !aligned16(x)) return fail(ctx, WG_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer");
   if (x_dtype < WG_F32 || x_dtype > WG_BF16) return fail(ctx, WG_INVALID_ARGUMENT, "unknown x dtype %d", x_dtype);
   return run_matmul(ctx, m, x, x_dtype, M, y, y_dtype, nullptr, nullptr, epi);
+}
+
+int wg_q4_matmul_residual(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, const void *x, int x_dtype,
+                          int M, float *resid, float *stats) {
+  if (!ctx || !m) return fail(ctx, WG_INVALID_ARGUMENT, "wg_q4_matmul_residual: null argument");
+  int st = check_matmul(ctx, m, M, resid, WG_F32);
+  if (st) return st;
+  if (M == 0) return WG_OK;
+  if (!stats || !aligned16(stats)) return fail(ctx, WG_INVALID_ARGUMENT, "stats must be a 16-byte aligned pointer");
+  if (pro) {
+    wg::Prologue p;
+    if ((st = to_prologue(ctx, pro, "wg_q4_matmul_residual", &p))) return st;
+    return run_matmul(ctx, m, nullptr, WG_F16, M, resid, WG_F32, &p, nullptr, wg::kEpiResidual, stats);
+  }
+  if (!x || !aligned16(x)) return fail(ctx, WG_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer");
+  if (x_dtype < WG_F32 || x_dtype > WG_BF16) return fail(ctx, WG_INVALID_ARGUMENT, "unknown x dtype %d", x_dtype);
+  return run_matmul(ctx, m, x, x_dtype, M, resid, WG_F32, nullptr, nullptr, wg::kEpiResidual, stats);
 }
 
 int wg_q4_matmul_fused(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro, int M, void *y, int y_dtype) {

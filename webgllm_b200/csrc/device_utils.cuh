@@ -170,6 +170,19 @@ __device__ __forceinline__ void unpack_codes(uint32_t w, uint32_t lo_g, uint32_t
   P[3] = hfma2_u(and_or(w8, 0x00F000F0u, kMagic), kSixteenth, hi_g8);
 }
 
+// One word of codes -> the raw pairs (1024 + q) (e 0-1 of each row, from the
+// low nibbles) and (64 + q) (e 2-3, from the high nibbles: the exponent of
+// 64.0h puts mantissa bits 4-7 at weight 1), exact fp16, in P's order; the
+// offsets (1024 + z, 64 + z) are subtracted by a second MMA against the same
+// activations (tile_mma).
+__device__ __forceinline__ void unpack_codes_raw(uint32_t w, uint32_t P[4]) {
+  const uint32_t w8 = w >> 8;
+  P[0] = and_or(w, 0x000F000Fu, 0x64006400u);
+  P[1] = and_or(w, 0x00F000F0u, 0x54005400u);
+  P[2] = and_or(w8, 0x000F000Fu, 0x64006400u);
+  P[3] = and_or(w8, 0x00F000F0u, 0x54005400u);
+}
+
 __device__ __forceinline__ float clamp_half(float v) { return fminf(fmaxf(v, -65504.0f), 65504.0f); }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

@@ -45,8 +45,12 @@ namespace wg {
 
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kStages = 4;         // tensor-memory A stages (dequantised weights)
 constexpr int kMaxSplits = 8;  // K splits of a tile: one portable thread-block cluster
+// Shared-memory stages (x + codes) per tile height: as many as keep two CTAs
+// an SM (one for BM = 256), so that a CTA's whole K range of a small-M split
+// (8 tiles) is in flight at once.
+__host__ __device__ constexpr int smem_stages(int BM) { return BM <= 64 ? 8 : (BM <= 128 ? 5 : 4); }
 constexpr int kBN = 128;          // weight rows per CTA = MMA M
 constexpr int kDequantWarps = 8;  // warps 2..9
 constexpr int kGemmThreads = (2 + kDequantWarps) * 32;
@@ -70,13 +74,14 @@ struct GemmSmem {
 
 __host__ __device__ inline GemmSmem gemm_smem(int BM) {
   GemmSmem s;
+  const int S = smem_stages(BM);
   s.x = 0;  // 1024-aligned (SW128 atoms)
-  s.nib = s.x + kStages * kXStageBytes(BM);
-  s.scl = s.nib + kStages * kNibStageBytes;
-  s.zro = s.scl + kStages * kSclStageBytes;
-  s.bar = s.zro + kStages * kZroStageBytes;
-  // wfull[S] (weights), xfull[S] (x), empty[S], afull[S], accfull
-  s.tmem_slot = s.bar + (4 * kStages + 1) * 8;
+  s.nib = s.x + S * kXStageBytes(BM);
+  s.scl = s.nib + S * kNibStageBytes;
+  s.zro = s.scl + S * kSclStageBytes;
+  s.bar = s.zro + S * kZroStageBytes;
+  // wfull[S] (weights), xfull[S] (x), sempty[S], afull[T], tempty[T], accfull
+  s.tmem_slot = s.bar + (3 * S + 2 * kStages + 1) * 8;
   s.total = s.tmem_slot + 16;
   return s;
 }
@@ -179,9 +184,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ float ld_cluster_f32(uint32_t caddr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(caddr) : "memory");
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t caddr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(caddr)
+               : "memory");
   return v;
 }
 
@@ -198,11 +206,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // weights and x of a stage complete separately: the dequantisers start on
   // prefetched weights while x is still waiting for its producer
+  constexpr int S = smem_stages(BM), T = kStages;
   uint64_t *wfull = reinterpret_cast<uint64_t *>(smem + L.bar);
-  uint64_t *xfull = wfull + kStages;
-  uint64_t *empty = xfull + kStages;
-  uint64_t *afull = empty + kStages;
-  uint64_t *accfull = afull + kStages;
+  uint64_t *xfull = wfull + S;
+  uint64_t *sempty = xfull + S;  // shared-memory stage free (the MMA that read it is done)
+  uint64_t *afull = sempty + S;  // tensor-memory A stage written
+  uint64_t *tempty = afull + T;  // tensor-memory A stage free
+  uint64_t *accfull = tempty + T;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
   __shared__ int aborted;
 
@@ -215,11 +225,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     aborted = 0;
-    for (int i = 0; i < kStages; i++) {
+    for (int i = 0; i < S; i++) {
       mbar_init(&wfull[i], 1);
       mbar_init(&xfull[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&sempty[i], 1);
+    }
+    for (int i = 0; i < T; i++) {
       mbar_init(&afull[i], kDequantWarps);
+      mbar_init(&tempty[i], 1);
     }
     mbar_init(accfull, 1);
     fence_mbar_init();
@@ -242,26 +255,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t wbytes = kNibStageBytes + kSclStageBytes + (ZEROS ? kZroStageBytes : 0);
       const uint32_t xbytes = kXStageBytes(BM);
       auto load_w = [&](int it) {
-        const int s = it % kStages, kt = kt_begin + it;
+        const int s = it % S, kt = kt_begin + it;
         mbar_expect_tx(&wfull[s], wbytes);
         tma_load_3d(smem + L.nib + s * kNibStageBytes, &tm_nib, 0, kt, nt0, &wfull[s]);
         tma_load_3d(smem + L.scl + s * kSclStageBytes, &tm_scl, 0, kt, nt0, &wfull[s]);
         if (ZEROS) tma_load_3d(smem + L.zro + s * kZroStageBytes, &tm_zro, 0, kt, nt0, &wfull[s]);
       };
       auto load_x = [&](int it) {
-        const int s = it % kStages;
+        const int s = it % S;
         mbar_expect_tx(&xfull[s], xbytes);
         tma_load_2d(smem + L.x + s * kXStageBytes(BM), &tm_x, (kt_begin + it) * kTileK, m0, &xfull[s]);
       };
       // The first stages' weights depend on no earlier kernel: copied (and
       // dequantised) before the dependency wait; x, the previous kernel's
       // output, after it.
-      const int pre = nk < kStages ? nk : kStages;
+      const int pre = nk < S ? nk : S;
       for (int it = 0; it < pre; it++) load_w(it);
       pdl_wait();
       for (int it = 0; it < pre; it++) load_x(it);
       for (int it = pre; it < nk; it++) {
-        wait(&empty[it % kStages], ((it / kStages) & 1) ^ 1);
+        wait(&sempty[it % S], ((it / S) & 1) ^ 1);
         load_w(it);
         load_x(it);
       }
@@ -270,16 +283,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(BM);
       for (int it = 0; it < nk; it++) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        wait(&xfull[s], ph);
-        wait(&afull[s], ph);
+        const int s = it % S, t = it % T;
+        wait(&xfull[s], (it / S) & 1);
+        wait(&afull[t], (it / T) & 1);
         tc_fence_after();
         const uint64_t bdesc = sw128_desc(smem_u32(smem + L.x + s * kXStageBytes(BM)));
 #pragma unroll
         for (int kk = 0; kk < 4; kk++)
-          mma_f16_tmem_a(tmem_d, tmem_a + s * 32 + kk * 8, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&empty[s]);
+          mma_f16_tmem_a(tmem_d, tmem_a + t * 32 + kk * 8, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&sempty[s]);  // x and codes of stage s read (the dequantisers finished before afull)
+        tc_commit(&tempty[t]);
       }
       tc_commit(accfull);
     }
@@ -291,10 +304,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int tile = 2 * q + sub;
     const int g = lane >> 2;
     for (int it = 0; it < nk; it++) {
-      const int s = it % kStages;
-      const uint32_t ph = (it / kStages) & 1;
-      wait(&wfull[s], ph);
-      wait(&empty[s], ph ^ 1);  // the MMA that last read A stage s is done
+      const int s = it % S, t = it % T;
+      wait(&wfull[s], (it / S) & 1);
+      wait(&tempty[t], ((it / T) & 1) ^ 1);  // the MMA that last read A stage t is done
       tc_fence_after();
       const uint4 wv = *reinterpret_cast<const uint4 *>(smem + L.nib + s * kNibStageBytes + tile * kTileNibBytes +
                                                         lane * 16);
@@ -321,11 +333,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         v[4 * j + 2] = hmul2_u(P[2], d_g8);
         v[4 * j + 3] = hmul2_u(P[3], d_g8);
       }
-      tmem_st_16x256b_x4(tmem_a + ((uint32_t)(32 * q + 16 * sub) << 16) + s * 32, v);
+      tmem_st_16x256b_x4(tmem_a + ((uint32_t)(32 * q + 16 * sub) << 16) + t * 32, v);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&afull[s]);
+      if (lane == 0) mbar_arrive(&afull[t]);
     }
 
     // Epilogue: this warp's 32 TMEM lanes (weight rows 32q..32q+31) and half
@@ -365,14 +377,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int C = a.splits;
     uint32_t crank;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
-    const int E = BM * kBN;
-    const int e0 = (int)((long long)E * crank / C), e1 = (int)((long long)E * (crank + 1) / C);
-    const uint32_t red_local = smem_u32(smem + L.x);
+    const int E4 = BM * kBN / 4;  // float4 entries: 4 consecutive weight rows of a token
+    const int e0 = (int)((long long)E4 * crank / C), e1 = (int)((long long)E4 * (crank + 1) / C);
+    uint32_t peer[kMaxSplits];
+    for (int r = 0; r < C; r++) peer[r] = map_rank(smem_u32(smem + L.x), (uint32_t)r);
     for (int e = e0 + (int)threadIdx.x; e < e1; e += kGemmThreads) {
-      float acc = 0.0f;
-      for (int r = 0; r < C; r++) acc += ld_cluster_f32(map_rank(red_local + (uint32_t)e * 4u, (uint32_t)r));
-      const int tok = m0 + e / kBN, nn = nt0 * kTileRows + (e % kBN);
-      if (tok < a.M && nn < a.N) store_out(a.y, a.y_dtype, (size_t)tok * a.N + nn, acc);
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int r = 0; r < C; r++) {
+        const float4 v = ld_cluster_f32x4(peer[r] + (uint32_t)e * 16u);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int tok = m0 + (4 * e) / kBN, nn = nt0 * kTileRows + (4 * e) % kBN;
+      if (tok < a.M && nn < a.N) {  // N % 4 == 0: all four rows or none
+        const size_t o = (size_t)tok * a.N + nn;
+        store_out(a.y, a.y_dtype, o, acc.x);
+        store_out(a.y, a.y_dtype, o + 1, acc.y);
+        store_out(a.y, a.y_dtype, o + 2, acc.z);
+        store_out(a.y, a.y_dtype, o + 3, acc.w);
+      }
     }
     cluster_sync_all();  // no CTA leaves while a peer still reads its tile
   }
@@ -386,9 +411,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // No TMA may still be writing this CTA's shared memory when it exits (only
   // possible after a timed-out wait): wait for the last round of each stage.
   if (threadIdx.x == 0 && aborted) {
-    for (int it = nk > kStages ? nk - kStages : 0; it < nk; it++) {
-      mbar_wait_bounded(&wfull[it % kStages], (it / kStages) & 1, a.flags);
-      mbar_wait_bounded(&xfull[it % kStages], (it / kStages) & 1, a.flags);
+    for (int it = nk > S ? nk - S : 0; it < nk; it++) {
+      mbar_wait_bounded(&wfull[it % S], (it / S) & 1, a.flags);
+      mbar_wait_bounded(&xfull[it % S], (it / S) & 1, a.flags);
     }
   }
 }
@@ -743,6 +768,7 @@ cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream, boo
   const GemmSmem L = gemm_smem(BM);
   auto kern = gemm_kernel<BM, ZEROS>;
   static_assert(BM <= tmem_a_col(BM) && tmem_a_col(BM) + kStages * 32 <= tmem_cols(BM), "TMEM columns");
+  static_assert(BM * kBN * 4 <= smem_stages(BM) * kXStageBytes(BM), "the split-K staging tile fits the x ring");
   const int smem_bytes = L.total + 1024 > min_smem(BM) ? L.total + 1024 : min_smem(BM);
   static bool configured = false;
   if (!configured) {

@@ -43,6 +43,10 @@ namespace wg {
 
 namespace {
 
+// Codes unpacked to raw (1024 + q) / (64 + q) pairs with the offsets taken
+// off by a second MMA (5 instead of 9 instructions a word, one more MMA a K
+// step; up to 16 rows), or to exact (q - z) pairs.
+constexpr bool kRawUnpack = true;
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxTilesPerWarp = 8;
@@ -123,7 +127,10 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
     for (int js = 0; js < 2; js++) {
       const int j = 2 * bsel + js;
       uint32_t P[4];
-      unpack_codes(w[j], lo_g, hi_g, lo_g8, hi_g8, P);
+      if (kRawUnpack && NG <= 2)
+        unpack_codes_raw(w[j], P);
+      else
+        unpack_codes(w[j], lo_g, hi_g, lo_g8, hi_g8, P);
 #pragma unroll
       for (int ng = 0; ng < NG; ng++) {
         const int tok = ng * 8 + g;
@@ -131,6 +138,8 @@ __device__ __forceinline__ void tile_mma(const uint8_t *s_nib, const uint8_t *s_
         if (tok < M) b = *reinterpret_cast<const uint2 *>(xt + (size_t)tok * stride + 16 * j);
         // fragment k {2t,2t+1 | 2t+8,2t+9} <-> K offset {4t,4t+1 | 4t+2,4t+3}
         mma_16816(blk[SPLIT ? js : 0][ng], P[0], P[2], P[1], P[3], b.x, b.y);
+        // raw codes: minus (1024 + z) x on e 0-1 and (64 + z) x on e 2-3
+        if (kRawUnpack && NG <= 2) mma_16816(blk[SPLIT ? js : 0][ng], lo_g ^ 0x80008000u, lo_g8 ^ 0x80008000u, hi_g, hi_g8, b.x, b.y);
       }
     }
     const uint32_t sp = bsel ? sv.y : sv.x;
@@ -181,6 +190,28 @@ __device__ __forceinline__ void emit_pair(const GemvArgs &a, int nt, int r, int 
   store_out(a.y, a.y_dtype, (size_t)tok * (a.N / 2) + f, silu_mul(gate, up));
 }
 
+// The residual epilogue (kEpiResidual): y fp32 [M][N] += v, returning the
+// new value (0 for padding rows and tokens past M, which add nothing to the
+// statistics).
+__device__ __forceinline__ float emit_residual(const GemvArgs &a, int nt, int r, int tok, float v) {
+  const int n = nt * kTileRows + r;
+  if (n >= a.N || tok >= a.M) return 0.0f;
+  float *y = reinterpret_cast<float *>(a.y) + (size_t)tok * a.N + n;
+  v += *y;
+  *y = v;
+  return v;
+}
+
+// Tile nt's statistics from sq[r * 8 + tok] = (new residual)^2 of its 16
+// rows (one token group): stats[nt][tok] = the sum over r, in order. Called
+// by threads 0 .. M-1 after a barrier.
+__device__ __forceinline__ void emit_stats(const GemvArgs &a, int nt, int tok, const float *sq) {
+  float t = 0.0f;
+#pragma unroll
+  for (int r = 0; r < kTileRows; r++) t += sq[r * 8 + tok];
+  a.stats[(size_t)nt * a.M + tok] = t;
+}
+
 // Eight consecutive x values (row m, columns k..k+7) as fp16, made by the
 // prologue: (residual + b) * inv * w for the norm, silu(gate) * up for SwiGLU.
 template <int PRO>
@@ -215,6 +246,18 @@ __device__ void rmsnorm_rows(const Prologue &p, int M, int K, float *s_part, flo
   constexpr int kThreads = NW * 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K4 = K / 4;
+  if (p.stats) {
+    // the producer's per-tile sums of squares (a fixed order: deterministic)
+    static_assert(NW >= kProMaxTokens, "a warp per row");
+    if (warp < M) {
+      float t = 0.0f;
+      for (int i = lane; i < K / kTileRows; i += 32) t += p.stats[(size_t)i * M + warp];
+      t = warp_sum_f(t);
+      if (lane == 0) s_inv[warp] = rsqrtf(t / (float)K + p.eps);
+    }
+    __syncthreads();
+    return;
+  }
   for (int m = 0; m < M; m++) {
     const float4 *r = reinterpret_cast<const float4 *>(p.a + (size_t)m * K);
     const float4 *b = p.b ? reinterpret_cast<const float4 *>(p.b + (size_t)m * K) : nullptr;
@@ -579,6 +622,7 @@ __host__ __device__ inline WideSmem wide_smem(int M, int ktc, int S, int J, int 
 
 template <int NG, bool ZEROS, int PRO>
 __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs a) {
+  if (NG != 1 && a.epi == kEpiResidual) return;  // one token group only (the host checks it too)
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = lane & 3;
@@ -692,9 +736,29 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   //    rank c takes entries c, c + C, ... of the chunk.
   constexpr int kOut = 16 * 8 * NG;
   const int Jc = a.part_cols;
+  __shared__ float sq[2][128];  // kEpiResidual: a column's squared new residuals, per warp group
   auto flush = [&](int j0, int j1) {  // columns [j0, j1), all CTAs of the cluster together
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
+    if (a.epi == kEpiResidual) {
+      // whole columns per rank (column jj to rank jj mod C), so that a
+      // column's statistics sum in one CTA
+      for (int jj = crank; jj < j1 - j0; jj += C) {
+        const int nt = g + (j0 + jj) * G;
+        for (int o = threadIdx.x; o < kOut; o += kWThreads) {
+          const int r = o / (8 * NG), tok = o - r * (8 * NG);
+          float sum = 0.0f;
+          for (int c = 0; c < C; c++) sum += cluster.map_shared_rank(part, c)[jj * kOut + o];
+          const float v = emit_residual(a, nt, r, tok, sum);
+          sq[0][o] = v * v;
+        }
+        __syncthreads();
+        if ((int)threadIdx.x < M) emit_stats(a, nt, threadIdx.x, sq[0]);
+        __syncthreads();
+      }
+      cluster.sync();
+      return;
+    }
     const int per = a.epi == kEpiNone ? kOut : kOut / 2;  // outputs per column
     for (int idx = crank + C * (int)threadIdx.x; idx < (j1 - j0) * per; idx += C * kWThreads) {
       const int jj = idx / per, o = idx - jj * per;
@@ -768,13 +832,21 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
           const int r = o / (8 * NG), tok = o - r * (8 * NG);
           emit(a, parity, nt, r, tok, gsum_at(r, tok));
         }
+      } else if (a.epi == kEpiResidual) {
+        for (int o = gtid; o < kOut; o += 256) {
+          const int r = o / (8 * NG), tok = o - r * (8 * NG);
+          const float v = emit_residual(a, nt, r, tok, gsum_at(r, tok));
+          sq[grp][o] = v * v;
+        }
+        named_bar_sync(1 + grp, 256);
+        if (gtid < M) emit_stats(a, nt, gtid, sq[grp]);
       } else {
         for (int o = gtid; o < kOut / 2; o += 256) {
           const int r = o / (8 * NG), tok = o - r * (8 * NG);
           emit_pair(a, nt, r, tok, gsum_at(r, tok), gsum_at(r + 8, tok));
         }
       }
-      named_bar_sync(1 + grp, 256);  // the group's half of red is reused next
+      named_bar_sync(1 + grp, 256);  // the group's half of red (and sq) is reused next
     }
     // No copy may still be writing shared memory at exit (only possible
     // after a timed-out wait): the group's last use of each of its stages.
@@ -823,6 +895,14 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
         else
           emit(a, parity, nt, r, tok, sum);
       }
+    } else if (a.epi == kEpiResidual) {
+      for (int o = threadIdx.x; o < kOut; o += kWThreads) {
+        const int r = o / (8 * NG), tok = o - r * (8 * NG);
+        const float v = emit_residual(a, nt, r, tok, warp_sum_at(r, tok));
+        sq[0][o] = v * v;
+      }
+      __syncthreads();
+      if ((int)threadIdx.x < M) emit_stats(a, nt, threadIdx.x, sq[0]);
     } else {
       for (int o = threadIdx.x; o < kOut / 2; o += kWThreads) {
         const int r = o / (8 * NG), tok = o - r * (8 * NG);

@@ -43,6 +43,10 @@ struct Prologue {
   const float *w;  // kProRmsNorm: norm weight [K]
   float eps;
   float *out;      // kProRmsNorm: receives residual + b [M][K], or null
+  // kProRmsNorm: per-16-column-tile sums of squares of a [K/16][M] (written
+  // by a kEpiResidual matmul): the row statistics without reading all of a
+  // (b and out are null then)
+  const float *stats;
 };
 // Rows of one fused GEMV launch (the prologue needs the whole row per CTA).
 constexpr int kProMaxTokens = 8;
@@ -72,10 +76,12 @@ struct GemvArgs {
   int part_cols;   // wide GEMV with a K split: columns reduced across the cluster at a time
   int push_on;     // outputs go to every rank's exchange buffer (comm.cuh), not y
   CommDev push;
-  int epi;         // kEpiNone, or kEpiSwigluPairs: y [M][N/2] = silu(rows 16t..16t+7) * rows 16t+8..16t+15
+  int epi;         // kEpiNone, or kEpiSwigluPairs: y [M][N/2] = silu(rows 16t..16t+7) * rows 16t+8..16t+15,
+                   // or kEpiResidual: y fp32 [M][N] += the product, stats [N/16][M] = per-tile sums of squares
+  float *stats;    // kEpiResidual
   int wide_groups; // wide GEMV without a K split: two 8-warp groups take alternate columns
 };
-enum EpiKind { kEpiNone = 0, kEpiSwigluPairs = 1 };
+enum EpiKind { kEpiNone = 0, kEpiSwigluPairs = 1, kEpiResidual = 2 };
 
 constexpr int kGemvMaxTokens = 32;
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl);

@@ -211,6 +211,9 @@ class DecoderModel:
         self.o = torch.zeros((R, D), device="cuda")
         self.gu = torch.zeros((R, 2 * Il), device="cuda")
         self.act = torch.zeros((R, Il), dtype=torch.float16, device="cuda")
+        # the norm statistics a residual-epilogue matmul leaves for the next
+        # norm: [D / 16][rows] sums of squares (decode batches of 2-8 rows)
+        self.stats = torch.zeros((D // 16, 8), device="cuda")
         self.logits = torch.zeros((B, self.V), device="cuda")
         self.keys = torch.zeros(B, dtype=torch.int64, device="cuda")
         self.pos = torch.zeros(B, dtype=torch.int32, device="cuda")
@@ -226,6 +229,7 @@ class DecoderModel:
         # first row goes (None: not kept)
         self.conv_prefixes = None
         self.prefix_slot = None
+        self._resid_mode, self._resid = False, None  # inside _forward_residual
         # row-parallel exchange: the push all-reduce for decode rows, NCCL
         # for the rest (and for everything when push is False)
         self.comm = None
@@ -337,6 +341,19 @@ class DecoderModel:
             self.comm.close()
             self.comm = None
 
+    def _residual(self, lin: Linear, x: torch.Tensor, resid: torch.Tensor, rows: int):
+        """resid += x . W^T in the matmul's epilogue, leaving the next norm's
+        statistics in self.stats."""
+        xd = WG_F16 if x.dtype == torch.float16 else WG_F32
+        self._c(_lib.lib().wg_q4_matmul_residual(P(self.ctx.handle), P(lin.m.handle), None, P(x.data_ptr()), xd,
+                                                 rows, P(resid.data_ptr()), P(self.stats.data_ptr())))
+
+    def _stats_norm(self, resid, w):
+        """The prologue x = rmsnorm(resid) * w whose statistics come from the
+        last residual-epilogue matmul."""
+        return _lib.wg_prologue(WG_PRO_RMSNORM, resid.data_ptr(), None, w.data_ptr(), self.cfg.eps, None,
+                                self.stats.data_ptr())
+
     def _convolve(self, lay, rows):
         cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
         s = lay["slot"]
@@ -351,7 +368,10 @@ class DecoderModel:
             self._c(L.wg_short_conv(c, P(self.bcx.data_ptr()), rows, self.batch, cfg.hidden, cfg.conv_width,
                                     P(lay["conv_w"].data_ptr()), P(self.conv_state[s].data_ptr()),
                                     P(self.cv.data_ptr()), WG_F16))
-        self._mm(lay["out"], self.cv, self.o, rows)
+        if self._resid_mode:
+            self._residual(lay["out"], self.cv, self._resid, rows)
+        else:
+            self._mm(lay["out"], self.cv, self.o, rows)
 
     @property
     def has_conv(self) -> bool:
@@ -429,6 +449,8 @@ class DecoderModel:
         D = cfg.hidden
         self.ctx.use_torch_stream()
         self._c(L.wg_embed(c, P(ids.data_ptr()), rows, P(self.embed.data_ptr()), cfg.vocab, D, P(self.x.data_ptr())))
+        if self._use_residual_epilogue(rows):
+            return self._forward_residual(rows)
         cur, other = self.x, self.x2
         fused_ex = self.comm is not None and rows <= 8 and rows * D <= self.comm.slot
         add = None
@@ -469,6 +491,55 @@ class DecoderModel:
                 self._mm_rowpar(lay["down"], rows, x=self.act)
                 normed, add = False, self.o
         self._head(cur, add, rows)
+
+    # Decode batches whose norm statistics would make every CTA of a fused
+    # GEMV read more than this many bytes take the residual epilogue.
+    _NORM_FUSE_BYTES = 64 << 10
+
+    def _use_residual_epilogue(self, rows: int) -> bool:
+        """On one GPU, a decode batch of 2-8 rows whose norms are too large
+        to fuse from the residual alone (each CTA would read rows * D * 8
+        bytes): each layer's residual add runs in the epilogue of the matmul
+        that makes the addend, which leaves the next norm's statistics for
+        the next matmul's prologue — no norm pass of its own."""
+        mode = os.environ.get("WG_RESIDUAL_EPILOGUE", "1")  # 0 off, 1 by size, 2 every batch of 2-8 rows
+        if mode == "0" or self.world != 1 or self.row_picks is not None or self.prefix_slot is not None:
+            return False
+        if not 2 <= rows <= 8 or self.cfg.hidden % 16:
+            return False
+        return mode == "2" or rows * self.cfg.hidden * 8 > self._NORM_FUSE_BYTES
+
+    def _forward_residual(self, rows: int):
+        """The fused forward with the residual add in the epilogues (see
+        _use_residual_epilogue): per layer q|k|v (norm from the statistics)
+        -> attention -> o (+= residual) -> gate|up (norm from the
+        statistics, SwiGLU epilogue) -> down (+= residual); the first
+        layer's norm reads the embedding rows."""
+        cfg, L, c = self.cfg, _lib.lib(), P(self.ctx.handle)
+        cur = self.x
+        self._resid_mode, self._resid = True, cur
+        try:
+            for li, lay in enumerate(self.layers):
+                proj = self.qkv if lay["type"] == "attn" else self.bcx
+                lin = lay["qkv"] if lay["type"] == "attn" else lay["in"]
+                if li == 0:
+                    self._mm_norm(lin, cur, None, lay["norm1"], None, proj, rows)
+                else:
+                    pro = self._stats_norm(cur, lay["norm1"])
+                    self._c(L.wg_q4_matmul_fused(c, P(lin.m.handle), ctypes.byref(pro), rows, P(proj.data_ptr()),
+                                                 WG_F32))
+                if lay["type"] == "attn":
+                    self._rope_attend(lay, rows)
+                    self._residual(lay["o"], self.att, cur, rows)
+                else:
+                    self._convolve(lay, rows)
+                pro = self._stats_norm(cur, lay["norm2"])
+                self._c(L.wg_q4_matmul_ex(c, P(lay["gu"].m.handle), ctypes.byref(pro), None, WG_F16, rows,
+                                          P(self.act.data_ptr()), WG_F16, _lib.WG_EPI_SWIGLU_PAIRS))
+                self._residual(lay["down"], self.act, cur, rows)
+        finally:
+            self._resid_mode, self._resid = False, None
+        self._head(cur, None, rows)
 
     def _forward_passes(self, ids: torch.Tensor, rows: int):
         """One launch per engine pass (norm, matmul, SwiGLU, ... each on its
