@@ -47,10 +47,11 @@ namespace {
 
 constexpr int kStages = 4;         // tensor-memory A stages (dequantised weights)
 constexpr int kMaxSplits = 8;  // K splits of a tile: one portable thread-block cluster
-// Shared-memory stages (x + codes) per tile height: as many as keep two CTAs
-// an SM (one for BM = 256), so that a CTA's whole K range of a small-M split
-// (8 tiles) is in flight at once.
-__host__ __device__ constexpr int smem_stages(int BM) { return BM <= 64 ? 8 : (BM <= 128 ? 5 : 4); }
+// Shared-memory stages (x + codes) per tile height: at BM = 64 a split's
+// whole K range (8 tiles) is in flight at once within the two-CTAs-an-SM
+// budget; larger tiles keep 4 (measured at M = 1024: 5 stages 45.5 us, 4
+// stages 42.4 us).
+__host__ __device__ constexpr int smem_stages(int BM) { return BM <= 64 ? 8 : 4; }
 constexpr int kBN = 128;          // weight rows per CTA = MMA M
 constexpr int kDequantWarps = 8;  // warps 2..9
 constexpr int kGemmThreads = (2 + kDequantWarps) * 32;

@@ -45,8 +45,12 @@ namespace {
 
 // Codes unpacked to raw (1024 + q) / (64 + q) pairs with the offsets taken
 // off by a second MMA (5 instead of 9 instructions a word, one more MMA a K
-// step; up to 16 rows), or to exact (q - z) pairs.
-constexpr bool kRawUnpack = true;
+// step; up to 16 rows), or to exact (q - z) pairs. Measured on B200 (64-launch
+// graphs): raw is slower — M = 1 at 4096^2 4.18 -> 4.67 us, M = 16 8.6 ->
+// 9.9 us, config-4 decode step 3.19 -> 3.34 ms: the second mma.sync costs
+// more tensor-pipe time (one per ~10 cycles a sub-partition) than the four
+// ALU instructions it saves. Kept off.
+constexpr bool kRawUnpack = false;
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxTilesPerWarp = 8;
