@@ -53,13 +53,8 @@ constexpr int kMaxSplits = 8;  // K splits of a tile: one portable thread-block 
 // stages 42.4 us).
 __host__ __device__ constexpr int smem_stages(int BM) { return BM <= 64 ? 8 : 4; }
 constexpr int kBN = 128;          // weight rows per CTA = MMA M
-constexpr int kDequantWarps = 8;  // warps that dequantise one stage (a 128-row weight tile)
-constexpr int kGemmThreads = (2 + kDequantWarps) * 32;  // the 2-SM kernel's block
-// The 1-SM kernel: two groups of 8 dequantising warps take alternate stages
-// (warps 2..9 the even ones, 10..17 the odd), all 16 then share the
-// epilogue.
-constexpr int kDequantGroups = 2;
-constexpr int kGemm1Threads = (2 + kDequantGroups * kDequantWarps) * 32;
+constexpr int kDequantWarps = 8;  // warps 2..9
+constexpr int kGemmThreads = (2 + kDequantWarps) * 32;
 constexpr int kXStageBytes(int BM) { return BM * 128; }
 constexpr int kNibStageBytes = 8 * kTileNibBytes;  // 4096
 constexpr int kSclStageBytes = 8 * kTileSclBytes;  // 512
@@ -200,7 +195,7 @@ __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t caddr) {
 }
 
 template <int BM, bool ZEROS>
-__global__ void __launch_bounds__(kGemm1Threads, 2)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_nib,
                 const __grid_constant__ CUtensorMap tm_scl, const __grid_constant__ CUtensorMap tm_zro,
                 const GemmArgs a) {
@@ -303,16 +298,13 @@ __global__ void __launch_bounds__(kGemm1Threads, 2)
       tc_commit(accfull);
     }
   } else {
-    // Dequantisers: warp w of group grp handles tile 2q + sub (16 rows) of
-    // every stage it = grp (mod kDequantGroups), q = w % 4 its TMEM lane
-    // quarter.
-    const int dw = warp - 2;
-    const int grp = dw >> 3;
+    // Dequantisers: warp w handles tile 2q + sub of each stage (16 rows),
+    // q = w % 4 its TMEM lane quarter.
     const int q = warp & 3;
-    const int sub = (dw >> 2) & 1;
+    const int sub = (warp - 2) >> 2;
     const int tile = 2 * q + sub;
     const int g = lane >> 2;
-    for (int it = grp; it < nk; it += kDequantGroups) {
+    for (int it = 0; it < nk; it++) {
       const int s = it % S, t = it % T;
       wait(&wfull[s], (it / S) & 1);
       wait(&tempty[t], ((it / T) & 1) ^ 1);  // the MMA that last read A stage t is done
@@ -349,15 +341,14 @@ __global__ void __launch_bounds__(kGemm1Threads, 2)
       if (lane == 0) mbar_arrive(&afull[t]);
     }
 
-    // Epilogue: this warp's 32 TMEM lanes (weight rows 32q..32q+31) and a
-    // quarter of the token columns: into y, or (K split over the cluster) into this
+    // Epilogue: this warp's 32 TMEM lanes (weight rows 32q..32q+31) and half
+    // of the token columns: into y, or (K split over the cluster) into this
     // CTA's staging tile red[token][128 rows] over the idle ring.
     wait(accfull, 0);
     tc_fence_after();
     pdl_wait();  // y may still be read by an earlier kernel until it completes
     const int n = nt0 * kTileRows + 32 * q + lane;
-    const int quarter = dw >> 2;  // this warp's quarter of the token columns
-    const int c_begin = quarter * (BM / 4), c_end = c_begin + BM / 4;
+    const int c_begin = sub * (BM / 2), c_end = c_begin + BM / 2;
     float *red = reinterpret_cast<float *>(smem + L.x);
     for (int c = c_begin; c < c_end; c += 16) {
       float v[16];
@@ -391,7 +382,7 @@ __global__ void __launch_bounds__(kGemm1Threads, 2)
     const int e0 = (int)((long long)E4 * crank / C), e1 = (int)((long long)E4 * (crank + 1) / C);
     uint32_t peer[kMaxSplits];
     for (int r = 0; r < C; r++) peer[r] = map_rank(smem_u32(smem + L.x), (uint32_t)r);
-    for (int e = e0 + (int)threadIdx.x; e < e1; e += kGemm1Threads) {
+    for (int e = e0 + (int)threadIdx.x; e < e1; e += kGemmThreads) {
       float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       for (int r = 0; r < C; r++) {
         const float4 v = ld_cluster_f32x4(peer[r] + (uint32_t)e * 16u);
@@ -794,7 +785,7 @@ cudaError_t launch_bm(const GemmArgs &a, const void *x, cudaStream_t stream, boo
   if (ZEROS && !encode_plane(&tz, a.zro, kTileZroBytes / 4, a.KT, a.NT)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((a.NT + 7) / 8), (unsigned)((a.M + BM - 1) / BM), (unsigned)a.splits);
-  cfg.blockDim = dim3(kGemm1Threads);
+  cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = (size_t)smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute at[2];
