@@ -664,12 +664,19 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   };
   auto issue = [&](int j) { issue_to(j, j % S); };
 
-  // 1. Weight copies of the first S columns: they depend on nothing the
-  //    previous kernel writes.
+  // 1. Weight copies of the first column: they depend on nothing the
+  //    previous kernel writes. With fp16 x (one bulk copy a row) the other
+  //    first S columns follow x's copies (below): copies issued ahead of x's
+  //    would delay it by their bytes at this SM's share of HBM (measured on
+  //    B200, M = 8 chains: 6144x4096 7.14 -> 6.46 us, 28672x4096 19.8 ->
+  //    18.2 us, 4096x14336 15.8 -> 14.5 us with x first).
   if (threadIdx.x == 0) {
     for (int st = 0; st <= S; st++) mbar_init(&bars[st], 1);  // stages and x
     fence_mbar_init();
-    for (int j = 0; j < min(S, J); j++) issue(j);
+    // (x made by a prologue is loads and arithmetic, not a copy: all S
+    // columns go first then; measured on the config-4 decode step, issuing
+    // them after its x staging was 1 % slower)
+    for (int j = 0; j < (x_bulk ? min(1, J) : min(S, J)); j++) issue(j);
   }
   __syncthreads();
   if (a.trace && threadIdx.x == 0) ts[1] = globaltimer();
@@ -693,6 +700,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
       for (int m = 0; m < M; m++)
         bulk_g2s(xs + (size_t)m * L.xstride, reinterpret_cast<const __half *>(a.x) + (size_t)m * a.K + kbase,
                  kcols * 2, xbar);
+      for (int j = 1; j < min(S, J); j++) issue(j);  // the rest of the first S columns, after x
     }
     // the partial last tile reads zeros past K
     const int tail = ktc * kTileK - kcols;
