@@ -227,11 +227,14 @@ def test_config1_sweep(s, M):
 @pytest.mark.parametrize("M,N,K", [
     (33, 128, 128),      # smallest GEMM row count, one CTA
     (64, 128, 128),
-    (64, 512, 4096),     # few tiles: K split across CTAs (fp32 workspace)
+    (64, 512, 4096),     # few tiles: K split across CTAs (a cluster, reduced on chip)
+    (256, 4096, 4096),   # config 1's M = 256: a 4-way K split
     (65, 128, 256),      # second token tile, partial
     (129, 100, 96),      # N not a multiple of 128 (TMA fills), K % 64 == 32
     (300, 1024, 2048),
-    (1024, 512, 512),
+    (1024, 512, 512),    # few tiles: a 2-way K split
+    (1024, 4096, 1024),  # K unsplit, 256 CTAs
+    (520, 4144, 2080),   # the last weight tile partial (N % 128 = 48), K % 64 == 32
     (96, 2560, 2048),    # a q|k|v-shaped matrix
 ])
 def test_gemm_parity(M, N, K):
@@ -241,8 +244,9 @@ def test_gemm_parity(M, N, K):
     check_close(y, O.c_prefill_emulate(host, x16), f"GEMM {M}x{N}x{K} vs f16 route")
 
 
-def test_gemm_zero_points():
-    N, K, M = 256, 1024, 100
+@pytest.mark.parametrize("M,N", [(100, 256), (600, 4096)])  # K split / unsplit
+def test_gemm_zero_points(M, N):
+    K = 1024
     quant, scales, zp = _nbits(N, K, 8)
     m = wg.newQuantMatrix(N, K, withZeros=True)
     wg.packMatMulNBits(m, 0, quant, scales, zp, N)
