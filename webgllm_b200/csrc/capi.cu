@@ -507,6 +507,10 @@ int run_matmul(wg_ctx *ctx, const wg_q4mat *m, const void *x, int x_dtype, int M
     g.KT = m->d.KT;
     g.y_dtype = y_dtype;
     g.flags = ctx->d_flags;
+    g.trace = ctx->trace;
+    g.trace_next = ctx->d_trace_next;
+    g.trace_cap = ctx->trace_cap;
+    g.launch_index = ctx->launch_index++;
     wg::plan_gemm(g, ctx->num_sms);
     const size_t xh_bytes = (x_dtype == WG_F16 && !pro) ? 0 : align_up((size_t)M * K * 2, 256);
     st = ensure_work(ctx, xh_bytes);

@@ -216,6 +216,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *accfull = tempty + T;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
   __shared__ int aborted;
+  __shared__ unsigned long long ts[6];  // wg_trace timestamps
+  if (a.trace && threadIdx.x == 0) ts[0] = globaltimer();
 
   const int nt0 = blockIdx.x * (kBN / kTileRows);  // first 16-row tile
   const int m0 = blockIdx.y * BM;
@@ -272,7 +274,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // output, after it.
       const int pre = nk < S ? nk : S;
       for (int it = 0; it < pre; it++) load_w(it);
+      if (a.trace) ts[1] = globaltimer();
       pdl_wait();
+      if (a.trace) ts[2] = globaltimer();
       for (int it = 0; it < pre; it++) load_x(it);
       for (int it = pre; it < nk; it++) {
         wait(&sempty[it % S], ((it / S) & 1) ^ 1);
@@ -286,6 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int it = 0; it < nk; it++) {
         const int s = it % S, t = it % T;
         wait(&xfull[s], (it / S) & 1);
+        if (a.trace && it == 0) ts[3] = globaltimer();
         wait(&afull[t], (it / T) & 1);
         tc_fence_after();
         const uint64_t bdesc = sw128_desc(smem_u32(smem + L.x + s * kXStageBytes(BM)));
@@ -345,6 +350,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // of the token columns: into y, or (K split over the cluster) into this
     // CTA's staging tile red[token][128 rows] over the idle ring.
     wait(accfull, 0);
+    if (a.trace && warp == 2 && lane == 0) ts[4] = globaltimer();
     tc_fence_after();
     pdl_wait();  // y may still be read by an earlier kernel until it completes
     const int n = nt0 * kTileRows + 32 * q + lane;
@@ -408,6 +414,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, tmem_cols(BM));
+  }
+  if (a.trace && threadIdx.x == 0) {
+    ts[5] = globaltimer();
+    trace_record(a.trace, a.trace_next, a.trace_cap, ts, a.launch_index,
+                 (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x);
   }
   // No TMA may still be writing this CTA's shared memory when it exits (only
   // possible after a timed-out wait): wait for the last round of each stage.

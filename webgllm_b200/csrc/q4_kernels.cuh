@@ -103,6 +103,12 @@ struct GemmArgs {
   int splits, kt_per_split;  // K splits of a tile (one thread-block cluster), K tiles each
   unsigned *flags;
   int fwd_relaxed;  // pair kernel: forward A stages with relaxed arrives (measurement knob)
+  // Tracing (wg_trace), as GemvArgs: entry, weight copies issued, x's
+  // producer released, first x stage landed, last multiply done, exit.
+  unsigned long long *trace;
+  unsigned long long *trace_next;
+  unsigned long long trace_cap;
+  unsigned launch_index;
 };
 
 bool gemm_supported();
