@@ -51,6 +51,8 @@ constexpr int kMaxSplits = 8;  // K splits of a tile: one portable thread-block 
 // whole K range (8 tiles) is in flight at once within the two-CTAs-an-SM
 // budget; larger tiles keep 4 (measured at M = 1024: 5 stages 45.5 us, 4
 // stages 42.4 us).
+// (BM = 256, one CTA an SM, measured the same or 1-3 % slower with 6 smem
+// stages and an 8-stage A ring: the waits are not latency.)
 __host__ __device__ constexpr int smem_stages(int BM) { return BM <= 64 ? 8 : 4; }
 constexpr int kBN = 128;          // weight rows per CTA = MMA M
 constexpr int kDequantWarps = 8;  // warps 2..9
@@ -876,7 +878,12 @@ static int gemm_tile_m(int M) {
     if (forced != 64 && forced != 128 && forced != 256) forced = 0;
   }
   if (forced) return forced;
-  return M <= 64 ? 64 : 128;
+  // Measured at 4096 x 4096 (8-launch CUDA graph): M = 128: 14.9 us at BM =
+  // 128, 17.0 at 256; M = 256: 18.1 / 17.4; M = 1024: 45.0 / 40.5; M = 4096:
+  // 161 / 156. A BM = 256 tile issues MMAs of N = 256: the single issuing
+  // thread spends ~80-100 cycles an MMA whatever its N, so N = 128 MMAs
+  // (75 cycles of tensor work each) leave the tensor pipe waiting on issue.
+  return M <= 64 ? 64 : M <= 128 ? 128 : 256;
 }
 
 size_t plan_gemm(GemmArgs &a, int num_sms) {
@@ -885,11 +892,13 @@ size_t plan_gemm(GemmArgs &a, int num_sms) {
   // CTAs of one K range (the pair kernel runs one per SM, the 1-SM kernel two)
   const int tiles = pair ? 2 * ((a.NT + 15) / 16) * ((a.M + BM - 1) / BM)
                          : ((a.NT + 7) / 8) * ((a.M + BM - 1) / BM);
-  // Split K while the grid fits two CTAs per SM (both resident at once: the
-  // shared-memory padding allows two), keeping >= 4 stages per split.
+  // Split K while the grid stays one wave: two CTAs an SM where a CTA holds
+  // 256 TMEM columns (BM <= 128; the shared-memory padding allows two), one
+  // where it holds all 512 (BM = 256), keeping >= 4 stages per split.
   // Measured at 4096 x 4096: M = 64, 17 us with 9 splits vs 19 with 4-5;
   // M = 256, 26 us with 4 splits vs 31 with 2. WG_GEMM_SPLITS overrides
   // (tuning).
+  const int per_sm = pair || tmem_cols(BM) == 512 ? 1 : 2;
   static int force = -1;
   if (force < 0) {
     const char *e = getenv("WG_GEMM_SPLITS");
@@ -899,7 +908,7 @@ size_t plan_gemm(GemmArgs &a, int num_sms) {
   // the 2-SM kernel keeps its workspace and does not split).
   int splits = 1;
   if (!pair)
-    while (splits < kMaxSplits && tiles * (splits + 1) <= 2 * num_sms && a.KT / (splits + 1) >= 4) splits++;
+    while (splits < kMaxSplits && tiles * (splits + 1) <= per_sm * num_sms && a.KT / (splits + 1) >= 4) splits++;
   if (force > 0 && !pair) splits = force < kMaxSplits ? force : kMaxSplits;
   if (splits > a.KT) splits = a.KT;
   a.kt_per_split = (a.KT + splits - 1) / splits;
