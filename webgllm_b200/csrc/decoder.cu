@@ -136,12 +136,15 @@ __global__ void rope_kv_kernel(const float *qkv, int rps, int H, int Hkv, int Dh
 // then HS, are as large as keeps the grid within about one wave.
 // Per slice, tiles of 128 keys (64 for Dh = 256) of K and V are staged in
 // shared memory with cp.async (all copies in flight at once; the first
-// tile's while the queries are made; K rows padded by 16 bytes so that
-// row-strided reads hit distinct banks). Scores: the tile's (head, key)
-// pairs spread over all threads. An online softmax keeps (max, sum, acc)
-// per head. P.V: warp w takes the w-th quarter of the tile's keys, lane l the
-// head dims l*DPL .. +DPL-1, and each V element it loads serves four heads
-// at once; the warps' sums meet in shared memory. The key slices are merged
+// tile's while the queries are made; K and V rows padded by 16 bytes so
+// that row-strided fragment reads hit distinct banks). Both products run on
+// the tensor cores (mma.m16n8k16, fp32 sums), the G query heads as the rows
+// of A (rows >= G zero): scores S = Q K^T, warp w taking key blocks w, w +
+// 4, ... of 8 keys (q and K are fp16 values: the products are exact); an
+// online softmax keeps (max, sum) per head in fp32; then O += P V, warp w
+// owning head dims [w Dh / 4, (w + 1) Dh / 4) in registers across tiles,
+// with P split as fp16 hi + lo (two MMAs: fp32-level precision) and V read
+// by ldmatrix.trans from the key-major tile. The key slices are merged
 // at the cluster's leader: every CTA pushes (max, sum, acc) into the
 // leader's shared memory (distributed shared memory stores), one cluster
 // barrier, and the leader writes the outputs. No global scratch: one launch
@@ -151,7 +154,6 @@ constexpr int kAttnCluster = 8;  // largest cluster
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxGroup = 16;
-constexpr int kAttnHeadChunk = 4;
 constexpr int kAttnSliceKeys = 128;  // cache positions per CTA before the keys are split over a cluster
 
 // Keys per tile: 128 (one tile covers a decode step's slice up to 1024
@@ -185,28 +187,16 @@ struct AttnSmem {
     k = o;
     o += (size_t)kAttnTile * (Dh + 8) * 2;
     v = o;
-    o += (size_t)kAttnTile * Dh * 2;
+    o += (size_t)kAttnTile * (Dh + 8) * 2;
     p = o;
-    o += (size_t)G * kAttnTile * 4;
+    o += (size_t)G * (kAttnTile + 8) * 4;
     red = o;
-    o += (size_t)kAttnWarps * G * Dh * 4;
     const size_t gbytes = (size_t)kAttnCluster * (2 * G + G * Dh) * 4;
     alias = o + gbytes > kAttnGatherBudget;
     gather = alias ? k : o;
     total = alias ? (k + gbytes > o ? k + gbytes : o) : o + gbytes;
   }
 };
-
-__device__ __forceinline__ float dot8(uint4 k, const float *q) {
-  const __half2 *h = reinterpret_cast<const __half2 *>(&k);
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const float2 f = __half22float2(h[i]);
-    s += f.x * q[2 * i] + f.y * q[2 * i + 1];
-  }
-  return s;
-}
 
 // DPL consecutive halves from shared memory as floats.
 template <int DPL>
@@ -289,6 +279,46 @@ __device__ __forceinline__ void rope_head(const float *src, const float *nw, flo
   }
 }
 
+__device__ __forceinline__ void attn_mma(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// Four 8x8 fp16 matrices from shared memory, transposed (B fragments of a
+// key-major tile); lane l gives the address of row l & 7 of matrix l >> 3.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t r[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t r[2], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_u32(p)));
+}
+
+// A fragment rows g and g + 8 (g < 16), columns c, c + 1 and c + 8, c + 9
+// of a row-major fp32 matrix with `rows` valid rows, as fp16 pairs (hi) and
+// the remainders (lo): value = hi + lo to ~2^-22 relative.
+__device__ __forceinline__ void a_frag_split(const float *m, int stride, int rows, int g, int c, uint32_t hi[4],
+                                             uint32_t lo[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int row = g + 8 * (i & 1), col = c + 8 * (i >> 1);
+    float2 v = make_float2(0.0f, 0.0f);
+    if (row < rows) v = *reinterpret_cast<const float2 *>(m + (size_t)row * stride + col);
+    const __half2 h = __float22half2_rn(v);
+    const float2 hf = __half22float2(h);
+    hi[i] = half2_bits(h);
+    lo[i] = half2_bits(__float22half2_rn(make_float2(v.x - hf.x, v.y - hf.y)));
+  }
+}
+
 template <int DPL, bool ROPE>  // head dims per lane: Dh = 32 * DPL
 __global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const __half *q, int rps, int H, int Hkv, __half *k_cache, __half *v_cache, int cache_len,
@@ -316,7 +346,9 @@ __global__ void __launch_bounds__(kAttnThreads)
   constexpr int kAttnTile = attn_tile(Dh);
   constexpr int kPerLane = kAttnTile / 32;  // scores per lane in the softmax
   constexpr int vecs = Dh / 8;  // 16-byte vectors per key row
-  constexpr int kstride = Dh + 8;
+  constexpr int kstride = Dh + 8;        // K and V rows (halves)
+  constexpr int pstride = kAttnTile + 8;  // P rows (floats)
+  constexpr int kDw = Dh / kAttnWarps;    // head dims of a warp's P.V (DPL blocks of 8)
   extern __shared__ __align__(16) unsigned char smem[];
   cg::cluster_group cluster = cg::this_cluster();
   // grid: x the cluster's key slices, y KV head x HS head groups, z rows
@@ -332,7 +364,6 @@ __global__ void __launch_bounds__(kAttnThreads)
   float *sm = reinterpret_cast<float *>(smem + lay.m);
   float *sl = reinterpret_cast<float *>(smem + lay.l);
   float *sacc = reinterpret_cast<float *>(smem + lay.acc);
-  float *sred = reinterpret_cast<float *>(smem + lay.red);
   float *sgather = reinterpret_cast<float *>(smem + lay.gather);
 
   const int c = (int)cluster.block_rank();
@@ -350,7 +381,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     for (int i = tid; i < nt * vecs; i += kAttnThreads) {
       const int t = i / vecs, e = i - t * vecs;
       cp_async16(sk + t * kstride + e * 8, kb + (size_t)(tt + t) * Dh + e * 8);
-      cp_async16(sv + t * Dh + e * 8, vb + (size_t)(tt + t) * Dh + e * 8);
+      cp_async16(sv + t * kstride + e * 8, vb + (size_t)(tt + t) * Dh + e * 8);
     }
   };
   // the first tile's keys and values load while the queries are made
@@ -397,11 +428,25 @@ __global__ void __launch_bounds__(kAttnThreads)
   }
   for (int i = tid; i < G * Dh; i += kAttnThreads) sacc[i] = 0.0f;
 
+  const int gq = lane >> 2, tq = lane & 3;  // MMA fragment row group / column pair
+  uint32_t qa[Dh / 16][4];  // A fragments of the queries (heads x dims), made at the first tile
+  float o[DPL][4];          // this warp's dims of O: heads gq, gq + 8 x 8 dims per block
+#pragma unroll
+  for (int b = 0; b < DPL; b++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[b][e] = 0.0f;
   for (int tt = t0; tt < t1; tt += kAttnTile) {
     const int nt = min(kAttnTile, t1 - tt);
+    const int kch = (nt + 15) >> 4;  // 16-key chunks of P.V
     if (tt != t0) {
       __syncthreads();  // previous tile fully consumed
       issue_tile(tt, nt);
+    }
+    // V rows past the tile's keys up to the chunk's end: zero (their P is
+    // 0, and 0 times a stale NaN would not be)
+    for (int i = tid; i < (kch * 16 - nt) * (Dh / 2); i += kAttnThreads) {
+      const int t = nt + i / (Dh / 2), e = i - (t - nt) * (Dh / 2);
+      reinterpret_cast<uint32_t *>(sv + t * kstride)[e] = 0u;
     }
     cp_async_wait_all();
     __syncthreads();
@@ -410,35 +455,49 @@ __global__ void __launch_bounds__(kAttnThreads)
 #pragma unroll
         for (int i = 0; i < DPL; i++) {
           sk[(pnew - tt) * kstride + lane + 32 * i] = __float2half_rn(knew[i]);
-          sv[(pnew - tt) * Dh + lane + 32 * i] = __float2half_rn(vnew[i]);
+          sv[(pnew - tt) * kstride + lane + 32 * i] = __float2half_rn(vnew[i]);
         }
       }
       __syncthreads();
     }
-    // scores of the tile's nt keys for the G heads, spread over all threads
-    // (consecutive threads take consecutive keys of one head: q reads
-    // broadcast), stored at sp[g * tile + t]; slots t >= nt hold -inf
-    for (int i = tid; i < G * nt; i += kAttnThreads) {
-      const int g = i / nt, t = i - g * nt;
-      const uint4 *kr = reinterpret_cast<const uint4 *>(sk + t * kstride);
-      const float *qr = sq + g * Dh;
-      float a0 = 0.0f, a1 = 0.0f;
+    if (tt == t0) {
 #pragma unroll
-      for (int e = 0; e < vecs; e += 2) {
-        a0 += dot8(kr[e], qr + e * 8);
-        if (e + 1 < vecs) a1 += dot8(kr[e + 1], qr + e * 8 + 8);
+      for (int kc = 0; kc < Dh / 16; kc++) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {  // q values are fp16 already: exact
+          const int row = gq + 8 * (i & 1), col = kc * 16 + 2 * tq + 8 * (i >> 1);
+          const float2 v = row < G ? *reinterpret_cast<const float2 *>(sq + row * Dh + col) : make_float2(0.f, 0.f);
+          qa[kc][i] = half2_bits(__float22half2_rn(v));
+        }
       }
-      sp[g * kAttnTile + t] = a0 + a1;
     }
-    if (nt < kAttnTile)
-      for (int i = tid; i < G * (kAttnTile - nt); i += kAttnThreads) {
-        const int g = i / (kAttnTile - nt);
-        sp[g * kAttnTile + nt + (i - g * (kAttnTile - nt))] = -INFINITY;
+    // scores: S[head][key] at sp[head * pstride + key]; keys >= nt -> -inf
+    {
+      const int nblk = (nt + 7) >> 3;
+      for (int nb = warp; nb < nblk; nb += kAttnWarps) {
+        float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const __half *kr = sk + (nb * 8 + gq) * kstride + 2 * tq;
+#pragma unroll
+        for (int kc = 0; kc < Dh / 16; kc++)
+          attn_mma(c4, qa[kc], *reinterpret_cast<const uint32_t *>(kr + kc * 16),
+                   *reinterpret_cast<const uint32_t *>(kr + kc * 16 + 8));
+        const int key = nb * 8 + 2 * tq;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int g = gq + 8 * (i >> 1), t = key + (i & 1);
+          if (g < G) sp[g * pstride + t] = t < nt ? c4[i] : -INFINITY;
+        }
       }
+      const int rest = kAttnTile - 8 * nblk;
+      for (int i = tid; i < G * rest; i += kAttnThreads) {
+        const int g = i / rest;
+        sp[g * pstride + 8 * nblk + (i - g * rest)] = -INFINITY;
+      }
+    }
     __syncthreads();
     // per head: new max, rescale factor, probabilities (one warp per head)
     for (int g = warp; g < G; g += kAttnWarps) {
-      float *pg = sp + g * kAttnTile;
+      float *pg = sp + g * pstride;
       float sv_[kPerLane];
       float mx = -INFINITY;
 #pragma unroll
@@ -446,7 +505,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         sv_[j] = pg[lane + 32 * j];
         mx = fmaxf(mx, sv_[j]);
       }
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      for (int o2 = 16; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
       const float mold = sm[g], mnew = fmaxf(mold, mx);
       float psum = 0.0f;
 #pragma unroll
@@ -464,45 +523,49 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
     }
     __syncthreads();
-    // P.V for this warp's quarter of the tile's keys, four heads per pass
-    // over V
+    // O = O * corr + P V over this warp's dims
     {
-      const int kper = (nt + kAttnWarps - 1) / kAttnWarps;
-      const int kw0 = warp * kper;
-      const int kw1 = min(nt, kw0 + kper);
-      for (int g0 = 0; g0 < G; g0 += kAttnHeadChunk) {
-        float a[kAttnHeadChunk][DPL];
+      const float c_lo = gq < G ? scorr[gq] : 0.0f, c_hi = gq + 8 < G ? scorr[gq + 8] : 0.0f;
 #pragma unroll
-        for (int gg = 0; gg < kAttnHeadChunk; gg++)
+      for (int b = 0; b < DPL; b++) {
+        o[b][0] *= c_lo;
+        o[b][1] *= c_lo;
+        o[b][2] *= c_hi;
+        o[b][3] *= c_hi;
+      }
+      const int d0 = warp * kDw;
+      for (int kc = 0; kc < kch; kc++) {
+        uint32_t phi[4], plo[4];
+        a_frag_split(sp, pstride, G, gq, kc * 16 + 2 * tq, phi, plo);
+        const __half *vr = sv + (kc * 16 + (lane & 15)) * kstride + d0 + (lane >> 4) * 8;
+        if constexpr (DPL == 1) {
+          uint32_t b[2];
+          ldsm_x2_trans(b, sv + (kc * 16 + (lane & 15)) * kstride + d0);
+          attn_mma(o[0], phi, b[0], b[1]);
+          attn_mma(o[0], plo, b[0], b[1]);
+        } else {
 #pragma unroll
-          for (int d = 0; d < DPL; d++) a[gg][d] = 0.0f;
-        for (int t = kw0; t < kw1; t++) {
-          float v[DPL];
-          load_halves<DPL>(sv + t * Dh + lane * DPL, v);
-#pragma unroll
-          for (int gg = 0; gg < kAttnHeadChunk; gg++) {
-            const float pr = g0 + gg < G ? sp[(g0 + gg) * kAttnTile + t] : 0.0f;
-#pragma unroll
-            for (int d = 0; d < DPL; d++) a[gg][d] += pr * v[d];
+          for (int b2 = 0; b2 < DPL; b2 += 2) {
+            uint32_t b[4];
+            ldsm_x4_trans(b, vr + b2 * 8);
+            attn_mma(o[b2], phi, b[0], b[1]);
+            attn_mma(o[b2], plo, b[0], b[1]);
+            attn_mma(o[b2 + 1], phi, b[2], b[3]);
+            attn_mma(o[b2 + 1], plo, b[2], b[3]);
           }
         }
-#pragma unroll
-        for (int gg = 0; gg < kAttnHeadChunk; gg++)
-          if (g0 + gg < G) {
-#pragma unroll
-            for (int d = 0; d < DPL; d++) sred[((size_t)warp * G + g0 + gg) * Dh + lane * DPL + d] = a[gg][d];
-          }
       }
     }
-    __syncthreads();
-    for (int i = tid; i < G * Dh; i += kAttnThreads) {
-      const int g = i / Dh;
-      float s = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; w++) s += sred[(size_t)w * G * Dh + i];
-      sacc[i] = sacc[i] * scorr[g] + s;
-    }
   }
+  // this warp's dims of O into sacc for the merge
+#pragma unroll
+  for (int b = 0; b < DPL; b++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int g = gq + 8 * (i >> 1), d = warp * kDw + b * 8 + 2 * tq + (i & 1);
+      if (g < G) sacc[g * Dh + d] = o[b][i];
+    }
+  __syncthreads();
   // merge the slices at the leader (rank 0): every CTA with keys pushes its
   // (m, l, acc) into the leader's gather slots (stores to distributed shared
   // memory: no round trip), one cluster barrier, and the leader combines them
@@ -521,8 +584,9 @@ __global__ void __launch_bounds__(kAttnThreads)
   cluster.sync();
   if (c != 0) return;  // nothing reads this CTA's shared memory any more
   // weights of each slice per head: w[j][g] = exp(m_j - M) / sum_j' l_j' exp(m_j' - M)
-  // (slices without keys carry none; sred is free scratch now unless the
-  // gather overlays it: then the corr slots hold the per-head sums)
+  // (slices without keys carry none; the weights go to the probability tile,
+  // or to q's slots when the gather overlays the tiles; corr holds the
+  // per-head sums)
   const int nslices = min(CL, (L + per - 1) / max(per, 1));  // slices holding keys
   float *wts = sp;  // G * kAttnCluster floats of the probability tile (free now)
   if (lay.alias) wts = reinterpret_cast<float *>(smem + lay.q);  // q is free too
