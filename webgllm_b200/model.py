@@ -56,7 +56,7 @@ class DecoderConfig:
 
 # Decode batches of up to this many sequences run RoPE + KV append inside the
 # attention launch (WG_FUSED_ROPE_MAX_ROWS overrides: tuning).
-_FUSED_ROPE_MAX_ROWS = int(os.environ.get("WG_FUSED_ROPE_MAX_ROWS", "4"))
+_FUSED_ROPE_MAX_ROWS = int(os.environ.get("WG_FUSED_ROPE_MAX_ROWS", "8"))
 
 # Llama-style 1.1B.
 CONFIG2 = DecoderConfig("llama-1.1b", 22, 2048, 32, 4, 64, 5632, 32000, 1e-5, 1e4)
@@ -305,9 +305,9 @@ class DecoderModel:
         s = lay["slot"]
         kc, vc = self.k_cache[s], self.v_cache[s]
         qn, kn = lay.get("q_norm"), lay.get("k_norm")
-        # decode of a few sequences: one launch (measured: configs 2 / 3 gain
-        # 3-5 %; at batch 8 every CTA's own query RoPE costs more than the
-        # launch it saves: 3.24 vs 3.19 ms a config-4 step)
+        # decode of up to 8 sequences: one launch (measured: configs 2 / 3
+        # gain 3-5 %; config 4 at batch 8, with the tensor-core attention,
+        # 3.07 -> 3.00 ms a step)
         if rows == self.batch and rows <= _FUSED_ROPE_MAX_ROWS and Dh % 64 == 0:
             self._c(L.wg_rope_attention(c, P(self.qkv.data_ptr()), rows, H, Hkv, Dh, P(self.pos.data_ptr()), cfg.theta,
                                         P(qn.data_ptr() if qn is not None else None),
