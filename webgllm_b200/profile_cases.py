@@ -161,6 +161,81 @@ def decode(config: str, batch: int, reps: int):
     print(f"decode config {config} batch {batch}: {us:.1f} us/step (eager)")
 
 
+def exchange(reps: int):
+    """Cost of one push all-reduce of config 4's decode (batch 8) at the
+    tensor-parallel degree of the launch (`python -m torch.distributed.run
+    --nproc-per-node N ... -m webgllm_b200.profile_cases exchange_config4_b8`):
+    the row-parallel GEMV shard pushing its partials + `wg_comm_reduce_norm`,
+    against the same shard GEMV + a local norm, each as a graph of 32
+    iterations replayed `reps` times; max over ranks."""
+    import os
+
+    import torch.distributed as dist
+
+    from .comm import TensorGroup
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    c = context(rank)
+    group = TensorGroup.from_torch(c)
+    comm = group.push_comm()
+    L = _lib.lib()
+    D, M = 4096, 8
+    for name, (N, K) in {"o": (D, D // world), "down": (D, 14336 // world)}.items():
+        m = _q4(N, K, rank)
+        x = torch.randn((M, K), device="cuda").half()
+        r0 = torch.randn((M, D), device="cuda")
+        r1 = torch.empty_like(r0)
+        w = torch.ones(D, device="cuda")
+        xo = torch.empty((M, D), dtype=torch.float16, device="cuda")
+        y = torch.empty((M, D), device="cuda")
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        times = {}
+        for mode in ("push", "local"):
+            with torch.cuda.stream(s):
+                c.use_torch_stream()
+
+                def it():
+                    if mode == "push":
+                        comm.push(m, M, x=x)
+                        comm.reduce_norm(r0, w, 1e-5, r1, xo, M, D)
+                    else:
+                        _lib.check(L.wg_q4_matmul(P(c.handle), P(m.handle), P(x.data_ptr()), _lib.WG_F16, M,
+                                                  P(y.data_ptr()), _lib.WG_F32), c.handle)
+                        _lib.check(L.wg_rmsnorm(P(c.handle), P(r0.data_ptr()), P(y.data_ptr()), P(w.data_ptr()),
+                                                ctypes.c_float(1e-5), M, D, P(xo.data_ptr()), _lib.WG_F16),
+                                   c.handle)
+
+                it()
+                s.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for _ in range(32):
+                        it()
+                g.replay()
+                s.synchronize()
+                dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(s)
+                s.synchronize()
+                t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (32 * reps)], device="cuda", dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                times[mode] = t.item()
+                del g
+        if rank == 0:
+            print(f"TP{world} {name} shard {N}x{K}, M={M}: push GEMV + reduce_norm {times['push']:.2f} us, "
+                  f"GEMV + local norm {times['local']:.2f} us, exchange {times['push'] - times['local']:.2f} us",
+                  flush=True)
+    comm.close()
+    group.close()
+    dist.destroy_process_group()
+
+
 CASES = {
     "gemv_config1_m1": lambda r: gemv(1, 4096, 4096, r),
     "gemv_wide_m8": lambda r: gemv(8, 28672, 4096, r),
@@ -176,6 +251,7 @@ CASES = {
     "head_config4_b8": lambda r: head(8, 4096, 128256, r),
     "decode_config4_b8": lambda r: decode("4", 8, r),
     "decode_config2": lambda r: decode("2", 1, r),
+    "exchange_config4_b8": lambda r: exchange(r),
 }
 
 
