@@ -366,8 +366,9 @@ def test_head_rmsnorm_is_norm_then_head(rows, D, V, with_add):
     assert torch.equal(ids.long(), logits.argmax(dim=1))
 
 
-def test_head_fused_argmax_ties_pick_the_lowest_index():
-    D, V = 64, 5000
+@pytest.mark.parametrize("D", [64, 128])  # the CUDA-core kernel; the TMA-ring tensor-core kernel (D % 128 == 0)
+def test_head_fused_argmax_ties_pick_the_lowest_index(D):
+    V = 5000
     x = torch.ones((1, D), dtype=torch.float16, device="cuda")
     W = torch.zeros((V, D), dtype=torch.float16, device="cuda")
     logits = torch.empty((1, V), device="cuda")

@@ -189,7 +189,8 @@ int wg_head(wg_ctx *ctx, const void *x, int rows, int D, const void *W, int V, f
   if (!x || !W || !logits) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_head: null");
   return finish(ctx,
                 wg::launch_head(x, nullptr, nullptr, nullptr, 0.0f, rows, 1, D, W, V, 0, logits, argmax, nullptr,
-                                ctx->d_reduce, wg::kReduceBytes, ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
+                                ctx->d_reduce, wg::kReduceBytes, ctx->d_count, ctx->d_flags, ctx->num_sms,
+                                ctx->stream, ctx->pdl),
                 "wg_head");
 }
 
@@ -205,7 +206,7 @@ int wg_head_rmsnorm(wg_ctx *ctx, const float *resid, const float *add, const flo
   return finish(ctx,
                 wg::launch_head(nullptr, resid, add, weight, eps, rows, row_stride, D, W, V, vocab_offset, logits,
                                 argmax, reinterpret_cast<unsigned long long *>(keys), ctx->d_reduce, wg::kReduceBytes,
-                                ctx->d_count, ctx->num_sms, ctx->stream, ctx->pdl),
+                                ctx->d_count, ctx->d_flags, ctx->num_sms, ctx->stream, ctx->pdl),
                 "wg_head_rmsnorm");
 }
 

@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "decoder_kernels.cuh"
+#include "tma.cuh"
 #include "device_utils.cuh"
 
 namespace wg {
@@ -884,19 +885,35 @@ __global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm)
   if (threadIdx.x == 0) *count = 0;  // ready for the next launch (stream order)
 }
 
-// The head on tensor cores (D % 32 == 0): a warp computes 16 vocabulary
-// rows against all (up to 8) input rows with mma.m16n8k16, fp32 accumulate.
-// Per 32 dims a lane loads 16 contiguous bytes of each of its two W rows
-// (rows g and g + 8 of the tile, dims 8t .. 8t+7) and uses them as the A
-// fragments of two MMAs; the same K order is read from x (dims 8t + 4j ..
-// 8t + 4j + 3 for MMA j), so W streams with full 64-byte row segments per
-// instruction and no data shuffling. x lives in shared memory (fp16, 8
-// rows, zero past `rows`). Grid: one 16-warp CTA per SM, tiles strided
-// over all warps; the greedy pick as in head_kernel.
+// The head on tensor cores (D % 128 == 0): W streams through a ring of
+// shared-memory stages filled by TMA (one thread issues 2-D tiled copies of
+// 128 vocabulary rows x 64 dims, 16 KB, 128-byte swizzled), so the bytes in
+// flight cost no registers and the first stages are requested before the
+// wait for the previous kernel (W depends on none). 16 compute warps in two
+// groups of 8 take alternate stages of a 128-row block (group g the stages
+// s = g mod 2), warp w of a group 16 of its rows, reading A fragments with
+// ldmatrix from the swizzled stage and x (fp16, 8 rows, zero past `rows`)
+// from shared memory; mma.m16n8k16 with fp32 sums. At the end of a block the
+// second group's sums meet the first's in shared memory and the first
+// writes the logits and keeps each token's best (row, value); then the
+// greedy pick as in head_kernel. A CTA per SM, blocks strided over the CTAs.
 
-constexpr int kHmWarps = 16;
-constexpr int kHmThreads = kHmWarps * 32;
-constexpr int kHmChunks = 4;  // 32-dim chunks per batch of loads (8 x 16 B in flight per lane)
+constexpr int kHtWarps = 16;                    // compute warps; warp 16 issues the copies
+constexpr int kHtThreads = (kHtWarps + 1) * 32;
+constexpr int kHtStages = 8;
+constexpr int kHtRows = 128;                    // vocabulary rows of a block
+constexpr int kHtStageBytes = kHtRows * 128;    // 128 rows x 64 fp16 dims
+
+struct HeadSmem {
+  size_t ring, x, red, bar, total;
+  __host__ __device__ explicit HeadSmem(int D) {
+    ring = 0;  // 1024-aligned (128-byte swizzle atoms)
+    x = ring + (size_t)kHtStages * kHtStageBytes;
+    red = x + (size_t)8 * (D + 8) * 2;
+    bar = red + (size_t)2 * 8 * 32 * 4 * 4;
+    total = bar + (size_t)2 * kHtStages * 8;
+  }
+};
 
 __device__ __forceinline__ void mma_f16_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {
@@ -907,18 +924,63 @@ __device__ __forceinline__ void mma_f16_16816(float c[4], uint32_t a0, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
 template <bool NORM>
-__global__ void __launch_bounds__(kHmThreads, 1)
-    head_mma_kernel(const __half *x, HeadNorm nrm, int rows, int row_stride, int D, const __half *W, int V,
-                    int vocab_offset, float *logits, int32_t *amax, unsigned long long *keys,
-                    unsigned long long *part, unsigned *count) {
+__global__ void __launch_bounds__(kHtThreads, 1)
+    head_tma_kernel(const __grid_constant__ CUtensorMap tm_w, const __half *x, HeadNorm nrm, int rows,
+                    int row_stride, int D, int V, int vocab_offset, float *logits, int32_t *amax,
+                    unsigned long long *keys, unsigned long long *part, unsigned *count, unsigned *flags) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
-  pdl_wait();     // inputs come from the previous kernel
-  extern __shared__ __align__(16) __half xh[];  // [8][D + 16]
-  __shared__ unsigned long long s_key[kHmWarps][8];
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const HeadSmem L(D);
+  uint8_t *ring = smem + L.ring;
+  __half *xh = reinterpret_cast<__half *>(smem + L.x);  // [8][D + 8]
+  float *sred = reinterpret_cast<float *>(smem + L.red);  // [2 block parities][8 warps][32 lanes][4]
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
+  uint64_t *empty = full + kHtStages;
+  __shared__ unsigned long long s_key[kHtWarps + 1][8];
   __shared__ bool s_last;
   __shared__ float red[32];
-  const int xstride = D + 16;
+  __shared__ int aborted;
+  __shared__ int issued;
+  const int xstride = D + 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int KS = D / 64;  // stages a block (even: D % 128 == 0)
+  const int nblocks = (V + kHtRows - 1) / kHtRows;
+  const int my_blocks = (int)blockIdx.x < nblocks ? (nblocks - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = my_blocks * KS;  // stages this CTA consumes
+
+  if (threadIdx.x == 0) {
+    aborted = 0;
+    issued = 0;
+    for (int i = 0; i < kHtStages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kHtWarps / 2);  // the 8 warps of the stage's group
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool producer = warp == kHtWarps && lane == 0;
+  auto issue = [&](int q) {
+    const int slot = q % kHtStages, bi = q / KS, s = q - bi * KS;
+    const int row0 = ((int)blockIdx.x + bi * (int)gridDim.x) * kHtRows;
+    mbar_expect_tx(&full[slot], kHtStageBytes);
+    tma_load_2d(ring + (size_t)slot * kHtStageBytes, &tm_w, s * 64, row0, &full[slot]);
+  };
+  // the first stages: W depends on no earlier kernel
+  int q_next = 0;
+  if (producer) {
+    prefetch_tensormap(&tm_w);
+    for (; q_next < min(kHtStages, total); q_next++) issue(q_next);
+  }
+
+  pdl_wait();  // x / the residual come from the previous kernel; logits may still be read by it
   for (int r = 0; r < 8; r++) {
     if (r >= rows) {
       for (int i = threadIdx.x; i < D; i += blockDim.x) xh[r * xstride + i] = __float2half_rn(0.0f);
@@ -943,72 +1005,99 @@ __global__ void __launch_bounds__(kHmThreads, 1)
     }
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  const int ntiles = (V + 15) / 16;
-  const int nchunks = D / 32;
+
   float bv[2] = {-INFINITY, -INFINITY};
-  int bi[2] = {0x7fffffff, 0x7fffffff};
-  const __half *xg = xh + g * xstride + 8 * t;  // this lane's B rows: token g
-  for (int tile = blockIdx.x * kHmWarps + warp; tile < ntiles; tile += gridDim.x * kHmWarps) {
-    const int v0 = tile * 16;
-    const int ra = min(v0 + g, V - 1), rb = min(v0 + g + 8, V - 1);  // past V: read a valid row, drop it
-    const uint4 *wa = reinterpret_cast<const uint4 *>(W + (size_t)ra * D) + t;
-    const uint4 *wb = reinterpret_cast<const uint4 *>(W + (size_t)rb * D) + t;
-    float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int k0 = 0; k0 < nchunks; k0 += kHmChunks) {
-      uint4 ua[kHmChunks], ub[kHmChunks];
-#pragma unroll
-      for (int u = 0; u < kHmChunks; u++) {
-        if (k0 + u < nchunks) {
-          ua[u] = __ldcs(wa + (k0 + u) * 4);  // read once: stream past L2
-          ub[u] = __ldcs(wb + (k0 + u) * 4);
+  int bi_[2] = {0x7fffffff, 0x7fffffff};
+  if (warp == kHtWarps) {
+    // the rest of the stages, each once the group that read its slot is done
+    if (producer) {
+      for (; q_next < total; q_next++) {
+        const int slot = q_next % kHtStages;
+        if (aborted || !mbar_wait_bounded(&empty[slot], ((q_next / kHtStages) & 1) ^ 1, flags)) {
+          aborted = 1;
+          break;
         }
+        issue(q_next);
       }
-#pragma unroll
-      for (int u = 0; u < kHmChunks; u++) {
-        if (k0 + u >= nchunks) break;
-        const uint2 b0 = *reinterpret_cast<const uint2 *>(xg + (k0 + u) * 32);
-        const uint2 b1 = *reinterpret_cast<const uint2 *>(xg + (k0 + u) * 32 + 4);
-        mma_f16_16816(c, ua[u].x, ub[u].x, ua[u].y, ub[u].y, b0.x, b0.y);
-        mma_f16_16816(c, ua[u].z, ub[u].z, ua[u].w, ub[u].w, b1.x, b1.y);
-      }
+      issued = q_next;
     }
-    // c0, c1: row v0 + g, tokens 2t, 2t + 1; c2, c3: row v0 + g + 8
+  } else {
+    const int grp = warp >> 3, wr = warp & 7;
+    const int gq = lane >> 2, tq = lane & 3;
+    const int arow = 16 * wr + (lane & 15);  // this lane's ldmatrix row of the stage
+    const __half *xg = xh + gq * xstride + 2 * tq;
+    for (int bi = 0; bi < my_blocks; bi++) {
+      float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int s = grp; s < KS; s += 2) {
+        const int q = bi * KS + s, slot = q % kHtStages;
+        if (!aborted && !mbar_wait_bounded(&full[slot], (q / kHtStages) & 1, flags)) aborted = 1;
+        const uint8_t *st = ring + (size_t)slot * kHtStageBytes + arow * 128;
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int v = v0 + g + 8 * h;
-      if (v >= V) continue;
+        for (int kk = 0; kk < 4; kk++) {
+          const int chunk = 2 * kk + (lane >> 4);
+          uint32_t a[4];
+          ldsm_x4(a, st + ((chunk ^ (arow & 7)) << 4));
+          const int k0 = s * 64 + kk * 16;
+          const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xg + k0);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xg + k0 + 8);
+          mma_f16_16816(c, a[0], a[1], a[2], a[3], b0, b1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+      // the two groups' sums of this block meet; group 0 writes them
+      float *rb = sred + ((size_t)((bi & 1) * 8 + wr) * 32 + lane) * 4;
+      if (grp == 1) {
 #pragma unroll
-      for (int q = 0; q < 2; q++) {
-        const int tok = 2 * t + q;
-        if (tok >= rows) continue;
-        const float val = c[2 * h + q];
-        logits[(size_t)tok * V + v] = val;
-        if (val > bv[q]) {  // v grows along a lane's walk: ties keep the lower index
-          bv[q] = val;
-          bi[q] = v;
+        for (int e = 0; e < 4; e++) rb[e] = c[e];
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kHtWarps * 32) : "memory");
+      if (grp == 0) {
+        const int v0 = ((int)blockIdx.x + bi * (int)gridDim.x) * kHtRows + 16 * wr;
+        // c0, c1: row v0 + gq, tokens 2tq, 2tq + 1; c2, c3: row v0 + gq + 8
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int v = v0 + gq + 8 * h;
+          if (v >= V) continue;
+#pragma unroll
+          for (int q2 = 0; q2 < 2; q2++) {
+            const int tok = 2 * tq + q2;
+            if (tok >= rows) continue;
+            const float val = c[2 * h + q2] + rb[2 * h + q2];
+            logits[(size_t)tok * V + v] = val;
+            if (val > bv[q2]) {  // v grows along a lane's walk: ties keep the lower index
+              bv[q2] = val;
+              bi_[q2] = v;
+            }
+          }
         }
       }
     }
   }
+  // No copy may still be writing this CTA's shared memory when it exits
+  // (only possible after a timed-out wait): the producer waits for the last
+  // copy issued into each slot.
+  if (producer && aborted)
+    for (int q = issued > kHtStages ? issued - kHtStages : 0; q < issued; q++)
+      mbar_wait_bounded(&full[q % kHtStages], (q / kHtStages) & 1, flags);
+
   if (!amax && !keys) return;
-  // best per token: lanes with the same t (g = 0..7) hold tokens 2t, 2t + 1
-  unsigned long long k0 = argmax_key(bv[0], vocab_offset + bi[0]);
-  unsigned long long k1 = argmax_key(bv[1], vocab_offset + bi[1]);
+  // best per token: lanes with the same tq (gq = 0..7) hold tokens 2tq, 2tq + 1
+  unsigned long long k0 = argmax_key(bv[0], vocab_offset + bi_[0]);
+  unsigned long long k1 = argmax_key(bv[1], vocab_offset + bi_[1]);
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) {
     k0 = max(k0, __shfl_xor_sync(0xffffffffu, k0, o));
     k1 = max(k1, __shfl_xor_sync(0xffffffffu, k1, o));
   }
-  if (g == 0) {
-    s_key[warp][2 * t] = k0;
-    s_key[warp][2 * t + 1] = k1;
+  if ((lane >> 2) == 0) {
+    s_key[warp][2 * (lane & 3)] = k0;
+    s_key[warp][2 * (lane & 3) + 1] = k1;
   }
   __syncthreads();
   if (threadIdx.x < rows) {
     unsigned long long k = 0;
-    for (int w = 0; w < kHmWarps; w++) k = max(k, s_key[w][threadIdx.x]);
+    for (int w = 0; w <= kHtWarps; w++) k = max(k, s_key[w][threadIdx.x]);
     part[(size_t)blockIdx.x * rows + threadIdx.x] = k;
     __threadfence();
   }
@@ -1026,7 +1115,7 @@ __global__ void __launch_bounds__(kHmThreads, 1)
     __syncthreads();
     if (threadIdx.x == 0) {
       unsigned long long kk = 0;
-      for (int w = 0; w < kHmWarps; w++) kk = max(kk, s_key[w][0]);
+      for (int w = 0; w <= kHtWarps; w++) kk = max(kk, s_key[w][0]);
       if (amax) amax[r] = (int32_t)(0xffffffffu - (unsigned)(kk & 0xffffffffu));
       if (keys) keys[r] = kk ^ 0x8000000000000000ull;  // signed-orderable: an int64 MAX picks it
     }
@@ -1320,23 +1409,29 @@ cudaError_t launch_conv_restore(const void *prefixes, int slots, int batch, int 
 cudaError_t launch_head(const void *x, const float *na, const float *nb, const float *nw, float eps, int rows,
                         int row_stride, int D, const void *W, int V, int vocab_offset, float *logits, int32_t *amax,
                         unsigned long long *keys, unsigned long long *part, size_t part_bytes, unsigned *count,
-                        int num_sms, cudaStream_t s, bool pdl) {
+                        unsigned *flags, int num_sms, cudaStream_t s, bool pdl) {
   if (rows > kHeadMaxRows || D % 8) return cudaErrorInvalidValue;
   const bool norm = na != nullptr;
   const HeadNorm hn{na, nb, nw, eps};
-  const size_t smem_mma = (size_t)8 * (D + 16) * sizeof(__half);
-  if (D % 32 == 0 && smem_mma <= 200 * 1024) {
-    auto kern = norm ? head_mma_kernel<true> : head_mma_kernel<false>;
-    if (smem_mma > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mma);
-      if (e != cudaSuccess) return e;
-    }
+  const size_t smem_tma = HeadSmem(D).total + 1024;  // + slack for the 1024-byte alignment
+  if (D % 128 == 0 && smem_tma <= 227 * 1024 && encode_fn() && (reinterpret_cast<uintptr_t>(W) & 15) == 0) {
+    CUtensorMap tm;
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)V};
+    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)kHtRows};
+    cuuint32_t elem[2] = {1, 1};
+    if (encode_fn()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(W), dims, strides, box, elem,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    auto kern = norm ? head_tma_kernel<true> : head_tma_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_tma);
+    if (e != cudaSuccess) return e;
     int grid = num_sms;
     const int max_grid = (int)(part_bytes / (sizeof(unsigned long long) * (rows ? rows : 1)));
     if (grid > max_grid) grid = max_grid;
-    return launch_k(kern, dim3(grid), dim3(kHmThreads), smem_mma, s, pdl, reinterpret_cast<const __half *>(x), hn,
-                    rows, row_stride, D, reinterpret_cast<const __half *>(W), V, vocab_offset, logits, amax, keys,
-                    part, count);
+    return launch_k(kern, dim3(grid), dim3(kHtThreads), smem_tma, s, pdl, tm, reinterpret_cast<const __half *>(x),
+                    hn, rows, row_stride, D, V, vocab_offset, logits, amax, keys, part, count, flags);
   }
   const size_t smem = (size_t)rows * D * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;

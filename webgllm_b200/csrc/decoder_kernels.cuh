@@ -48,7 +48,7 @@ cudaError_t launch_conv_restore(const void *prefixes, int slots, int batch, int 
 cudaError_t launch_head(const void *x, const float *na, const float *nb, const float *nw, float eps, int rows,
                         int row_stride, int D, const void *W, int V, int vocab_offset, float *logits, int32_t *amax,
                         unsigned long long *keys, unsigned long long *part, size_t part_bytes, unsigned *count,
-                        int num_sms, cudaStream_t s, bool pdl);
+                        unsigned *flags, int num_sms, cudaStream_t s, bool pdl);
 cudaError_t launch_pick_keys(const unsigned long long *keys, int rows, int32_t *ids, cudaStream_t s, bool pdl);
 cudaError_t launch_argmax(const float *logits, int rows, int V, int32_t *out, cudaStream_t s, bool pdl);
 cudaError_t launch_add_i32(int32_t *p, int n, int delta, cudaStream_t s, bool pdl);
