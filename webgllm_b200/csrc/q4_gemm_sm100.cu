@@ -373,16 +373,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int E4 = BM * kBN / 4;  // float4 entries: 4 consecutive weight rows of a token
     const int e0 = (int)((long long)E4 * crank / C), e1 = (int)((long long)E4 * (crank + 1) / C);
     uint32_t peer[kMaxSplits];
-    for (int r = 0; r < C; r++) peer[r] = map_rank(smem_u32(smem + L.x), (uint32_t)r);
+#pragma unroll
+    for (int r = 0; r < kMaxSplits; r++) peer[r] = r < C ? map_rank(smem_u32(smem + L.x), (uint32_t)r) : 0u;
     for (int e = e0 + (int)threadIdx.x; e < e1; e += kGemmThreads) {
+      // every rank's partial in flight at once, then summed in rank order
+      // (interleaving each load with its add serialised C round trips of
+      // distributed shared memory)
+      float4 v[kMaxSplits];
+#pragma unroll
+      for (int r = 0; r < kMaxSplits; r++)
+        if (r < C) v[r] = ld_cluster_f32x4(peer[r] + (uint32_t)e * 16u);
       float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      for (int r = 0; r < C; r++) {
-        const float4 v = ld_cluster_f32x4(peer[r] + (uint32_t)e * 16u);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
+#pragma unroll
+      for (int r = 0; r < kMaxSplits; r++)
+        if (r < C) {
+          acc.x += v[r].x;
+          acc.y += v[r].y;
+          acc.z += v[r].z;
+          acc.w += v[r].w;
+        }
       const int tok = m0 + (4 * e) / kBN, nn = nt0 * kTileRows + (4 * e) % kBN;
       if (tok < a.M && nn < a.N) {  // N % 4 == 0: all four rows or none
         const size_t o = (size_t)tok * a.N + nn;
