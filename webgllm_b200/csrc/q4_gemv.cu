@@ -1047,6 +1047,22 @@ bool plan_gemv(GemvArgs &a, int num_sms) {
   return true;
 }
 
+// Clusters of several CTAs: four fewer than the occupancy query allows, then
+// the fewest that give each cluster the same number of columns. The query's
+// count of co-resident clusters is more than the hardware places behind a
+// previous kernel's tail (wg_trace of the config-4 decode step, clusters of
+// 3 after the gate|up GEMV on all 148 SMs: of 45 planned, 43 placed and the
+// last two ran as a second wave, the down projection 29 us a layer; of 43,
+// one or two late in most layers, 26 us; of 37 (this reserve) none late,
+// 19.8 us; the step 2.91 -> 2.67 ms). Single CTAs keep one an SM (each SM's
+// share of HBM bounds a CTA with more columns).
+static int wide_balance(int NT, int G, int C) {
+  if (C == 1) return G;
+  if (G > 8) G -= 4;
+  const int J = (NT + G - 1) / G;
+  return (NT + J - 1) / J;
+}
+
 bool plan_gemv_wide(GemvArgs &a, int num_sms) {
   if (a.M < 1 || a.M > kWideMaxTokens || (a.pro.kind != kProNone && a.M > kProMaxTokens)) return false;
   const bool zeros = a.zro != nullptr;
@@ -1090,6 +1106,8 @@ bool plan_gemv_wide(GemvArgs &a, int num_sms) {
   const int fit = wide_max_clusters(C, wide_smem(a.M, ktc, S, Jc, C, zeros).total, num_sms);
   if (G > fit) G = fit;
   int J = (a.NT + G - 1) / G;
+  G = wide_balance(a.NT, G, C);
+  J = (a.NT + G - 1) / G;
   if (Jc > J) Jc = J;
   // With a K split the group walk keeps every column's partial sums in
   // `part` and reduces them across the cluster once, after the walk: only
@@ -1105,7 +1123,7 @@ bool plan_gemv_wide(GemvArgs &a, int num_sms) {
     while (S2 > 2 && wide_smem(a.M, ktc, S2, Jest, C, zeros).total > budget) S2 -= 2;
     const int smem2 = wide_smem(a.M, ktc, S2, Jest, C, zeros).total;
     if (smem2 <= budget) {
-      const int G2 = min(Gmax, wide_max_clusters(C, smem2, num_sms));
+      const int G2 = wide_balance(a.NT, min(Gmax, wide_max_clusters(C, smem2, num_sms)), C);
       const int J2 = (a.NT + G2 - 1) / G2;
       if (J2 <= Jest) {
         S = S2;
