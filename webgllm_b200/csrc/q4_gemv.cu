@@ -665,18 +665,16 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
   auto issue = [&](int j) { issue_to(j, j % S); };
 
   // 1. Weight copies of the first column: they depend on nothing the
-  //    previous kernel writes. With fp16 x (one bulk copy a row) the other
-  //    first S columns follow x's copies (below): copies issued ahead of x's
-  //    would delay it by their bytes at this SM's share of HBM (measured on
-  //    B200, M = 8 chains: 6144x4096 7.14 -> 6.46 us, 28672x4096 19.8 ->
-  //    18.2 us, 4096x14336 15.8 -> 14.5 us with x first).
+  //    previous kernel writes. The other first S columns follow x: copies
+  //    issued ahead of x's would delay it by their bytes at this SM's share
+  //    of HBM (measured on B200, M = 8 chains with fp16 x: 6144x4096 7.14 ->
+  //    6.46 us, 28672x4096 19.8 -> 18.2 us, 4096x14336 15.8 -> 14.5 us; the
+  //    norm prologue's x in the config-4 decode step, wg_trace: gate|up
+  //    6.7 -> 5.4 us a CTA, the step 1.2 % shorter).
   if (threadIdx.x == 0) {
     for (int st = 0; st <= S; st++) mbar_init(&bars[st], 1);  // stages and x
     fence_mbar_init();
-    // (x made by a prologue is loads and arithmetic, not a copy: all S
-    // columns go first then; measured on the config-4 decode step, issuing
-    // them after its x staging was 1 % slower)
-    for (int j = 0; j < (x_bulk ? min(1, J) : min(S, J)); j++) issue(j);
+    if (J > 0) issue(0);
   }
   __syncthreads();
   if (a.trace && threadIdx.x == 0) ts[1] = globaltimer();
@@ -739,6 +737,10 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
       }
     }
   }
+  // x made by a prologue (loads, not a copy): the rest of the first S
+  // columns once its loads are done
+  if (!x_bulk && threadIdx.x == 0)
+    for (int j = 1; j < min(S, J); j++) issue(j);
   __syncthreads();
   if (a.trigger_at <= 1) pdl_trigger();
   if (a.trace && threadIdx.x == 0) ts[3] = globaltimer();

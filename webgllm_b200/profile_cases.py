@@ -161,6 +161,59 @@ def decode(config: str, batch: int, reps: int):
     print(f"decode config {config} batch {batch}: {us:.1f} us/step (eager)")
 
 
+def trace_decode(config: str, batch: int, reps: int):
+    """Per-CTA timeline of one decode step (CUDA graph) from wg_trace: for
+    each of a layer's four GEMVs (q|k|v, o, gate|up, down) the mean span from
+    the dependency release to the last CTA's exit and its phases per CTA
+    (release -> x staged, the multiplies, the tail), the gap before it (for
+    o: the attention launch), and the CTAs released more than 5 us after the
+    first (a second wave: CTAs that found no room until others finished)."""
+    import numpy as np
+
+    cfg = CONFIGS[config]
+    m = DecoderModel(cfg, seed=0, max_ctx=1024, max_rows=batch * 512, batch=batch)
+    m.prefill(torch.randint(0, cfg.vocab, (batch, 512), device="cuda", dtype=torch.int32))
+    m.decode_step()
+    torch.cuda.synchronize()
+    c, L = m.ctx, _lib.lib()
+    buf = torch.zeros(8 * 256 * 4 * cfg.layers * 2, dtype=torch.int64, device="cuda")
+    _lib.check(L.wg_trace(P(c.handle), P(buf.data_ptr()), buf.numel() * 8), c.handle)
+    m.capture_decode()
+    for _ in range(3):
+        m.graph.replay()
+    us = _time(m.graph.replay, reps)
+    _lib.check(L.wg_trace(P(c.handle), P(buf.data_ptr()), buf.numel() * 8), c.handle)  # restart the records
+    m.graph.replay()
+    torch.cuda.synchronize()
+    n = ctypes.c_size_t()
+    _lib.check(L.wg_trace_count(P(c.handle), ctypes.byref(n)), c.handle)
+    _lib.check(L.wg_trace(P(c.handle), None, 0), c.handle)
+    rec = buf[: n.value * 8].view(-1, 8).cpu().numpy().astype(np.float64)
+    launch = rec[:, 7].astype(np.int64) >> 32
+    ids = sorted(set(launch.tolist()))
+    names = ["q|k|v", "o", "gate|up", "down"]
+    acc = {k: {f: [] for f in ("span", "x", "mul", "tail", "gap", "late", "ctas")} for k in names}
+    prev_exit = None
+    for i, li in enumerate(ids):
+        r = rec[launch == li] / 1e3  # us
+        a = acc[names[i % 4]]
+        a["span"].append(r[:, 5].max() - r[:, 2].min())
+        a["x"].append(np.median(r[:, 3] - r[:, 2]))
+        a["mul"].append(np.median(r[:, 4] - r[:, 3]))
+        a["tail"].append(np.median(r[:, 5] - r[:, 4]))
+        a["late"].append(int((r[:, 2] > r[:, 2].min() + 5).sum()))
+        a["ctas"].append(len(r))
+        if prev_exit is not None:
+            a["gap"].append(r[:, 2].min() - prev_exit)
+        prev_exit = r[:, 5].max()
+    print(f"decode config {config} batch {batch}: {us:.1f} us/step (CUDA graph), {len(ids)} traced GEMV launches")
+    for k in names:
+        a = acc[k]
+        print(f"  {k:8s} ctas {np.mean(a['ctas']):5.0f}  release->exit {np.mean(a['span']):6.2f} us  per CTA: x "
+              f"{np.mean(a['x']):5.2f}, multiplies {np.mean(a['mul']):5.2f}, tail {np.mean(a['tail']):4.2f}  "
+              f"gap before {np.mean(a['gap']) if a['gap'] else float('nan'):5.2f}  late CTAs {sum(a['late'])}")
+
+
 def exchange(reps: int):
     """Cost of one push all-reduce of config 4's decode (batch 8) at the
     tensor-parallel degree of the launch (`python -m torch.distributed.run
@@ -252,6 +305,7 @@ CASES = {
     "decode_config4_b8": lambda r: decode("4", 8, r),
     "decode_config2": lambda r: decode("2", 1, r),
     "exchange_config4_b8": lambda r: exchange(r),
+    "trace_decode_config4_b8": lambda r: trace_decode("4", 8, r),
 }
 
 
