@@ -281,7 +281,8 @@ def test_gemm_repeated_calls_are_deterministic():
 def test_gemm_pair_kernel_parity():
     """The 2-SM (cta_group::2) GEMM, opt-in through WG_GEMM_PAIR=1 (read once
     per process, hence a child process): the same products as the fp32
-    product of the dequantised weights, rel 1e-3."""
+    product of the dequantised weights within the suite's two measures (rel
+    L2 and max |error| / max |ref| <= 1e-3)."""
     import subprocess
     import sys
 
@@ -291,7 +292,7 @@ sys.path.insert(0, ".")
 import webgllm_b200 as wg
 from webgllm_b200.model import quantize_q4_0, dequantize_q4_0
 c = wg.context(); c.use_torch_stream()
-worst = 0.0
+worst = worst_max = 0.0
 for (M, N, K) in [(256, 256, 256), (300, 512, 1024), (1024, 4096, 4096), (77, 768, 2048)]:
     g = torch.Generator(device="cuda"); g.manual_seed(M + N + K)
     w = torch.randn((N, K), generator=g, device="cuda") * 0.02
@@ -302,7 +303,8 @@ for (M, N, K) in [(256, 256, 256), (300, 512, 1024), (1024, 4096, 4096), (77, 76
     c.sync()
     ref = x.float() @ dequantize_q4_0(bl, N, K).t()
     worst = max(worst, ((y - ref).norm() / ref.norm()).item())
-print(worst)
+    worst_max = max(worst_max, ((y - ref).abs().max() / ref.abs().max()).item())
+print(worst, worst_max)
 '''
     import os
 
@@ -310,4 +312,5 @@ print(worst)
     env = dict(os.environ, WG_GEMM_PAIR="1")
     out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stderr[-2000:]
-    assert float(out.stdout.strip().splitlines()[-1]) < 1e-3
+    l2, mx = map(float, out.stdout.strip().splitlines()[-1].split())
+    assert l2 <= TOL and mx <= TOL, f"pair kernel: l2 {l2:.3e} max {mx:.3e}"
