@@ -85,8 +85,8 @@ int wg_comm_reduce_norm(wg_ctx *ctx, wg_comm *comm, int M, int K, const float *r
  * PyTorch (the reference's TypeScript host through a Node-API addon) can
  * join a group, all-reduce and set up the push exchange. The reference runs
  * one worker per model (src/client.ts:64); here one process per GPU joins a
- * group of `nranks` (the SURVEY's wg_tp_init(ctx, nranks, rank,
- * ncclUniqueId) row). NCCL is loaded on first use (dlopen of libnccl.so.2,
+ * group of `nranks` with wg_tp_init(ctx, nranks, rank, id), the 128-byte
+ * NCCL unique id made by one rank. NCCL is loaded on first use (dlopen of libnccl.so.2,
  * or the path in WG_NCCL_LIBRARY): a process that already loaded it shares
  * that copy, and the library still loads where NCCL is absent (these calls
  * then return WG_UNSUPPORTED).
