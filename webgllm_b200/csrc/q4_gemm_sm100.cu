@@ -55,6 +55,10 @@ constexpr int kMaxSplits = 8;  // K splits of a tile: one portable thread-block 
 // (BM = 256, one CTA an SM, measured the same or 1-3 % slower with 6 smem
 // stages and an 8-stage A ring: the waits are not latency.)
 __host__ __device__ constexpr int smem_stages(int BM) { return BM <= 64 ? 8 : 4; }
+// K tiles (of 64) a pipeline stage carries: two at BM = 256, so that each
+// round of barrier waits (x landed, A dequantised) feeds eight N = 256 MMAs
+// instead of four; the rings keep their bytes (half as many stages).
+__host__ __device__ constexpr int stage_ktiles(int BM) { return BM == 256 ? 2 : 1; }
 constexpr int kBN = 128;          // weight rows per CTA = MMA M
 constexpr int kDequantWarps = 8;  // warps 2..9
 constexpr int kGemmThreads = (2 + kDequantWarps) * 32;
@@ -78,7 +82,7 @@ struct GemmSmem {
 
 __host__ __device__ inline GemmSmem gemm_smem(int BM) {
   GemmSmem s;
-  const int S = smem_stages(BM);
+  const int S = smem_stages(BM);  // K tiles of ring (stage_ktiles(BM) a stage)
   s.x = 0;  // 1024-aligned (SW128 atoms)
   s.nib = s.x + S * kXStageBytes(BM);
   s.scl = s.nib + S * kNibStageBytes;
@@ -192,8 +196,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const GemmSmem L = gemm_smem(BM);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // weights and x of a stage complete separately: the dequantisers start on
-  // prefetched weights while x is still waiting for its producer
-  constexpr int S = smem_stages(BM), T = kStages;
+  // prefetched weights while x is still waiting for its producer. A stage
+  // carries P K tiles (S stages, T tensor-memory A stages: the rings keep
+  // their bytes).
+  constexpr int P = stage_ktiles(BM);
+  constexpr int S = smem_stages(BM) / P, T = kStages / P;
+  constexpr int XS = P * kXStageBytes(BM), NS = P * kNibStageBytes, SS = P * kSclStageBytes, ZS = P * kZroStageBytes;
   uint64_t *wfull = reinterpret_cast<uint64_t *>(smem + L.bar);
   uint64_t *xfull = wfull + S;
   uint64_t *sempty = xfull + S;  // shared-memory stage free (the MMA that read it is done)
@@ -210,7 +218,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int kpc = a.kt_per_split;  // K tiles per split
   const int kt_begin = blockIdx.z * kpc;
   const int kt_end = min(a.KT, kt_begin + kpc);
-  const int nk = kt_end - kt_begin;  // >= 1
+  // stages of this split (P tiles each; kt_per_split is a multiple of P, so
+  // a stage's tiles past kt_end are past K: the copies read zeros there)
+  const int nk = (kt_end - kt_begin + P - 1) / P;
 
   if (threadIdx.x == 0) {
     aborted = 0;
@@ -241,19 +251,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t wbytes = kNibStageBytes + kSclStageBytes + (ZEROS ? kZroStageBytes : 0);
-      const uint32_t xbytes = kXStageBytes(BM);
+      const uint32_t wbytes = NS + SS + (ZEROS ? ZS : 0);
+      const uint32_t xbytes = XS;
       auto load_w = [&](int it) {
-        const int s = it % S, kt = kt_begin + it;
+        const int s = it % S;
         mbar_expect_tx(&wfull[s], wbytes);
-        tma_load_3d(smem + L.nib + s * kNibStageBytes, &tm_nib, 0, kt, nt0, &wfull[s]);
-        tma_load_3d(smem + L.scl + s * kSclStageBytes, &tm_scl, 0, kt, nt0, &wfull[s]);
-        if (ZEROS) tma_load_3d(smem + L.zro + s * kZroStageBytes, &tm_zro, 0, kt, nt0, &wfull[s]);
+#pragma unroll
+        for (int p = 0; p < P; p++) {
+          const int kt = kt_begin + it * P + p;
+          tma_load_3d(smem + L.nib + s * NS + p * kNibStageBytes, &tm_nib, 0, kt, nt0, &wfull[s]);
+          tma_load_3d(smem + L.scl + s * SS + p * kSclStageBytes, &tm_scl, 0, kt, nt0, &wfull[s]);
+          if (ZEROS) tma_load_3d(smem + L.zro + s * ZS + p * kZroStageBytes, &tm_zro, 0, kt, nt0, &wfull[s]);
+        }
       };
       auto load_x = [&](int it) {
         const int s = it % S;
         mbar_expect_tx(&xfull[s], xbytes);
-        tma_load_2d(smem + L.x + s * kXStageBytes(BM), &tm_x, (kt_begin + it) * kTileK, m0, &xfull[s]);
+#pragma unroll
+        for (int p = 0; p < P; p++)
+          tma_load_2d(smem + L.x + s * XS + p * kXStageBytes(BM), &tm_x, (kt_begin + it * P + p) * kTileK, m0,
+                      &xfull[s]);
       };
       // The first stages' weights depend on no earlier kernel: copied (and
       // dequantised) before the dependency wait; x, the previous kernel's
@@ -279,10 +296,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (a.trace && it == 0) ts[3] = globaltimer();
         wait(&afull[t], (it / T) & 1);
         tc_fence_after();
-        const uint64_t bdesc = sw128_desc(smem_u32(smem + L.x + s * kXStageBytes(BM)));
 #pragma unroll
-        for (int kk = 0; kk < 4; kk++)
-          mma_f16_tmem_a(tmem_d, tmem_a + t * 32 + kk * 8, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+        for (int p = 0; p < P; p++) {
+          const uint64_t bdesc = sw128_desc(smem_u32(smem + L.x + s * XS + p * kXStageBytes(BM)));
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_f16_tmem_a(tmem_d, tmem_a + (t * P + p) * 32 + kk * 8, bdesc + 2 * kk, idesc,
+                           (it > 0 || p > 0 || kk > 0) ? 1u : 0u);
+        }
         tc_commit(&sempty[s]);  // x and codes of stage s read (the dequantisers finished before afull)
         tc_commit(&tempty[t]);
       }
@@ -300,32 +321,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       wait(&wfull[s], (it / S) & 1);
       wait(&tempty[t], ((it / T) & 1) ^ 1);  // the MMA that last read A stage t is done
       tc_fence_after();
-      const uint4 wv = *reinterpret_cast<const uint4 *>(smem + L.nib + s * kNibStageBytes + tile * kTileNibBytes +
-                                                        lane * 16);
-      const uint2 sv =
-          *reinterpret_cast<const uint2 *>(smem + L.scl + s * kSclStageBytes + tile * kTileSclBytes + g * 8);
-      uint32_t zv = 0x08080808u;
-      if (ZEROS)
-        zv = *reinterpret_cast<const uint32_t *>(smem + L.zro + s * kZroStageBytes + tile * kTileZroBytes + g * 4);
-      const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
-      uint32_t v[16];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int bsel = j >> 1;
-        const uint32_t zz = zv >> (16 * bsel);
-        const uint32_t z_g = zz & 15u, z_g8 = (zz >> 8) & 15u;
-        uint32_t P[4];
-        unpack_codes(w[j], zp_lo(z_g), zp_hi(z_g), zp_lo(z_g8), zp_hi(z_g8), P);
-        const uint32_t sp = bsel ? sv.y : sv.x;  // (d_g, d_g8)
-        const uint32_t d_g = (sp & 0xFFFFu) * 0x00010001u;
-        const uint32_t d_g8 = (sp >> 16) * 0x00010001u;
-        // (q - z) * d rounded to fp16, as the reference's dequant pass.
-        v[4 * j + 0] = hmul2_u(P[0], d_g);
-        v[4 * j + 1] = hmul2_u(P[1], d_g);
-        v[4 * j + 2] = hmul2_u(P[2], d_g8);
-        v[4 * j + 3] = hmul2_u(P[3], d_g8);
+      for (int p = 0; p < P; p++) {
+        const uint4 wv = *reinterpret_cast<const uint4 *>(smem + L.nib + s * NS + p * kNibStageBytes +
+                                                          tile * kTileNibBytes + lane * 16);
+        const uint2 sv = *reinterpret_cast<const uint2 *>(smem + L.scl + s * SS + p * kSclStageBytes +
+                                                          tile * kTileSclBytes + g * 8);
+        uint32_t zv = 0x08080808u;
+        if (ZEROS)
+          zv = *reinterpret_cast<const uint32_t *>(smem + L.zro + s * ZS + p * kZroStageBytes +
+                                                   tile * kTileZroBytes + g * 4);
+        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t v[16];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int bsel = j >> 1;
+          const uint32_t zz = zv >> (16 * bsel);
+          const uint32_t z_g = zz & 15u, z_g8 = (zz >> 8) & 15u;
+          uint32_t pc[4];
+          unpack_codes(w[j], zp_lo(z_g), zp_hi(z_g), zp_lo(z_g8), zp_hi(z_g8), pc);
+          const uint32_t sp = bsel ? sv.y : sv.x;  // (d_g, d_g8)
+          const uint32_t d_g = (sp & 0xFFFFu) * 0x00010001u;
+          const uint32_t d_g8 = (sp >> 16) * 0x00010001u;
+          // (q - z) * d rounded to fp16, as the reference's dequant pass.
+          v[4 * j + 0] = hmul2_u(pc[0], d_g);
+          v[4 * j + 1] = hmul2_u(pc[1], d_g);
+          v[4 * j + 2] = hmul2_u(pc[2], d_g8);
+          v[4 * j + 3] = hmul2_u(pc[3], d_g8);
+        }
+        tmem_st_16x256b_x4(tmem_a + ((uint32_t)(32 * q + 16 * sub) << 16) + (t * P + p) * 32, v);
       }
-      tmem_st_16x256b_x4(tmem_a + ((uint32_t)(32 * q + 16 * sub) << 16) + t * 32, v);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -889,6 +914,10 @@ size_t plan_gemm(GemmArgs &a, int num_sms) {
   if (force > 0 && !pair) splits = force < kMaxSplits ? force : kMaxSplits;
   if (splits > a.KT) splits = a.KT;
   a.kt_per_split = (a.KT + splits - 1) / splits;
+  // whole stages per split: a stage's tiles past its split would be the
+  // next split's
+  const int P = pair ? 1 : stage_ktiles(BM);
+  a.kt_per_split = (a.kt_per_split + P - 1) / P * P;
   a.splits = (a.KT + a.kt_per_split - 1) / a.kt_per_split;
   return 0;
 }
