@@ -83,6 +83,16 @@ int wg_rope_kv(wg_ctx *ctx, const float *qkv, int rows, int batch, int H, int Hk
                 "wg_rope_kv");
 }
 
+// The context's wg_trace buffer for one launch (a launch index of its own).
+static wg::TraceSink trace_sink(wg_ctx *ctx) {
+  wg::TraceSink t;
+  t.buf = ctx->trace;
+  t.next = ctx->d_trace_next;
+  t.cap = ctx->trace_cap;
+  t.launch_index = ctx->launch_index++;
+  return t;
+}
+
 int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                  const void *v_cache, int cache_len, const int32_t *pos, void *out) {
   WG_BEGIN(ctx);
@@ -95,7 +105,7 @@ int wg_attention(wg_ctx *ctx, const void *q, int rows, int batch, int H, int Hkv
   if (!q || !k_cache || !v_cache || !pos || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_attention: null");
   return finish(ctx,
                 wg::launch_attention(q, rows, batch, H, Hkv, Dh, k_cache, v_cache, cache_len, pos, out, ctx->num_sms,
-                                     ctx->stream, ctx->pdl),
+                                     ctx->stream, ctx->pdl, trace_sink(ctx)),
                 "wg_attention");
 }
 
@@ -110,7 +120,8 @@ int wg_rope_attention(wg_ctx *ctx, const float *qkv, int batch, int H, int Hkv, 
   if (!qkv || !pos || !k_cache || !v_cache || !out) return dfail(ctx, WG_INVALID_ARGUMENT, "wg_rope_attention: null");
   return finish(ctx,
                 wg::launch_rope_attention(qkv, batch, H, Hkv, Dh, pos, theta, q_norm, k_norm, eps, k_cache, v_cache,
-                                          cache_len, out, ctx->d_flags, ctx->num_sms, ctx->stream, ctx->pdl),
+                                          cache_len, out, ctx->d_flags, ctx->num_sms, ctx->stream, ctx->pdl,
+                                          trace_sink(ctx)),
                 "wg_rope_attention");
 }
 

@@ -236,6 +236,10 @@ struct RopeArgs {
   const float *q_norm, *k_norm;  // or null
   float eps;
   unsigned *flags;
+  // wg_trace (any attention launch): a record per CTA of entry, cache
+  // prefetch issued, dependency release, queries made, the last tile's P.V
+  // done, exit (the cluster leader after the merge)
+  TraceSink tr;
 };
 
 // q / k rows of qkv for one head, as rope_kv_kernel computes them: optional
@@ -325,6 +329,9 @@ __global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const __half *q, int rps, int H, int Hkv, __half *k_cache, __half *v_cache, int cache_len,
                      const int *pos0, __half *out, const RopeArgs ra) {
   pdl_trigger();  // dependents may launch now; they wait for this grid to finish
+  __shared__ unsigned long long tstamp[6];
+  const bool tracing = ra.tr.buf != nullptr;
+  if (tracing && threadIdx.x == 0) tstamp[0] = globaltimer();
   // While the previous kernel finishes: an L2 prefetch of this CTA's slice
   // of the caches (rows written by earlier steps; a prefetch is only a hint
   // and L2 is where writes land, so a position read early or a row still
@@ -341,7 +348,9 @@ __global__ void __launch_bounds__(kAttnThreads)
       prefetch_l2(v_cache + row0 * Dh, (uint32_t)(a1 - a0) * Dh * 2);
     }
   }
+  if (tracing && threadIdx.x == 0) tstamp[1] = globaltimer();
   pdl_wait();     // inputs come from the previous kernel
+  if (tracing && threadIdx.x == 0) tstamp[2] = globaltimer();
   constexpr int Dh = 32 * DPL;
   constexpr int kHalfDpl = DPL / 2 > 0 ? DPL / 2 : 1;  // rotate-half pairs per lane (ROPE: DPL >= 2)
   constexpr int kAttnTile = attn_tile(Dh);
@@ -428,6 +437,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     sl[g] = 0.0f;
   }
   for (int i = tid; i < G * Dh; i += kAttnThreads) sacc[i] = 0.0f;
+  if (tracing && tid == 0) tstamp[3] = globaltimer();
 
   const int gq = lane >> 2, tq = lane & 3;  // MMA fragment row group / column pair
   uint32_t qa[Dh / 16][4];  // A fragments of the queries (heads x dims), made at the first tile
@@ -558,6 +568,7 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
     }
   }
+  if (tracing && tid == 0) tstamp[4] = globaltimer();
   // this warp's dims of O into sacc for the merge
 #pragma unroll
   for (int b = 0; b < DPL; b++)
@@ -583,7 +594,14 @@ __global__ void __launch_bounds__(kAttnThreads)
       reinterpret_cast<float4 *>(ga)[i] = reinterpret_cast<const float4 *>(sacc)[i];
   }
   cluster.sync();
-  if (c != 0) return;  // nothing reads this CTA's shared memory any more
+  const unsigned cta_id = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  if (c != 0) {  // nothing reads this CTA's shared memory any more
+    if (tracing && tid == 0) {
+      tstamp[5] = globaltimer();
+      trace_record(ra.tr.buf, ra.tr.next, ra.tr.cap, tstamp, ra.tr.launch_index, cta_id);
+    }
+    return;
+  }
   // weights of each slice per head: w[j][g] = exp(m_j - M) / sum_j' l_j' exp(m_j' - M)
   // (slices without keys carry none; the weights go to the probability tile,
   // or to q's slots when the gather overlays the tiles; corr holds the
@@ -609,6 +627,10 @@ __global__ void __launch_bounds__(kAttnThreads)
     float a = 0.0f;
     for (int j = 0; j < nslices; j++) a += gacc[(size_t)j * G * Dh + i] * wts[j * G + g];
     out[((size_t)r * H + qh0) * Dh + i] = __float2half_rn(a * scorr[g]);
+  }
+  if (tracing && tid == 0) {
+    tstamp[5] = globaltimer();
+    trace_record(ra.tr.buf, ra.tr.next, ra.tr.cap, tstamp, ra.tr.launch_index, cta_id);
   }
 }
 
@@ -1310,13 +1332,14 @@ cudaError_t launch_attention_t(const void *q, int rows, int rps, int H, int Hkv,
 
 cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                              const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
-                             cudaStream_t s, bool pdl) {
+                             cudaStream_t s, bool pdl, const TraceSink &tr) {
   if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
   const int rps = rows / batch;
   static const bool no_flash = getenv("WG_NO_FLASH_PREFILL") != nullptr;  // the CUDA-core kernel (comparison)
   if (flash_prefill_supported(rps, Dh) && !no_flash)
     return launch_flash_prefill(q, rps, batch, H, Hkv, Dh, k_cache, v_cache, cache_len, pos0, out, s, pdl);
-  const RopeArgs ra{};
+  RopeArgs ra{};
+  ra.tr = tr;
   switch (Dh) {
     case 32:
       return launch_attention_t<1, false>(q, rows, rps, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms, s,
@@ -1336,9 +1359,10 @@ cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv,
 
 cudaError_t launch_rope_attention(const float *qkv, int batch, int H, int Hkv, int Dh, const int *pos0, float theta,
                                   const float *q_norm, const float *k_norm, float eps, void *k_cache, void *v_cache,
-                                  int cache_len, void *out, unsigned *flags, int num_sms, cudaStream_t s, bool pdl) {
+                                  int cache_len, void *out, unsigned *flags, int num_sms, cudaStream_t s, bool pdl,
+                                  const TraceSink &tr) {
   if (H % Hkv || H / Hkv > kAttnMaxGroup) return cudaErrorInvalidValue;
-  const RopeArgs ra{qkv, theta, q_norm, k_norm, eps, flags};
+  const RopeArgs ra{qkv, theta, q_norm, k_norm, eps, flags, tr};
   switch (Dh) {
     case 64:
       return launch_attention_t<2, true>(nullptr, batch, 1, H, Hkv, k_cache, v_cache, cache_len, pos0, out, num_sms,

@@ -9,6 +9,15 @@
 
 namespace wg {
 
+// Where a traced launch appends its per-CTA records (wg_trace); buf null:
+// no tracing.
+struct TraceSink {
+  unsigned long long *buf = nullptr;
+  unsigned long long *next = nullptr;
+  unsigned long long cap = 0;
+  unsigned launch_index = 0;
+};
+
 cudaError_t launch_embed(const int32_t *ids, int rows, const void *table, int V, int D, float *out, cudaStream_t s,
                          bool pdl);
 cudaError_t launch_rmsnorm(float *x, const float *add, const float *w, float eps, int rows, int D, void *out,
@@ -20,7 +29,7 @@ cudaError_t launch_rope_kv(const float *qkv, int rows, int batch, int H, int Hkv
                            void *k_cache, void *v_cache, int cache_len, unsigned *flags, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const void *q, int rows, int batch, int H, int Hkv, int Dh, const void *k_cache,
                              const void *v_cache, int cache_len, const int *pos0, void *out, int num_sms,
-                             cudaStream_t s, bool pdl);
+                             cudaStream_t s, bool pdl, const TraceSink &tr = TraceSink{});
 // Prompts (attention_prefill.cu): flash attention on the tensor cores for
 // rows / batch >= kFaPrefillMinRows query rows per sequence and Dh 64 / 128;
 // launch_attention routes those shapes to it.
@@ -32,7 +41,8 @@ cudaError_t launch_flash_prefill(const void *q, int rps, int batch, int H, int H
 // Decode (one row per sequence): rope_kv + attention in one launch.
 cudaError_t launch_rope_attention(const float *qkv, int batch, int H, int Hkv, int Dh, const int *pos0, float theta,
                                   const float *q_norm, const float *k_norm, float eps, void *k_cache, void *v_cache,
-                                  int cache_len, void *out, unsigned *flags, int num_sms, cudaStream_t s, bool pdl);
+                                  int cache_len, void *out, unsigned *flags, int num_sms, cudaStream_t s, bool pdl,
+                                  const TraceSink &tr = TraceSink{});
 cudaError_t launch_swiglu(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s, bool pdl);
 cudaError_t launch_swiglu_pairs(const float *gu, int rows, int I, void *out, int out_dtype, cudaStream_t s,
                                 bool pdl);

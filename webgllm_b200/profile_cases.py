@@ -163,11 +163,13 @@ def decode(config: str, batch: int, reps: int):
 
 def trace_decode(config: str, batch: int, reps: int):
     """Per-CTA timeline of one decode step (CUDA graph) from wg_trace: for
-    each of a layer's four GEMVs (q|k|v, o, gate|up, down) the mean span from
-    the dependency release to the last CTA's exit and its phases per CTA
-    (release -> x staged, the multiplies, the tail), the gap before it (for
-    o: the attention launch), and the CTAs released more than 5 us after the
-    first (a second wave: CTAs that found no room until others finished)."""
+    each of a layer's five traced launches (the q|k|v GEMV, attention, the
+    o, gate|up and down GEMVs) the mean span from the dependency release to
+    the last CTA's exit and its phases per CTA (GEMVs: release -> x staged,
+    the multiplies, the tail; attention: release -> queries made, the K / V
+    tiles, the merge of the key slices), the gap before it, and the CTAs
+    released more than 5 us after the first (a second wave: CTAs that found
+    no room until others finished)."""
     import numpy as np
 
     cfg = CONFIGS[config]
@@ -191,12 +193,12 @@ def trace_decode(config: str, batch: int, reps: int):
     rec = buf[: n.value * 8].view(-1, 8).cpu().numpy().astype(np.float64)
     launch = rec[:, 7].astype(np.int64) >> 32
     ids = sorted(set(launch.tolist()))
-    names = ["q|k|v", "o", "gate|up", "down"]
+    names = ["q|k|v", "attention", "o", "gate|up", "down"]
     acc = {k: {f: [] for f in ("span", "x", "mul", "tail", "gap", "late", "ctas")} for k in names}
     prev_exit = None
     for i, li in enumerate(ids):
         r = rec[launch == li] / 1e3  # us
-        a = acc[names[i % 4]]
+        a = acc[names[i % len(names)]]
         a["span"].append(r[:, 5].max() - r[:, 2].min())
         a["x"].append(np.median(r[:, 3] - r[:, 2]))
         a["mul"].append(np.median(r[:, 4] - r[:, 3]))
@@ -206,7 +208,7 @@ def trace_decode(config: str, batch: int, reps: int):
         if prev_exit is not None:
             a["gap"].append(r[:, 2].min() - prev_exit)
         prev_exit = r[:, 5].max()
-    print(f"decode config {config} batch {batch}: {us:.1f} us/step (CUDA graph), {len(ids)} traced GEMV launches")
+    print(f"decode config {config} batch {batch}: {us:.1f} us/step (CUDA graph), {len(ids)} traced launches")
     for k in names:
         a = acc[k]
         print(f"  {k:8s} ctas {np.mean(a['ctas']):5.0f}  release->exit {np.mean(a['span']):6.2f} us  per CTA: x "
