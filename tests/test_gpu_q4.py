@@ -134,13 +134,49 @@ def test_gemv_rows(M):
 
 @pytest.mark.parametrize("N,K", [(4, 32), (12, 96), (20, 160), (36, 64), (100, 4096),
                                  (2560, 2048), (2048, 5632), (256, 14336), (4, 32768),
-                                 # K split over clusters whose last CTA has a shorter range
-                                 (1024, 2048), (512, 1600), (64, 3520), (1536, 4608)])
+                                 # K in one CTA up to 128 tiles (formerly cluster splits)
+                                 (1024, 2048), (512, 1600), (64, 3520), (1536, 4608), (128, 8192)])
 def test_gemv_shapes(N, K):
     blocks, m, host = make(N, K, N + K)
     for M in (1, 5):
         y, x16 = run(m, O.config_activations(M, K, 3))
         check_close(y, O.c_ref_f64(blocks, x16, N, K), f"{N}x{K} M={M}")
+
+
+_SPLIT_CHILD = """
+import sys
+sys.path.insert(0, sys.argv[1])
+import torch, oracle as O, webgllm_b200 as wg
+for N, K, M in [(1024, 2048, 1), (512, 1600, 2), (64, 3520, 1), (1536, 4608, 3), (256, 14336, 1), (4, 32768, 1)]:
+    blocks = O.config_q4_0_blocks(N, K, N + K)
+    m = wg.newQuantMatrix(N, K)
+    wg.packQ4_0(m, 0, blocks, N)
+    x = torch.from_numpy(O.config_activations(M, K, 3)).to("cuda", torch.float16)
+    y = wg.matmul(x, m, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    l2, mx = O.rel_errors(y.cpu().numpy(), O.c_ref_f64(blocks, x.float().cpu().numpy(), N, K))
+    assert l2 <= O.TOL and mx <= O.TOL, f"{N}x{K} M={M}: {l2:.3e} {mx:.3e}"
+print("ok")
+"""
+
+
+def test_gemv_cluster_split_path():
+    # The tile-column GEMV splits K over a thread-block cluster only where a
+    # CTA's range does not fit (K > 8192 at one row); WG_GEMV_SPLIT_PCT=100
+    # restores the split of small grids and WG_GEMV_WIDE=0 keeps every shape
+    # on the tile-column kernel, so that the cluster reduction (including
+    # clusters whose last CTA has a shorter range) stays checked. The
+    # settings are read once per process: a child process runs the cases.
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, WG_GEMV_SPLIT_PCT="100", WG_GEMV_WIDE="0")
+    r = subprocess.run([sys.executable, "-c", _SPLIT_CHILD, str(root)], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-2000:]
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 14336),   # one stage: a column at a time

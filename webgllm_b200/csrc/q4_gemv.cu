@@ -53,7 +53,11 @@ namespace {
 constexpr bool kRawUnpack = false;
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxTilesPerWarp = 8;
+// Up to 16 tiles a warp: K up to 8192 in one CTA at one row (the smem budget
+// lowers it for more rows). A K split across a cluster costs its two cluster
+// barriers and the remote reads (~1.5 us a launch on B200) and is only used
+// where the range does not fit.
+constexpr int kMaxTilesPerWarp = 16;
 constexpr int kMaxTilesPerCta = kWarps * kMaxTilesPerWarp;
 constexpr int kSmemBudget = 100 * 1024;  // per CTA, so that two kernels' CTAs fit an SM
 constexpr int kMaxSmem = 200 * 1024;
@@ -383,18 +387,18 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
     }
   } else {
     // Up to 4 loads in flight per lane before any store (one L2 round trip
-    // for the usual M * 8 tiles <= 128 chunks). Entry idx = m * 64 + c
-    // (token m, chunk c of 8 K values; a warp has at most 64 chunks), so
-    // that shifts, not divisions, split it.
-    static_assert(kMaxTilesPerWarp * (kTileK / 8) == 64, "64 chunks per warp at most");
+    // for every 128 chunks). Entry idx = m * 128 + c (token m, chunk c of 8
+    // K values; a warp has at most 128 chunks), so that shifts, not
+    // divisions, split it.
+    static_assert(kMaxTilesPerWarp * (kTileK / 8) == 128, "128 chunks per warp at most");
     const int chunks = nw * (kTileK / 8);
     const int kbase = (kt0 + wt0) * kTileK;
-    for (int base = 0; base < M * 64; base += 4 * 32) {
+    for (int base = 0; base < M * 128; base += 4 * 32) {
       uint4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const int idx = base + u * 32 + lane;
-        const int m = idx >> 6, c = idx & 63;
+        const int m = idx >> 7, c = idx & 127;
         const int k = kbase + c * 8;
         v[u] = make_uint4(0, 0, 0, 0);
         if (m < M && c < chunks && k < a.K) {
@@ -407,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 4 : 2) gemv_kernel(const G
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const int idx = base + u * 32 + lane;
-        const int m = idx >> 6, c = idx & 63;
+        const int m = idx >> 7, c = idx & 127;
         if (m < M && c < chunks) *reinterpret_cast<uint4 *>(xw + (size_t)m * stride + c * 8) = v[u];
       }
     }
@@ -1031,16 +1035,26 @@ bool plan_gemv(GemvArgs &a, int num_sms) {
   int max_ktc = kMaxTilesPerCta;
   while (max_ktc > 1 && gemv_smem(a.M, max_ktc, NG, zeros).total > kSmemBudget) max_ktc--;
   int C = (a.KT + max_ktc - 1) / max_ktc;
-  // Few row tiles: split K further (up to a portable cluster of 8) until the
-  // grid covers the SMs `ctas_per_sm` times, keeping at least one tile per
-  // warp. WG_GEMV_CTAS_PER_SM overrides the target (tuning).
-  static int ctas_per_sm = -1;
+  // Few row tiles, where WG_GEMV_SPLIT_PCT allows it: split K further (up
+  // to a portable cluster of 8) until the grid covers the SMs `ctas_per_sm`
+  // times, keeping at least one tile per warp. WG_GEMV_CTAS_PER_SM overrides
+  // the target (tuning).
+  static int ctas_per_sm = -1, split_pct = -1;
   if (ctas_per_sm < 0) {
     const char *e = getenv("WG_GEMV_CTAS_PER_SM");
     ctas_per_sm = e ? atoi(e) : 1;
     if (ctas_per_sm < 1) ctas_per_sm = 1;
+    // Split K for a small grid only below this % of the target (tuning;
+    // default 0: never). Measured on B200 (M = 1, chains of 16 as a CUDA
+    // graph): 2048 x 2048 in clusters of 2 over 256 CTAs 3.89 us a launch,
+    // unsplit over 128 CTAs 2.45 us: the cluster reduction's ~1.5 us outweighs
+    // the halved multiplies, and the weights are in shared memory before the
+    // dependency release either way.
+    const char *f = getenv("WG_GEMV_SPLIT_PCT");
+    split_pct = f ? atoi(f) : 0;
   }
-  while (C < 8 && a.NT * C < ctas_per_sm * num_sms && (a.KT + C) / (C + 1) >= kWarps) C++;
+  if ((long)a.NT * 100 < (long)split_pct * ctas_per_sm * num_sms)
+    while (C < 8 && a.NT * C < ctas_per_sm * num_sms && (a.KT + C) / (C + 1) >= kWarps) C++;
   if (C > 16) return false;
   const int ktc = (a.KT + C - 1) / C;
   C = (a.KT + ktc - 1) / ktc;

@@ -63,6 +63,76 @@ def gemv(M: int, N: int, K: int, reps: int):
     print(f"gemv M={M} N={N} K={K}: {us:.2f} us/launch, {N * K * 18 / 32 / us / 1e3:.1f} GB/s (weights)")
 
 
+def trace_gemv_chain(M: int, N: int, K: int, reps: int, launches: int = 16):
+    """Per-CTA timeline (wg_trace) of a chain of `launches` decode GEMVs over
+    distinct matrices (> L2), captured as one CUDA graph with programmatic
+    dependent launch, as bench.py times them. Per launch after the first
+    two, medians over launches of: the period (last CTA exit to last CTA
+    exit), the gap from the previous launch's last exit to this one's first
+    dependency release, and per CTA (median) entry -> weight copies issued,
+    copies issued -> release, release -> x staged, the multiplies, the tail
+    (reduction, stores, exit); plus the spread of the CTAs' releases."""
+    import numpy as np
+
+    c = context()
+    mats = [_q4(N, K, i) for i in range(launches)]
+    x = torch.randn((M, K), device="cuda").half()
+    ys = torch.empty((launches, M, N), device="cuda", dtype=torch.float16)
+    L = _lib.lib()
+
+    def chain():
+        c.use_torch_stream()
+        for i in range(launches):
+            _lib.check(L.wg_q4_matmul(P(c.handle), P(mats[i].handle), P(x.data_ptr()), _lib.WG_F16, M,
+                                      P(ys[i].data_ptr()), _lib.WG_F16), c.handle)
+
+    s = torch.cuda.Stream()
+    buf = torch.zeros(8 * 4096 * launches, dtype=torch.int64, device="cuda")
+    with torch.cuda.stream(s):
+        chain()
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            chain()
+        for _ in range(3):
+            g.replay()
+        us = _time(g.replay, reps) / launches  # untraced
+        gt = torch.cuda.CUDAGraph()  # the traced copy: the record buffer is a kernel argument
+        _lib.check(L.wg_trace(P(c.handle), P(buf.data_ptr()), buf.numel() * 8), c.handle)
+        with torch.cuda.graph(gt, stream=s):
+            chain()
+        for _ in range(3):
+            gt.replay()
+        s.synchronize()
+        _lib.check(L.wg_trace(P(c.handle), P(buf.data_ptr()), buf.numel() * 8), c.handle)  # restart the records
+        gt.replay()
+        torch.cuda.synchronize()
+    n = ctypes.c_size_t()
+    _lib.check(L.wg_trace_count(P(c.handle), ctypes.byref(n)), c.handle)
+    _lib.check(L.wg_trace(P(c.handle), None, 0), c.handle)
+    rec = buf[: n.value * 8].view(-1, 8).cpu().numpy().astype(np.float64)
+    launch = rec[:, 7].astype(np.int64) >> 32
+    ids = sorted(set(launch.tolist()))
+    cols = {k: [] for k in ("period", "gap", "entry->copies", "copies->release", "x", "mul", "tail",
+                            "release spread")}
+    prev_exit = None
+    for j, li in enumerate(ids):
+        r = rec[launch == li] / 1e3  # us
+        if prev_exit is not None and j >= 2:
+            cols["period"].append(r[:, 5].max() - prev_exit)
+            cols["gap"].append(r[:, 2].min() - prev_exit)
+            cols["entry->copies"].append(np.median(r[:, 1] - r[:, 0]))
+            cols["copies->release"].append(np.median(r[:, 2] - r[:, 1]))
+            cols["x"].append(np.median(r[:, 3] - r[:, 2]))
+            cols["mul"].append(np.median(r[:, 4] - r[:, 3]))
+            cols["tail"].append(np.median(r[:, 5] - r[:, 4]))
+            cols["release spread"].append(r[:, 2].max() - r[:, 2].min())
+        prev_exit = r[:, 5].max()
+    print(f"gemv chain M={M} N={N} K={K}: {us:.2f} us/launch (graph of {launches}), {len(ids)} traced launches, "
+          f"{len(rec) // max(1, len(ids))} CTAs each")
+    print("  " + ", ".join(f"{k} {np.median(v):.2f}" for k, v in cols.items()) + " (us, medians)")
+
+
 def gemm(M: int, N: int, K: int, reps: int):
     """The prefill GEMM over `copies` distinct matrices (rotating, > L2 when
     the weights dominate the bytes)."""
@@ -295,6 +365,8 @@ CASES = {
     "gemv_config1_m1": lambda r: gemv(1, 4096, 4096, r),
     "gemv_wide_m8": lambda r: gemv(8, 28672, 4096, r),
     "gemv_m1_28672x4096": lambda r: gemv(1, 28672, 4096, r),
+    "trace_gemv_chain_m1": lambda r: trace_gemv_chain(1, 4096, 4096, r),
+    "trace_gemv_chain_m1_2048": lambda r: trace_gemv_chain(1, 2048, 2048, r),
     "gemm_m64": lambda r: gemm(64, 4096, 4096, r),
     "gemm_m256": lambda r: gemm(256, 4096, 4096, r),
     "gemm_m1024": lambda r: gemm(1024, 4096, 4096, r),
