@@ -367,6 +367,9 @@ CASES = {
     "gemv_m1_28672x4096": lambda r: gemv(1, 28672, 4096, r),
     "trace_gemv_chain_m1": lambda r: trace_gemv_chain(1, 4096, 4096, r),
     "trace_gemv_chain_m1_2048": lambda r: trace_gemv_chain(1, 2048, 2048, r),
+    # the GEMM's stamps: entry, copies issued, release, first x, last multiply, exit
+    "trace_gemm_chain_m64": lambda r: trace_gemv_chain(64, 4096, 4096, r),
+    "trace_gemm_chain_m256": lambda r: trace_gemv_chain(256, 4096, 4096, r),
     "gemm_m64": lambda r: gemm(64, 4096, 4096, r),
     "gemm_m256": lambda r: gemm(256, 4096, 4096, r),
     "gemm_m1024": lambda r: gemm(1024, 4096, 4096, r),
