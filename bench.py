@@ -13,7 +13,9 @@ is the max over ranks and `value` sums all ranks' bytes.
 
 Extra keys: `roofline` (the GEMV kernel against the measured HBM copy
 bandwidth), `e2e` (the same GB/s through the C ABI with pinned host buffers,
-copies inside the timed region), `cpu_baseline` (the CPU oracle's restatement
+copies inside the timed region: the step's matmuls recorded once with
+wg_graph_begin / wg_graph_end and replayed by wg_graph_launch; `per_call`
+beside it makes one C call per matmul), `cpu_baseline` (the CPU oracle's restatement
 of the reference's shader arithmetic on the host cores), `clocks`, `sweep`
 (config 1's other row counts, informational) and `decode` (BASELINE's
 "decode tokens/s": greedy generation of the random-init decoders of configs
@@ -478,30 +480,52 @@ def run_e2e(args, ctx, mats, x, ys, per_launch, world, barrier, max_over_ranks):
     c_dy, c_hy = ctypes.c_void_p(dy), ctypes.c_void_p(hy)
     bi, bo = M_ROWS * K_IN * 2, MATRICES * M_ROWS * N_OUT * 2
 
-    def e2e_step():
-        st = L.wg_upload(c_ctx, c_dx, c_hx, bi)
+    def matmuls():
+        st = 0
         for r in range(MATRICES):
             st |= L.wg_q4_matmul(c_ctx, c_mats[r], c_dx, 1, M_ROWS, c_ys[r], 1)
-        st |= L.wg_read(c_ctx, c_hy, c_dy, bo)
+        return st
+
+    def check(st):
         if st:
             raise RuntimeError(L.wg_last_error(c_ctx).decode())
 
+    def step_calls():  # one C call per matmul
+        check(L.wg_upload(c_ctx, c_dx, c_hx, bi) | matmuls() | L.wg_read(c_ctx, c_hy, c_dy, bo))
+
+    # the step's matmuls recorded once through the C ABI (wg_graph_*), as a
+    # host repeating a decode step would, and replayed with one call
+    graph = ctypes.c_void_p()
+    step_calls()  # first calls outside the recording
+    check(L.wg_graph_begin(c_ctx))
+    check(matmuls())
+    check(L.wg_graph_end(c_ctx, ctypes.byref(graph)))
+
+    def step_graph():
+        check(L.wg_upload(c_ctx, c_dx, c_hx, bi) | L.wg_graph_launch(c_ctx, graph) | L.wg_read(c_ctx, c_hy, c_dy, bo))
+
     e2e_steps = max(10, min(args.steps, 300))
-    for _ in range(max(args.warmup, 3)):
-        e2e_step()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        e2e_step()
-    t_e2e = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
-    e2e_value = world * MATRICES * per_launch / t_e2e / 1e9
-    y_e2e = np.ctypeslib.as_array((ctypes.c_uint16 * N_OUT).from_address(hy)).view(np.float16)
-    assert np.array_equal(y_e2e, ys[0, 0].cpu().numpy()), "e2e output differs from the graph's"
+    timed = {}
+    for name, fn in (("calls", step_calls), ("graph", step_graph)):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            fn()
+        timed[name] = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
+        y_e2e = np.ctypeslib.as_array((ctypes.c_uint16 * N_OUT).from_address(hy)).view(np.float16)
+        assert np.array_equal(y_e2e, ys[0, 0].cpu().numpy()), f"e2e output ({name}) differs from the bench graph's"
+    check(L.wg_graph_free(c_ctx, graph))
     ctx.free(dx), ctx.free(dy), ctx.host_free(hx), ctx.host_free(hy)
-    return {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": bi,
+    gbs = {k: world * MATRICES * per_launch / t / 1e9 for k, t in timed.items()}
+    return {"value": round(gbs["graph"], 2), "unit": "GB/s", "h2d_bytes_per_step": bi,
             "d2h_bytes_per_step": bo,
-            "how": f"wg_upload + {MATRICES} x wg_q4_matmul + wg_read through the C ABI (ctypes), "
-                   "pinned host buffers, wall clock, max over ranks"}
+            "how": f"wg_upload + the step's {MATRICES} wg_q4_matmul recorded once (wg_graph_begin/end) and "
+                   "replayed by wg_graph_launch + wg_read through the C ABI (ctypes), pinned host buffers, "
+                   "wall clock, max over ranks",
+            "per_call": {"value": round(gbs["calls"], 2), "unit": "GB/s",
+                         "how": f"wg_upload + {MATRICES} x wg_q4_matmul + wg_read, one C call per matmul"}}
 
 
 def run_sweep(mats, stream, hbm, bf16):

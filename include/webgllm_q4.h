@@ -246,6 +246,33 @@ int wg_q4_matmul_residual(wg_ctx *ctx, const wg_q4mat *m, const wg_prologue *pro
 int wg_trace(wg_ctx *ctx, void *buf, size_t bytes);
 int wg_trace_count(wg_ctx *ctx, size_t *records);
 
+/* ---- recorded steps ------------------------------------------------------ */
+
+/* The engine submits a decode step as a fixed sequence of passes, each its
+ * own Gpu.run (the layer loop, src/engine.ts:9106; one pass per matmul,
+ * src/engine.ts:4677). A host that repeats such a sequence can record it
+ * once and replay it as one submission: the launches then cost one host
+ * call, not one each, and keep their programmatic dependent launch edges.
+ * No reference counterpart (WebGL has no recorded command buffers). */
+typedef struct wg_graph wg_graph;
+/* Starts recording on the context's stream (CUDA stream capture, this
+ * thread only): the calls that enqueue work on it until wg_graph_end are
+ * recorded, not run. They read and write the device pointers they were
+ * given at every replay. Recorded calls must allocate nothing (make each
+ * kind of call once before recording, or use wg_q4_matmul_static) and must
+ * not wait (wg_read, wg_sync, wg_q4_matrix_row, wg_free): such a call fails
+ * and spoils the recording, which wg_graph_end then reports. Not on the
+ * legacy default stream. */
+int wg_graph_begin(wg_ctx *ctx);
+/* Ends the recording: *out replays it. If the recording failed, *out is
+ * NULL, nothing was enqueued, and the status says why. */
+int wg_graph_end(wg_ctx *ctx, wg_graph **out);
+/* Enqueues one replay of `g` on the context's stream (returns without
+ * waiting, like every other launch). */
+int wg_graph_launch(wg_ctx *ctx, const wg_graph *g);
+/* Releases `g` once the context's stream has finished its replays. */
+int wg_graph_free(wg_ctx *ctx, wg_graph *g);
+
 /* ---- errors -------------------------------------------------------------- */
 
 /* The name of a status code. */

@@ -350,3 +350,67 @@ print(worst, worst_max)
     assert out.returncode == 0, out.stderr[-2000:]
     l2, mx = map(float, out.stdout.strip().splitlines()[-1].split())
     assert l2 <= TOL and mx <= TOL, f"pair kernel: l2 {l2:.3e} max {mx:.3e}"
+
+
+# ---------------------------------------------------------------- recorded steps (wg_graph_*)
+
+
+def test_recorded_step_replays_the_calls():
+    # A recorded sequence of matmuls (GEMV rows, wide GEMV rows and the GEMM,
+    # as a decode step mixes them) replays to the same bytes as the same calls
+    # made one by one, reading the inputs' current contents at every replay.
+    import ctypes
+
+    from webgllm_b200 import _lib
+
+    L = _lib.lib()
+    cases = []
+    for i, (M, N, K) in enumerate([(1, 4096, 4096), (8, 2048, 4096), (64, 512, 4096)]):
+        _, m, _ = make(N, K, 40 + i)
+        x = torch.empty((M, K), device="cuda", dtype=torch.float16)
+        cases.append((m, x, torch.empty((M, N), device="cuda"), torch.empty((M, N), device="cuda")))
+    ctx = cases[0][0].ctx
+    h = ctypes.c_void_p(ctx.handle)
+    ctx.set_stream(None)  # the context's own stream (torch's default one is the legacy stream)
+
+    def calls(into):
+        for m, x, ya, yb in cases:
+            y = ya if into == 0 else yb
+            _lib.check(L.wg_q4_matmul(h, ctypes.c_void_p(m.handle), ctypes.c_void_p(x.data_ptr()), _lib.WG_F16,
+                                      x.shape[0], ctypes.c_void_p(y.data_ptr()), _lib.WG_F32), ctx.handle)
+
+    try:
+        for _, x, _, _ in cases:
+            x.zero_()
+        torch.cuda.synchronize()
+        calls(0)  # first calls of each kind outside the recording
+        _lib.check(L.wg_sync(h), ctx.handle)
+        g = ctypes.c_void_p()
+        _lib.check(L.wg_graph_begin(h), ctx.handle)
+        calls(1)
+        _lib.check(L.wg_graph_end(h, ctypes.byref(g)), ctx.handle)
+        assert g.value
+        try:
+            for rep in range(2):
+                for j, (_, x, _, _) in enumerate(cases):
+                    x.copy_(torch.from_numpy(O.config_activations(x.shape[0], x.shape[1], 10 * rep + j)))
+                torch.cuda.synchronize()
+                calls(0)
+                _lib.check(L.wg_graph_launch(h, g), ctx.handle)
+                _lib.check(L.wg_sync(h), ctx.handle)
+                for m, x, ya, yb in cases:
+                    assert torch.equal(ya, yb), f"replay {rep}, M={x.shape[0]}"
+                    assert ya.abs().max().item() > 0
+        finally:
+            _lib.check(L.wg_graph_free(h, g), ctx.handle)
+        # A call that waits spoils a recording; the end reports it, returns no
+        # graph, and the context works on.
+        _lib.check(L.wg_graph_begin(h), ctx.handle)
+        assert L.wg_sync(h) != _lib.WG_OK
+        g2 = ctypes.c_void_p()
+        assert L.wg_graph_end(h, ctypes.byref(g2)) == _lib.WG_CUDA_ERROR and not g2.value
+        assert b"recording failed" in L.wg_last_error(h)
+        calls(0)
+        _lib.check(L.wg_sync(h), ctx.handle)
+    finally:
+        ctx.use_torch_stream()

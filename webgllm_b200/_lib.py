@@ -67,6 +67,10 @@ SIGNATURES = {
     "wg_q4_matmul_residual": (_I, [_P, _P, _P, _P, _I, _I, _P, _P]),
     "wg_trace": (_I, [_P, _P, _SZ]),
     "wg_trace_count": (_I, [_P, ctypes.POINTER(_SZ)]),
+    "wg_graph_begin": (_I, [_P]),
+    "wg_graph_end": (_I, [_P, _PP]),
+    "wg_graph_launch": (_I, [_P, _P]),
+    "wg_graph_free": (_I, [_P, _P]),
     # include/webgllm_decoder.h
     "wg_embed": (_I, [_P, _P, _I, _P, _I, _I, _P]),
     "wg_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _I, _P, _I]),

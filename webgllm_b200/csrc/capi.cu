@@ -732,6 +732,73 @@ int wg_trace_count(wg_ctx *ctx, size_t *records) {
   return WG_OK;
 }
 
+// ---- recorded steps (CUDA graphs of the context's stream) -------------------
+
+struct wg_graph {
+  cudaGraphExec_t exec = nullptr;
+  int device = 0;
+};
+
+int wg_graph_begin(wg_ctx *ctx) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  int st = use_device(ctx);
+  if (st) return st;
+  if (ctx->stream == nullptr || ctx->stream == cudaStreamLegacy)
+    return fail(ctx, WG_INVALID_ARGUMENT, "wg_graph_begin: the legacy default stream cannot be recorded");
+  WG_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  return WG_OK;
+}
+
+int wg_graph_end(wg_ctx *ctx, wg_graph **out) {
+  if (!ctx || !out) return fail(ctx, WG_INVALID_ARGUMENT, "wg_graph_end: null argument");
+  *out = nullptr;
+  int st = use_device(ctx);
+  if (st) return st;
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  if (e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    (void)cudaGetLastError();  // a spoilt capture is not a context error
+    return fail(ctx, WG_CUDA_ERROR, "wg_graph_end: the recording failed (%s): a recorded call allocated or waited",
+                cudaGetErrorString(e));
+  }
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wg_graph_end: cudaGraphInstantiate");
+  wg_graph *g = new (std::nothrow) wg_graph;
+  if (!g) {
+    cudaGraphExecDestroy(exec);
+    return fail(ctx, WG_OUT_OF_MEMORY, "wg_graph_end: host allocation");
+  }
+  g->exec = exec;
+  g->device = ctx->device;
+  *out = g;
+  return WG_OK;
+}
+
+int wg_graph_launch(wg_ctx *ctx, const wg_graph *g) {
+  if (!ctx || !g) return fail(ctx, WG_INVALID_ARGUMENT, "wg_graph_launch: null argument");
+  if (g->device != ctx->device)
+    return fail(ctx, WG_INVALID_ARGUMENT, "wg_graph_launch: recorded on device %d, context on %d", g->device,
+                ctx->device);
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaGraphLaunch(g->exec, ctx->stream));
+  return WG_OK;
+}
+
+int wg_graph_free(wg_ctx *ctx, wg_graph *g) {
+  if (!ctx) return WG_INVALID_ARGUMENT;
+  if (!g) return WG_OK;
+  int st = use_device(ctx);
+  if (st) return st;
+  WG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  cudaGraphExecDestroy(g->exec);
+  delete g;
+  return WG_OK;
+}
+
 const char *wg_error_string(int status) {
   switch (status) {
     case WG_OK: return "ok";
