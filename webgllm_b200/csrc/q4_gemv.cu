@@ -222,6 +222,15 @@ __device__ __forceinline__ void emit_stats(const GemvArgs &a, int nt, int tok, c
 
 // Eight consecutive x values (row m, columns k..k+7) as fp16, made by the
 // prologue: (residual + b) * inv * w for the norm, silu(gate) * up for SwiGLU.
+// The norm of eight values: fp16((v * inv) * w), the one place this
+// arithmetic is written (every staging path gives the same bits).
+__device__ __forceinline__ uint4 norm_x8(float4 v0, float4 v1, float4 w0, float4 w1, float inv) {
+  float f[8];
+  f[0] = v0.x * inv * w0.x; f[1] = v0.y * inv * w0.y; f[2] = v0.z * inv * w0.z; f[3] = v0.w * inv * w0.w;
+  f[4] = v1.x * inv * w1.x; f[5] = v1.y * inv * w1.y; f[6] = v1.z * inv * w1.z; f[7] = v1.w * inv * w1.w;
+  return make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+}
+
 template <int PRO>
 __device__ __forceinline__ uint4 prologue_x8(const Prologue &p, int K, int m, int k, float inv) {
   float f[8];
@@ -234,8 +243,7 @@ __device__ __forceinline__ uint4 prologue_x8(const Prologue &p, int K, int m, in
       v1 = add4(v1, b[1]);
     }
     const float4 w0 = reinterpret_cast<const float4 *>(p.w + k)[0], w1 = reinterpret_cast<const float4 *>(p.w + k)[1];
-    f[0] = v0.x * inv * w0.x; f[1] = v0.y * inv * w0.y; f[2] = v0.z * inv * w0.z; f[3] = v0.w * inv * w0.w;
-    f[4] = v1.x * inv * w1.x; f[5] = v1.y * inv * w1.y; f[6] = v1.z * inv * w1.z; f[7] = v1.w * inv * w1.w;
+    return norm_x8(v0, v1, w0, w1, inv);
   } else {
     const float4 *g = reinterpret_cast<const float4 *>(p.a + (size_t)m * 2 * K + k);
     const float4 *u = reinterpret_cast<const float4 *>(p.a + (size_t)m * 2 * K + K + k);
@@ -711,6 +719,43 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_wide_kernel(const GemvArgs 
       xs[(size_t)m * L.xstride + kcols + (i - m * tail)] = __float2half_rn(0.0f);
     }
     mbar_wait_bounded(xbar, 0, a.flags);
+  } else if (PRO == kProRmsNorm && !a.wide_norm_rows) {
+    // The norm: the weight is the same for every row, so a thread takes one
+    // chunk of 8 columns for the rows, loading its 8 weights once and four
+    // rows' residuals at a time (10 loads in flight), instead of the weights
+    // again with every row.
+    constexpr int kRowsAtOnce = 4;
+    const int chunks = ktc * (kTileK / 8);
+    const int kbase = kt0 * kTileK;
+    for (int c = threadIdx.x; c < chunks; c += kWThreads) {
+      const int k = kbase + c * 8;
+      if (k >= a.K) {  // the partial last tile: zeros past K
+        for (int m = 0; m < M; m++) *reinterpret_cast<uint4 *>(xs + (size_t)m * L.xstride + c * 8) = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      const float4 w0 = reinterpret_cast<const float4 *>(a.pro.w + k)[0];
+      const float4 w1 = reinterpret_cast<const float4 *>(a.pro.w + k)[1];
+      for (int m0 = 0; m0 < M; m0 += kRowsAtOnce) {
+        float4 v[kRowsAtOnce][2];
+#pragma unroll
+        for (int i = 0; i < kRowsAtOnce; i++)
+          if (m0 + i < M) {
+            const float4 *r = reinterpret_cast<const float4 *>(a.pro.a + (size_t)(m0 + i) * a.K + k);
+            v[i][0] = r[0];
+            v[i][1] = r[1];
+            if (a.pro.b) {
+              const float4 *b = reinterpret_cast<const float4 *>(a.pro.b + (size_t)(m0 + i) * a.K + k);
+              v[i][0] = add4(v[i][0], b[0]);
+              v[i][1] = add4(v[i][1], b[1]);
+            }
+          }
+#pragma unroll
+        for (int i = 0; i < kRowsAtOnce; i++)
+          if (m0 + i < M)
+            *reinterpret_cast<uint4 *>(xs + (size_t)(m0 + i) * L.xstride + c * 8) =
+                norm_x8(v[i][0], v[i][1], w0, w1, s_inv[m0 + i]);
+      }
+    }
   } else {
     // entry idx = m << sh | c (token m, chunk c of 8 K values, 2^sh >=
     // chunks): shifts, not divisions, split it
@@ -1106,6 +1151,12 @@ bool plan_gemv_wide(GemvArgs &a, int num_sms) {
     const char *e = getenv("WG_GEMV_WIDE_GROUPS");
     groups_on = e ? atoi(e) : 2;
   }
+  static int norm_rows = -1;
+  if (norm_rows < 0) {
+    const char *e = getenv("WG_WIDE_NORM_ROWS");
+    norm_rows = e && e[0] == '1' ? 1 : 0;
+  }
+  a.wide_norm_rows = norm_rows;
   a.wide_groups = 0;
   if (groups_on && C == 1) {
     const int budget = groups_on == 2 ? kWideSmemMaxGroups : kWideSmemMax;

@@ -80,6 +80,7 @@ struct GemvArgs {
                    // or kEpiResidual: y fp32 [M][N] += the product, stats [N/16][M] = per-tile sums of squares
   float *stats;    // kEpiResidual
   int wide_groups; // wide GEMV without a K split: two 8-warp groups take alternate columns
+  int wide_norm_rows;  // wide GEMV, norm prologue: stage x row by row (WG_WIDE_NORM_ROWS=1, measurement)
 };
 enum EpiKind { kEpiNone = 0, kEpiSwigluPairs = 1, kEpiResidual = 2 };
 
