@@ -383,6 +383,7 @@ CASES = {
     "decode_config2": lambda r: decode("2", 1, r),
     "exchange_config4_b8": lambda r: exchange(r),
     "trace_decode_config4_b8": lambda r: trace_decode("4", 8, r),
+    "trace_decode_config2": lambda r: trace_decode("2", 1, r),
 }
 
 
