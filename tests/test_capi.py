@@ -51,6 +51,10 @@ def test_null_arguments_are_rejected_without_a_device():
     assert L.wg_sync(None) == _lib.WG_INVALID_ARGUMENT
     assert L.wg_q4_matmul(None, None, None, 0, 1, None, 0) == _lib.WG_INVALID_ARGUMENT
     assert L.wg_q4_info(None, None, None, None) == _lib.WG_INVALID_ARGUMENT
+    assert L.wg_graph_begin(None) == _lib.WG_INVALID_ARGUMENT
+    assert L.wg_graph_end(None, None) == _lib.WG_INVALID_ARGUMENT
+    assert L.wg_graph_launch(None, None) == _lib.WG_INVALID_ARGUMENT
+    assert L.wg_graph_free(None, None) == _lib.WG_INVALID_ARGUMENT
     assert L.wg_last_error(None) == b""
 
 
